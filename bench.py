@@ -1,0 +1,541 @@
+"""Benchmark of the B200 sparse-product path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl b200|reference] [--no-extras]
+
+Headline workload (default ``spmm_f32``): BASELINE config 2, CSR SpMM of a
+2^20 x 2^20 matrix with exactly 16 nonzeros per row times a dense 2^20 x 64
+fp32 RHS. ``value`` is GB/s of the metric's algorithmic bytes
+(nnz*(4+4) + 4(n+1) + 2*n*64*4 = 675.3 MB per product) over device time;
+with N GPUs (torchrun) rows are split by balanced nnz, the RHS is replicated,
+each rank times its share and the slowest rank sets the time (strong scaling).
+Other workloads (``--workload``): spmm_bf16, spmv_lap2d, spmv_powerlaw,
+pcg_poisson3d, spgemm. At N=1 the line also carries ``workloads`` with the
+other configs measured the same way (skip with ``--no-extras``).
+
+Timing: W warm-up steps, then K steps, each bracketed by CUDA events on the
+launching stream; the L2 is flushed (a 512 MiB write) before every step and
+outside its events. ``e2e`` repeats the product through the public API from
+pinned host buffers, with the host->device copy of the inputs and the
+device->host copy of the result inside the timed region. ``cpu_baseline`` times
+the CPU oracle (a restatement of the reference's CPU loops) on a bounded
+sample. ``--impl reference`` times that CPU implementation alone (all host
+threads) on the same workload and prints its own line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "mlx-sparse_b200"), os.path.join(ROOT, "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import workloads as wl  # noqa: E402
+
+METRIC = "SpMV/SpMM HBM GB/s (% of B200 peak); CG iters/s at 1/2/4/8 B200 vs host CPU"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def _shard_rows(indptr: np.ndarray, rank: int, world: int):
+    """nnz-balanced contiguous row range of this rank (the reference's weighted
+    ranges idea, cpu_parallel.cpp:202-253, applied to GPUs)."""
+    n = indptr.shape[0] - 1
+    nnz = int(indptr[-1])
+    targets = [(nnz * r) // world for r in range(world + 1)]
+    bounds = [int(np.searchsorted(indptr, t, side="left")) for t in targets]
+    bounds[0], bounds[-1] = 0, n
+    return bounds[rank], bounds[rank + 1]
+
+
+def _slice_rows(d, i, p, r0, r1):
+    k0, k1 = int(p[r0]), int(p[r1])
+    return d[k0:k1], i[k0:k1], (p[r0:r1 + 1] - p[r0]).astype(p.dtype)
+
+
+class Workload:
+    name = ""
+    unit = "GB/s"
+    higher_is_better = True
+    dtype = "f32"
+    scaling = "strong"
+
+    def setup(self, rank, world, device):
+        raise NotImplementedError
+
+    def step(self):
+        raise NotImplementedError
+
+    def e2e_step(self):
+        raise NotImplementedError
+
+
+class SpmmWorkload(Workload):
+    def __init__(self, bf16=False, n=1 << 20, k=64, per_row=16, seed=2):
+        self.bf16, self.n, self.k, self.per_row, self.seed = bf16, n, k, per_row, seed
+        self.name = f"spmm_{'bf16' if bf16 else 'f32'}"
+        self.dtype = "bf16 values/RHS, f32 accumulate" if bf16 else "f32"
+        s = 2 if bf16 else 4
+        nnz = n * per_row
+        self.problem_bytes = nnz * (s + 4) + 4 * (n + 1) + 2 * n * k * s
+
+    def config(self):
+        return {"workload": self.name, "matrix": f"{self.n}x{self.n} csr, {self.per_row} nnz/row uniform cols",
+                "rhs": f"{self.n}x{self.k} row-major", "index": "int32",
+                "l2": "flushed before every step (512 MiB write)"}
+
+    def setup(self, rank, world, device):
+        import torch
+        import mlx_sparse as ms
+
+        (d, i, p), shape = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
+        B = np.random.default_rng(self.seed + 100).uniform(-1, 1, (self.n, self.k)).astype(np.float32)
+        r0, r1 = _shard_rows(p, rank, world)
+        d, i, p = _slice_rows(d, i, p, r0, r1)
+        self.host = (d, i, p, B)
+        self.rows = r1 - r0
+        tdt = torch.bfloat16 if self.bf16 else torch.float32
+        self.A = ms.csr_array((torch.from_numpy(d).to(device).to(tdt), torch.from_numpy(i).to(device),
+                               torch.from_numpy(p).to(device)), shape=(self.rows, self.n), canonical=True)
+        self.B = torch.from_numpy(B).to(device).to(tdt)
+        self.out = torch.empty((self.rows, self.k), dtype=tdt, device=device)
+        # pinned host copies for the end-to-end leg
+        self.h_d = torch.from_numpy(d).to(tdt).pin_memory()
+        self.h_i = torch.from_numpy(i).pin_memory()
+        self.h_p = torch.from_numpy(p).pin_memory()
+        self.h_B = torch.from_numpy(B).to(tdt).pin_memory()
+        self.h_out = torch.empty((self.rows, self.k), dtype=tdt).pin_memory()
+        self.dev = device
+        self.launches_per_step = 1
+        s = 2 if self.bf16 else 4
+        self.h2d_bytes = d.size * s + i.nbytes + p.nbytes + B.size * s
+        self.d2h_bytes = self.rows * self.k * s
+
+    def step(self):
+        from mlx_sparse import _native
+
+        _native.csr_matmul(self.A.data, self.A.indices, self.A.indptr, self.B, self.A.shape, out=self.out)
+
+    def e2e_step(self):
+        import mlx_sparse as ms
+
+        A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
+                          self.h_p.to(self.dev, non_blocking=True)), shape=self.A.shape, canonical=True)
+        Y = A @ self.h_B.to(self.dev, non_blocking=True)
+        self.h_out.copy_(Y, non_blocking=True)
+
+    def cpu_sample(self, workers, budget_s=10.0):
+        from oracle import oracle
+
+        d, i, p, B = self.host
+        rows = min(self.rows, 1 << 16)
+        dd, ii, pp = _slice_rows(d, i, p, 0, rows)
+        if self.bf16:
+            dd, Bc = oracle.f32_to_bf16_bits(dd), oracle.f32_to_bf16_bits(B)
+        else:
+            Bc = B
+        s = 2 if self.bf16 else 4
+        sample_bytes = int(pp[-1]) * (s + 4) + 4 * (rows + 1) + 2 * rows * self.k * s
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            oracle.csr_matmul(dd, ii, pp, Bc, rows, bf16=self.bf16, workers=workers)
+            times.append(time.perf_counter() - t0)
+            if len(times) >= 200:
+                break
+        med = statistics.median(times)
+        return sample_bytes / med / 1e9, f"{rows} of {self.n} rows, median of {len(times)} runs"
+
+
+class SpmvWorkload(Workload):
+    def __init__(self, kind="lap2d"):
+        self.kind = kind
+        self.name = f"spmv_{kind}"
+        if kind == "lap2d":
+            self.make = lambda: wl.lap2d(1024, np.int32)
+            self.x_seed, self.it_bytes, self.dtype = 0, 4, "f32"
+        else:
+            self.make = lambda: wl.power_law(1 << 22, 3, np.int64)
+            self.x_seed, self.it_bytes, self.dtype = 5, 8, "f32 values, int64 indices"
+
+    def config(self):
+        if self.kind == "lap2d":
+            return {"workload": self.name, "matrix": "2D 5-point Laplacian 1024x1024 grid (n=1,048,576)",
+                    "index": "int32", "l2": "flushed before every step (512 MiB write)"}
+        return {"workload": self.name, "matrix": "power-law rows n=4,194,304 (Lomax alpha 2.1, mean ~20)",
+                "index": "int64", "l2": "flushed before every step (512 MiB write)"}
+
+    def setup(self, rank, world, device):
+        import torch
+        import mlx_sparse as ms
+
+        (d, i, p), shape = self.make()
+        x = wl.uniform_vector(shape[1], self.x_seed)
+        ib = self.it_bytes
+        # metric bytes of the whole product: (4+ib) per nnz, indptr, x once, y
+        self.problem_bytes = d.size * (4 + ib) + ib * (shape[0] + 1) + 4 * shape[1] + 4 * shape[0]
+        r0, r1 = _shard_rows(p, rank, world)
+        d, i, p = _slice_rows(d, i, p, r0, r1)
+        self.rows, self.n = r1 - r0, shape[1]
+        self.host = (d, i, p, x)
+        self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
+                               torch.from_numpy(p).to(device)), shape=(self.rows, self.n), canonical=True)
+        self.plan = self.A.spmv_plan()
+        self.x = torch.from_numpy(x).to(device)
+        self.y = torch.empty(self.rows, dtype=torch.float32, device=device)
+        self.h_d, self.h_i, self.h_p = (torch.from_numpy(a).pin_memory() for a in (d, i, p))
+        self.h_x = torch.from_numpy(x).pin_memory()
+        self.h_y = torch.empty(self.rows, dtype=torch.float32).pin_memory()
+        self.dev = device
+        self.launches_per_step = 1 + (1 if self.plan.n_split > 0 else 0)
+        self.h2d_bytes = d.nbytes + i.nbytes + p.nbytes + x.nbytes
+        self.d2h_bytes = self.rows * 4
+        self.local_bytes = d.size * (4 + ib) + ib * (self.rows + 1) + 4 * self.n + 4 * self.rows
+
+    def step(self):
+        from mlx_sparse import _native
+
+        _native.csr_matvec(self.A.data, self.A.indices, self.A.indptr, self.x, self.A.shape, plan=self.plan,
+                           out=self.y)
+
+    def e2e_step(self):
+        import mlx_sparse as ms
+
+        A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
+                          self.h_p.to(self.dev, non_blocking=True)), shape=self.A.shape, canonical=True)
+        y = A @ self.h_x.to(self.dev, non_blocking=True)
+        self.h_y.copy_(y, non_blocking=True)
+
+    def cpu_sample(self, workers, budget_s=10.0):
+        from oracle import oracle
+
+        d, i, p, x = self.host
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            oracle.csr_matvec(d, i, p, x, self.rows, workers=workers)
+            times.append(time.perf_counter() - t0)
+            if len(times) >= 500:
+                break
+        med = statistics.median(times)
+        return self.local_bytes / med / 1e9, f"full matrix, median of {len(times)} runs"
+
+
+WORKLOADS = {
+    "spmm_f32": lambda: SpmmWorkload(bf16=False),
+    "spmm_bf16": lambda: SpmmWorkload(bf16=True),
+    "spmv_lap2d": lambda: SpmvWorkload("lap2d"),
+    "spmv_powerlaw": lambda: SpmvWorkload("powerlaw"),
+}
+
+
+# ---------------------------------------------------------------------------
+# measurement
+# ---------------------------------------------------------------------------
+def _measure(wk, steps, warmup, device):
+    import torch
+
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        flush.fill_(1)
+        wk.step()
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for s in range(steps):
+        flush.fill_(s & 0xFF)
+        starts[s].record(stream)
+        wk.step()
+        ends[s].record(stream)
+    torch.cuda.synchronize(device)
+    times = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    del flush
+    return times
+
+
+def _measure_e2e(wk, steps, warmup, device):
+    import torch
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(1, warmup)):
+        wk.e2e_step()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        wk.e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) / steps
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    peak, peak_kind = _peaks()
+
+    wk = WORKLOADS[args.workload]()
+    wk.setup(rank, world, device)
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        times = _measure(wk, args.steps, args.warmup, device)
+    clock = clocks.summary()
+    ms_step = sum(times) / len(times)
+    t = torch.tensor([ms_step], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step_max = float(t.item())
+    e2e_ms = _measure_e2e(wk, max(3, args.steps // 2), args.warmup, device)
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+
+    problem_bytes = _problem_bytes(wk)
+    value = problem_bytes / (ms_step_max * 1e-3) / 1e9
+    # roofline of the dominant kernel on this rank: its local algorithmic bytes
+    local_bytes = getattr(wk, "local_bytes", None) or _local_bytes(wk)
+    achieved = local_bytes / (ms_step * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": wk.unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step_max, 5),
+        "higher_is_better": True,
+        "scaling": wk.scaling,
+        "vs_baseline": None,
+        "dtype": wk.dtype,
+        "data": "synthetic (seeded numpy default_rng, BASELINE config shapes)",
+        "config": dict(wk.config(), parallelism=f"row-shard x{world}, nnz-balanced" if world > 1 else "1 GPU"),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": _traffic(wk.name),
+                     "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else peak_kind},
+        "e2e": {"value": round(problem_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": wk.unit,
+                "h2d_bytes_per_step": int(wk.h2d_bytes), "d2h_bytes_per_step": int(wk.d2h_bytes),
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(wk.launches_per_step * args.steps),
+        "clocks": clock,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        workers = len(os.sched_getaffinity(0))
+        v, sample = wk.cpu_sample(workers, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
+                                "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop"}
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras = {}
+        for name in ("spmv_lap2d", "spmv_powerlaw", "spmm_bf16", "spmm_f32"):
+            if name == args.workload:
+                continue
+            try:
+                extras[name] = _extra(name, args, device, peak)
+            except Exception as exc:  # report, do not hide
+                extras[name] = {"error": f"{type(exc).__name__}: {exc}"}
+        line["workloads"] = extras
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _problem_bytes(wk):
+    return wk.problem_bytes
+
+
+def _local_bytes(wk):
+    if isinstance(wk, SpmmWorkload):
+        s = 2 if wk.bf16 else 4
+        d = wk.host[0]
+        return d.size * (s + 4) + 4 * (wk.rows + 1) + wk.n * wk.k * s + wk.rows * wk.k * s
+    return wk.local_bytes
+
+
+_TRAFFIC = {}
+
+
+def _traffic(name):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not _TRAFFIC and os.path.exists(path):
+        with open(path) as f:
+            _TRAFFIC.update(json.load(f))
+    return _TRAFFIC.get(name)
+
+
+def _extra(name, args, device, peak):
+    import torch
+
+    wk = WORKLOADS[name]()
+    wk.setup(0, 1, device)
+    times = _measure(wk, max(3, args.steps), args.warmup, device)
+    ms_step = sum(times) / len(times)
+    b = _local_bytes(wk)
+    out = {"value": round(b / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms_step, 5),
+           "frac_of_peak": round(b / (ms_step * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes": int(b),
+           "config": wk.config(), "dtype": wk.dtype}
+    del wk
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if world > 1 and rank != 0:
+        return
+    wk = WORKLOADS[args.workload]()
+    _setup_host_only(wk)
+    workers = len(os.sched_getaffinity(0))
+    vals = []
+    sample = ""
+    for _ in range(args.warmup):
+        wk.cpu_sample(workers, budget_s=0.0)
+    for _ in range(args.steps):
+        v, sample = wk.cpu_sample(workers, budget_s=0.0)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": round(v, 3), "unit": wk.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": wk.scaling, "vs_baseline": None,
+            "dtype": wk.dtype, "data": "synthetic (seeded numpy default_rng, BASELINE config shapes)",
+            "config": wk.config(), "impl": "reference",
+            "cpu_baseline": {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
+                             "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop "
+                                                "(the reference itself needs MLX, absent here)"},
+            "e2e": {"value": round(v, 3), "unit": wk.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _setup_host_only(wk):
+    if isinstance(wk, SpmmWorkload):
+        (d, i, p), shape = wl.random_k_per_row(wk.n, wk.n, wk.per_row, wk.seed)
+        B = np.random.default_rng(wk.seed + 100).uniform(-1, 1, (wk.n, wk.k)).astype(np.float32)
+        wk.host, wk.rows = (d, i, p, B), wk.n
+    else:
+        (d, i, p), shape = wk.make()
+        x = wl.uniform_vector(shape[1], wk.x_seed)
+        wk.host, wk.rows, wk.n = (d, i, p, x), shape[0], shape[1]
+        wk.local_bytes = d.size * (4 + wk.it_bytes) + wk.it_bytes * (wk.rows + 1) + 8 * wk.n
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="spmm_f32", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

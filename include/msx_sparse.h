@@ -1,0 +1,168 @@
+/*
+ * msx_sparse.h - C ABI of the B200 (sm_100a) sparse-product library.
+ *
+ * This is the drop-in boundary under the Python `mlx_sparse` package. Each entry
+ * point replaces one native op that mlx-sparse's `_native.py` reaches through its
+ * nanobind `_ext` module; the reference binding is cited beside each declaration
+ * (paths are relative to the mlx-sparse source tree).
+ *
+ * Conventions
+ *  - All array arguments are DEVICE pointers to contiguous (dense, stride-1)
+ *    buffers on the current CUDA device. Inputs are borrowed, never consumed.
+ *  - `value_dtype` is one of MSX_F32 / MSX_F16 / MSX_BF16; `index_dtype` is
+ *    MSX_I32 / MSX_I64 and applies to both `indices` and `indptr`.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Work is enqueued
+ *    and the call returns without synchronising, except where the reference op
+ *    is itself host-synchronising (SpGEMM sizes, solver status).
+ *  - Every function returns an msx_status; on failure msx_last_error() returns a
+ *    thread-local message. MSX_ERR_INVALID maps to ValueError, MSX_ERR_TYPE to
+ *    TypeError, MSX_ERR_OVERFLOW to OverflowError, the rest to RuntimeError.
+ *  - Temporary device memory comes from the stream-ordered allocator
+ *    (cudaMallocAsync on `stream`), so calls are re-entrant per stream.
+ */
+#ifndef MSX_SPARSE_H
+#define MSX_SPARSE_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MSX_API __attribute__((visibility("default")))
+#else
+#define MSX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum { MSX_F32 = 0, MSX_F16 = 1, MSX_BF16 = 2 } msx_value_dtype;
+typedef enum { MSX_I32 = 0, MSX_I64 = 1 } msx_index_dtype;
+
+typedef enum {
+  MSX_OK = 0,
+  MSX_ERR_INVALID = 1,  /* std::invalid_argument -> ValueError   */
+  MSX_ERR_TYPE = 2,     /* dtype problems          -> TypeError    */
+  MSX_ERR_OVERFLOW = 3, /* std::overflow_error     -> OverflowError */
+  MSX_ERR_RUNTIME = 4,  /* std::runtime_error      -> RuntimeError */
+  MSX_ERR_CUDA = 5      /* CUDA runtime failure    -> RuntimeError */
+} msx_status;
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+MSX_API const char *msx_last_error(void);
+
+/* Library version and the SM architecture it was compiled for (e.g. 100). */
+MSX_API int msx_version(void);
+MSX_API int msx_compiled_sm(void);
+
+/* ------------------------------------------------------------------------ */
+/* SpMV plan: nnz-balanced merge-path tile partition of a CSR matrix.        */
+/* ------------------------------------------------------------------------ */
+/* A plan caches the row-aligned, nnz-balanced tile partition that the SpMV
+ * kernel walks, so repeated products with one matrix skip the partition
+ * search. It depends only on `indptr`. The reference has no counterpart: its
+ * CPU path recomputes nnz-weighted worker ranges on every call
+ * (src/common/cpu_parallel.cpp:202-253, reached from
+ * src/sparse/csr_matvec/csr_matvec.cpp:156-166).
+ * msx_spmv_plan_create allocates device memory (cudaMalloc) and synchronises
+ * `stream` once; the plan is immutable afterwards and may be shared by
+ * concurrent calls on any stream of the same device. */
+typedef struct msx_spmv_plan msx_spmv_plan;
+MSX_API int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows,
+                         int64_t nnz, void *stream, msx_spmv_plan **out);
+MSX_API int msx_spmv_plan_destroy(msx_spmv_plan *plan);
+/* Number of tiles and of tile boundaries that fall inside a (long) row. */
+MSX_API int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_tiles,
+                       int64_t *n_split_boundaries);
+
+/* y = A @ x. Replaces `csr_matvec(data, indices, indptr, x, n_rows, n_cols)`
+ * (src/bindings.cpp:874-883 -> src/sparse/csr_matvec/csr_matvec.cpp:326-356,
+ * CPU loop :79-168). `plan` may be NULL: the partition is then built in
+ * stream-ordered scratch on every call. A plan must have been created for this
+ * matrix's indptr, n_rows and nnz. fp16/bf16 accumulate in fp32. */
+MSX_API int msx_csr_matvec(int value_dtype, int index_dtype, const void *data,
+                   const void *indices, const void *indptr, int64_t nnz,
+                   const void *x, void *y, int64_t n_rows, int64_t n_cols,
+                   const msx_spmv_plan *plan, void *stream);
+
+/* Y = A @ B for a row-major dense B[n_cols, k] -> Y[n_rows, k]. Replaces
+ * `csr_matmul(data, indices, indptr, rhs, n_rows, n_cols)`
+ * (src/bindings.cpp:965-975 -> src/sparse/csr_matmul/csr_matmul.cpp:383-418,
+ * CPU loop :83-222). fp16/bf16 accumulate in fp32. */
+MSX_API int msx_csr_matmul(int value_dtype, int index_dtype, const void *data,
+                   const void *indices, const void *indptr, int64_t nnz,
+                   const void *rhs, int64_t rhs_cols, void *out, int64_t n_rows,
+                   int64_t n_cols, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* SpGEMM C = A @ B, canonical (sorted, duplicate-free, exact zeros pruned). */
+/* ------------------------------------------------------------------------ */
+/* Replaces `csr_matmat(lhs_data, lhs_indices, lhs_indptr, rhs_data,
+ * rhs_indices, rhs_indptr, lhs_n_rows, lhs_n_cols, rhs_n_rows, rhs_n_cols)`
+ * (src/bindings.cpp:1116-1131 -> src/sparse/csr_matmat/csr_matmat.cpp:1319-1424,
+ * host Gustavson :544-817). Two-call protocol because the output size is data
+ * dependent:
+ *   1. msx_csr_matmat_symbolic computes the exact output row counts (after
+ *      zero pruning), writes the output indptr[lhs_n_rows + 1] (dtype
+ *      `out_index_dtype`) and returns the total in *out_nnz (synchronises
+ *      `stream`, as the reference's host path does).
+ *   2. msx_csr_matmat_numeric fills caller-allocated out_data[out_nnz] and
+ *      out_indices[out_nnz] using that indptr.
+ * The output index dtype follows the reference rule (:1354-1356): the inputs'
+ * dtype when lhs and rhs agree, else int64. Each output value is accumulated
+ * in the reference's order (lhs position, then rhs position) in fp32, so
+ * exact cancellations agree. `prune_zeros` = 1 drops entries whose stored
+ * value is exactly zero (the reference's csr_matmat behaviour, :613-641);
+ * 0 keeps them (used for duplicate summation, I @ A). */
+MSX_API int msx_csr_matmat_symbolic(int value_dtype, int lhs_index_dtype,
+                            const void *lhs_data, const void *lhs_indices,
+                            const void *lhs_indptr, int64_t lhs_nnz,
+                            int rhs_index_dtype, const void *rhs_data,
+                            const void *rhs_indices, const void *rhs_indptr,
+                            int64_t rhs_nnz, int64_t lhs_n_rows,
+                            int64_t lhs_n_cols, int64_t rhs_n_rows,
+                            int64_t rhs_n_cols, int out_index_dtype,
+                            void *out_indptr, int64_t *out_nnz,
+                            int prune_zeros, void *stream);
+MSX_API int msx_csr_matmat_numeric(int value_dtype, int lhs_index_dtype,
+                           const void *lhs_data, const void *lhs_indices,
+                           const void *lhs_indptr, int64_t lhs_nnz,
+                           int rhs_index_dtype, const void *rhs_data,
+                           const void *rhs_indices, const void *rhs_indptr,
+                           int64_t rhs_nnz, int64_t lhs_n_rows,
+                           int64_t lhs_n_cols, int64_t rhs_n_rows,
+                           int64_t rhs_n_cols, int out_index_dtype,
+                           const void *out_indptr, int64_t out_nnz,
+                           void *out_data, void *out_indices,
+                           int prune_zeros, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Conjugate gradients (fp32 values, int32/int64 indices).                   */
+/* ------------------------------------------------------------------------ */
+/* Plain CG. Replaces `csr_cg(data, indices, indptr, b, x0, n_rows, n_cols,
+ * rtol, atol, maxiter)` (src/bindings.cpp:1133-1145 -> src/linalg/cg/cg.cpp:
+ * 338-379, CPU loop :75-256). Writes x_out[n_rows] on the device and the
+ * scalars *info (0 converged, >0 iteration budget exhausted, -1 breakdown,
+ * -3 non-finite), *residual and *iterations on the HOST (the call synchronises
+ * `stream` at the end, like the reference's finish_solver_result). */
+MSX_API int msx_csr_cg(int index_dtype, const float *data, const void *indices,
+               const void *indptr, int64_t nnz, const float *b,
+               const float *x0, float *x_out, int64_t n_rows, int64_t n_cols,
+               float rtol, float atol, int32_t maxiter, int32_t *info,
+               float *residual, int32_t *iterations, void *stream);
+
+/* Jacobi-preconditioned CG. Replaces `csr_pcg_jacobi(data, indices, indptr, b,
+ * x0, inv_diag, n_rows, n_cols, rtol, atol, maxiter)` (src/bindings.cpp:
+ * 1147-1161 -> src/preconditioners/pcg/pcg.cpp:317-366, CPU loop :70-230).
+ * Status -2 = non-positive preconditioned inner product. */
+MSX_API int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *indices,
+                       const void *indptr, int64_t nnz, const float *b,
+                       const float *x0, const float *inv_diag, float *x_out,
+                       int64_t n_rows, int64_t n_cols, float rtol, float atol,
+                       int32_t maxiter, int32_t *info, float *residual,
+                       int32_t *iterations, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSX_SPARSE_H */

@@ -1,0 +1,170 @@
+// CSR x dense row-major matrix (SpMM) for sm_100a.
+//
+// Reference behaviour: src/sparse/csr_matmul/csr_matmul.cpp:83-222 - for each
+// row, every nonzero adds data[p] * rhs[col[p], :] into a row accumulator (fp32
+// for fp16/bf16 values), in nonzero order, then the row is cast and stored.
+//
+// B200 design: this is a gather of dense RHS rows, not a contraction, so it is
+// bound by HBM/L2 bandwidth and uses no tensor cores. A group of L lanes owns
+// one output row slab of W = L*V columns (V values per 16-byte vector per
+// lane); each lane accumulates V columns sequentially over the row's
+// nonzeros, which reproduces the reference's summation order exactly. The RHS
+// columns are processed in slabs (grid.y) small enough that one slab of the
+// RHS stays resident in L2 while all rows stream past it, so each random RHS
+// row gather hits L2 instead of HBM; the matrix arrays are re-streamed once
+// per slab with evict-first loads.
+#include "common.cuh"
+
+namespace msx {
+
+namespace {
+
+template <typename T, int V>
+__device__ __forceinline__ void load_vec(const T *p, float (&out)[V]) {
+  if constexpr (V * sizeof(T) == 16) {
+    const float4 raw = __ldg(reinterpret_cast<const float4 *>(p));
+    const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) out[i] = VT<T>::load(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) out[i] = VT<T>::load(__ldg(p + i));
+  }
+}
+
+template <typename T, int V>
+__device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
+  if constexpr (V * sizeof(T) == 16) {
+    float4 raw;
+    T *e = reinterpret_cast<T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) e[i] = VT<T>::store(in[i]);
+    __stcs(reinterpret_cast<float4 *>(p), raw);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) p[i] = VT<T>::store(in[i]);
+  }
+}
+
+// grid.x: row blocks, grid.y: column slabs. Each L-lane group handles one row
+// and W = L*V columns of slab blockIdx.y.
+template <typename T, typename I, int V, int L>
+__global__ void __launch_bounds__(256)
+spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+            const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+  constexpr int kRowsPerBlock = 256 / L;
+  const int lane_in_row = threadIdx.x % L;
+  const int64_t row = blockIdx.x * (int64_t)kRowsPerBlock + threadIdx.x / L;
+  if (row >= n_rows) return;
+  const int64_t slab0 = blockIdx.y * slab_cols;
+  const int64_t slab1 = min(slab0 + slab_cols, k);
+  const int64_t p0 = (int64_t)indptr[row], p1 = (int64_t)indptr[row + 1];
+  for (int64_t c = slab0 + (int64_t)lane_in_row * V; c < slab1; c += (int64_t)L * V) {
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    int64_t p = p0;
+    // Unrolled by 4 so four RHS row gathers are in flight per lane.
+    for (; p + 4 <= p1; p += 4) {
+      I col[4];
+      float a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        col[u] = ld_stream(indices + p + u);
+        a[u] = VT<T>::load(ld_stream(data + p + u));
+      }
+      float b[4][V];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load_vec<T, V>(rhs + (int64_t)col[u] * k + c, b[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a[u], b[u][i]));
+    }
+    for (; p < p1; ++p) {
+      const I col = ld_stream(indices + p);
+      const float a = VT<T>::load(ld_stream(data + p));
+      float b[V];
+      load_vec<T, V>(rhs + (int64_t)col * k + c, b);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, b[i]));
+    }
+    store_vec<T, V>(out + row * k + c, acc);
+  }
+}
+
+template <typename T, typename I, int V, int L>
+void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs, T *out, int64_t n_rows,
+                 int64_t k, int64_t slab_cols, cudaStream_t stream) {
+  constexpr int kRowsPerBlock = 256 / L;
+  const int64_t n_slabs = ceil_div(k, slab_cols);
+  dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
+  spmm_kernel<T, I, V, L><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  MSX_CHECK_LAUNCH();
+}
+
+// Bytes of the RHS slab that should stay L2 resident while rows stream by.
+int64_t spmm_l2_budget() {
+  static int64_t budget = [] {
+    const char *env = getenv("MSX_SPMM_L2_BYTES");
+    if (env && *env) return (int64_t)atoll(env);
+    int dev = 0, l2 = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) == cudaSuccess && l2 > 0)
+      return (int64_t)l2 / 2;
+    return (int64_t)48 << 20;
+  }();
+  return budget;
+}
+
+}  // namespace
+
+void spmm_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+              const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, cudaStream_t stream) {
+  if (n_rows == 0 || k == 0) return;
+  dispatch_value(value_dtype, [&](auto vtyp) {
+    using T = decltype(vtyp);
+    constexpr int kVec = 16 / sizeof(T);
+    dispatch_index(index_dtype, [&](auto ityp) {
+      using I = decltype(ityp);
+      const bool vec_ok = (k % kVec == 0) && (reinterpret_cast<uintptr_t>(rhs) % 16 == 0) &&
+                          (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+      const int64_t elem = sizeof(T);
+      // Number of column slabs so that one RHS slab (n_cols x slab) fits the
+      // L2 budget.
+      const int64_t budget = spmm_l2_budget();
+      int64_t n_slabs = 1;
+      if (n_cols > 0 && budget > 0) n_slabs = ceil_div(n_cols * k * elem, budget);
+      if (n_slabs < 1) n_slabs = 1;
+      const T *d = static_cast<const T *>(data);
+      const I *ix = static_cast<const I *>(indices);
+      const I *ip = static_cast<const I *>(indptr);
+      const T *b = static_cast<const T *>(rhs);
+      T *o = static_cast<T *>(out);
+      if (vec_ok) {
+        const int64_t kv = k / kVec;                     // 16-byte vectors per row
+        const int64_t slab_vecs = ceil_div(kv, n_slabs);  // >= 1
+        if (slab_vecs >= 8) {
+          launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream);
+        } else if (slab_vecs >= 4) {
+          launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream);
+        } else if (slab_vecs >= 2) {
+          launch_spmm<T, I, kVec, 2>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 2) * 2 * kVec, stream);
+        } else {
+          launch_spmm<T, I, kVec, 1>(d, ix, ip, b, o, n_rows, k, kVec, stream);
+        }
+      } else {
+        // Scalar path for widths that are not a multiple of the 16-byte vector.
+        if (k >= 16) {
+          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(ceil_div(k, n_slabs), 16) * 16, stream);
+        } else if (k >= 4) {
+          launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream);
+        } else {
+          launch_spmm<T, I, 1, 1>(d, ix, ip, b, o, n_rows, k, k, stream);
+        }
+      }
+    });
+  });
+}
+
+}  // namespace msx

@@ -1,0 +1,203 @@
+"""Native seam: ctypes bindings of the sm_100a C-ABI library ``libmsx_b200.so``.
+
+Mirrors mlx-sparse's ``mlx_sparse/_native.py`` (csr_matvec :179-189, csr_matmul
+:286-296, csr_matmat :393-408, csr_cg :883-909, csr_pcg_jacobi :1139-1167):
+same function names and argument meaning, torch CUDA tensors in place of MLX
+arrays. There is no CPU fallback: if the library or a CUDA device is missing,
+every op raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libmsx_b200.so")
+
+MSX_F32, MSX_F16, MSX_BF16 = 0, 1, 2
+MSX_I32, MSX_I64 = 0, 1
+
+VALUE_CODES = {torch.float32: MSX_F32, torch.float16: MSX_F16, torch.bfloat16: MSX_BF16}
+INDEX_CODES = {torch.int32: MSX_I32, torch.int64: MSX_I64}
+
+_ERRORS = {1: ValueError, 2: TypeError, 3: OverflowError, 4: RuntimeError, 5: RuntimeError}
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def extension():
+    """Loads the CUDA library; raises RuntimeError when it is unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"mlx_sparse CUDA library not found at {LIB_PATH}; build it with "
+                "`python mlx-sparse_b200/build.py` (there is no CPU fallback)."
+            )
+        L = ctypes.CDLL(LIB_PATH)
+        p, i64, c_int, c_float = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+        L.msx_last_error.restype = ctypes.c_char_p
+        L.msx_spmv_plan_create.argtypes = [c_int, p, i64, i64, p, ctypes.POINTER(p)]
+        L.msx_spmv_plan_destroy.argtypes = [p]
+        L.msx_spmv_plan_info.argtypes = [p, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.msx_csr_matvec.argtypes = [c_int, c_int, p, p, p, i64, p, p, i64, i64, p, p]
+        L.msx_csr_matmul.argtypes = [c_int, c_int, p, p, p, i64, p, i64, p, i64, i64, p]
+        mm = [c_int, c_int, p, p, p, i64, c_int, p, p, p, i64, i64, i64, i64, i64, c_int]
+        if hasattr(L, "msx_csr_matmat_symbolic"):
+            L.msx_csr_matmat_symbolic.argtypes = mm + [p, ctypes.POINTER(i64), c_int, p]
+            L.msx_csr_matmat_numeric.argtypes = mm + [p, i64, p, p, c_int, p]
+        if hasattr(L, "msx_csr_cg"):
+            L.msx_csr_cg.argtypes = [c_int, p, p, p, i64, p, p, p, i64, i64, c_float, c_float, ctypes.c_int32,
+                                     p, p, p, p]
+            L.msx_csr_pcg_jacobi.argtypes = [c_int, p, p, p, i64, p, p, p, p, i64, i64, c_float, c_float,
+                                             ctypes.c_int32, p, p, p, p]
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        msg = extension().msx_last_error().decode()
+        raise _ERRORS.get(status, RuntimeError)(msg)
+
+
+def require_cuda(*tensors) -> torch.device:
+    dev = None
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "mlx_sparse (B200 build) runs on CUDA tensors only; got a tensor on "
+                f"{t.device}. Move inputs to a CUDA device (there is no CPU fallback)."
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"all inputs must be on one device, got {dev} and {t.device}.")
+    return dev
+
+
+def stream_ptr(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _p(t) -> int:
+    return t.data_ptr() if t is not None else 0
+
+
+class SpmvPlan:
+    """Owns an ``msx_spmv_plan`` (nnz-balanced tile partition of one matrix)."""
+
+    __slots__ = ("handle", "n_tiles", "n_split", "device", "__weakref__")
+
+    def __init__(self, indptr: torch.Tensor, n_rows: int, nnz: int):
+        L = extension()
+        self.device = indptr.device
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(L.msx_spmv_plan_create(INDEX_CODES[indptr.dtype], _p(indptr), n_rows, nnz,
+                                         stream_ptr(self.device), ctypes.byref(h)))
+        self.handle = h
+        nt, ns = ctypes.c_int64(), ctypes.c_int64()
+        check(L.msx_spmv_plan_info(h, ctypes.byref(nt), ctypes.byref(ns)))
+        self.n_tiles, self.n_split = nt.value, ns.value
+
+    def __del__(self):
+        try:
+            if self.handle:
+                # outstanding kernels may still read the plan
+                torch.cuda.synchronize(self.device)
+                extension().msx_spmv_plan_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+def csr_matvec(data, indices, indptr, x, shape, *, plan: SpmvPlan | None = None, out=None):
+    L = extension()
+    dev = require_cuda(data, indices, indptr, x)
+    data, indices, indptr, x = (t.contiguous() for t in (data, indices, indptr, x))
+    y = out if out is not None else torch.empty(shape[0], dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_matvec(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                               _p(indptr), data.numel(), _p(x), _p(y), shape[0], shape[1],
+                               plan.handle if plan is not None else None, stream_ptr(dev)))
+    return y
+
+
+def csr_matmul(data, indices, indptr, rhs, shape, *, out=None):
+    L = extension()
+    dev = require_cuda(data, indices, indptr, rhs)
+    data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
+    k = rhs.shape[1]
+    y = out if out is not None else torch.empty((shape[0], k), dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_matmul(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                               _p(indptr), data.numel(), _p(rhs), k, _p(y), shape[0], shape[1],
+                               stream_ptr(dev)))
+    return y
+
+
+def csr_matmat(lhs, rhs, *, prune_zeros: bool = True):
+    """Returns (data, indices, indptr) of the canonical product lhs @ rhs."""
+    L = extension()
+    dev = require_cuda(lhs.data, lhs.indices, lhs.indptr, rhs.data, rhs.indices, rhs.indptr)
+    ld, li, lp = (t.contiguous() for t in (lhs.data, lhs.indices, lhs.indptr))
+    rd, ri, rp = (t.contiguous() for t in (rhs.data, rhs.indices, rhs.indptr))
+    out_it = li.dtype if li.dtype == ri.dtype else torch.int64
+    m, n = lhs.shape[0], rhs.shape[1]
+    args = [VALUE_CODES[ld.dtype], INDEX_CODES[li.dtype], _p(ld), _p(li), _p(lp), ld.numel(),
+            INDEX_CODES[ri.dtype], _p(rd), _p(ri), _p(rp), rd.numel(), lhs.shape[0], lhs.shape[1],
+            rhs.shape[0], rhs.shape[1], INDEX_CODES[out_it]]
+    out_indptr = torch.empty(m + 1, dtype=out_it, device=dev)
+    nnz = ctypes.c_int64()
+    with torch.cuda.device(dev):
+        s = stream_ptr(dev)
+        check(L.msx_csr_matmat_symbolic(*args, _p(out_indptr), ctypes.byref(nnz), int(prune_zeros), s))
+        out_data = torch.empty(nnz.value, dtype=ld.dtype, device=dev)
+        out_indices = torch.empty(nnz.value, dtype=out_it, device=dev)
+        check(L.msx_csr_matmat_numeric(*args, _p(out_indptr), nnz.value, _p(out_data), _p(out_indices),
+                                       int(prune_zeros), s))
+    return out_data, out_indices, out_indptr
+
+
+def _solver_outputs(dev, n):
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    return x, ctypes.c_int32(), ctypes.c_float(), ctypes.c_int32()
+
+
+def csr_cg(data, indices, indptr, b, x0, shape, *, rtol, atol, maxiter):
+    L = extension()
+    dev = require_cuda(data, indices, indptr, b, x0)
+    data, indices, indptr, b, x0 = (t.contiguous() for t in (data, indices, indptr, b, x0))
+    x, info, res, its = _solver_outputs(dev, shape[0])
+    with torch.cuda.device(dev):
+        check(L.msx_csr_cg(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(), _p(b),
+                           _p(x0), _p(x), shape[0], shape[1], float(rtol), float(atol), int(maxiter),
+                           ctypes.addressof(info), ctypes.addressof(res), ctypes.addressof(its), stream_ptr(dev)))
+    return x, info.value, res.value, its.value
+
+
+def csr_pcg_jacobi(data, indices, indptr, b, x0, inv_diag, shape, *, rtol, atol, maxiter):
+    L = extension()
+    dev = require_cuda(data, indices, indptr, b, x0, inv_diag)
+    data, indices, indptr, b, x0, inv_diag = (t.contiguous() for t in (data, indices, indptr, b, x0, inv_diag))
+    x, info, res, its = _solver_outputs(dev, shape[0])
+    with torch.cuda.device(dev):
+        check(L.msx_csr_pcg_jacobi(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(),
+                                   _p(b), _p(x0), _p(inv_diag), _p(x), shape[0], shape[1], float(rtol),
+                                   float(atol), int(maxiter), ctypes.addressof(info), ctypes.addressof(res),
+                                   ctypes.addressof(its), stream_ptr(dev)))
+    return x, info.value, res.value, its.value

@@ -1,0 +1,178 @@
+"""TEST INFRASTRUCTURE ONLY - numpy/ctypes front-end of the CPU oracle.
+
+Wraps ``liboracle.so`` (``oracle.cpp``: a C++ restatement of mlx-sparse's CPU
+loops for SpMV, SpMM, SpGEMM, CG and Jacobi-PCG, each function citing the
+reference lines it follows). Used by ``tests/`` as the parity checker and by
+``bench.py`` as the timed CPU baseline; the product path never imports it.
+
+Parity is pinned by ``tests/test_oracle.py``: the oracle reproduces every
+known-answer case of the reference's own tests for this path
+(tests/test_csr_matvec.py:25-36, tests/test_csr_matmul.py:25-45,383-432,480-517,
+tests/test_linalg_preconditioners.py:1977-2123) and agrees with SciPy, the
+secondary oracle those tests use.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+_VT = {np.dtype(np.float32): 0, np.dtype(np.float16): 1}
+_IT = {np.dtype(np.int32): 0, np.dtype(np.int64): 1}
+
+# bf16 arrays are carried as uint16 bit patterns on the numpy side.
+BF16 = "bf16"
+
+
+def build() -> str:
+    """Compiles liboracle.so if it is missing or older than oracle.cpp."""
+    src = os.path.join(HERE, "oracle.cpp")
+    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        c_i64, c_int, c_float, p = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+        L.orc_last_error.restype = ctypes.c_char_p
+        L.orc_csr_matvec.argtypes = [c_int, c_int, p, p, p, p, p, c_i64, c_int]
+        L.orc_csr_matmul.argtypes = [c_int, c_int, p, p, p, p, c_i64, p, c_i64, c_int]
+        L.orc_csr_matmat.argtypes = [c_int, c_int, p, p, p, c_int, p, p, p, c_i64, c_i64, c_i64]
+        L.orc_csr_matmat.restype = p
+        L.orc_matmat_nnz.argtypes = [p]
+        L.orc_matmat_nnz.restype = c_i64
+        L.orc_matmat_copy.argtypes = [p, p, p, p]
+        L.orc_matmat_free.argtypes = [p]
+        L.orc_csr_cg.argtypes = [c_int, p, p, p, p, p, p, c_i64, c_float, c_float, c_int, p, p, p]
+        L.orc_csr_pcg_jacobi.argtypes = [c_int, p, p, p, p, p, p, p, c_i64, c_float, c_float, c_int, p, p, p, c_int]
+        L.orc_weighted_ranges.argtypes = [p, c_i64, c_int, p]
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _vt(values: np.ndarray, bf16: bool) -> int:
+    if bf16:
+        assert values.dtype == np.uint16
+        return 2
+    return _VT[values.dtype]
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise RuntimeError(lib().orc_last_error().decode())
+
+
+def default_workers() -> int:
+    """The reference's auto worker count (src/common/cpu_parallel.cpp:97-123)."""
+    for name in ("OMP_NUM_THREADS", "SLURM_CPUS_PER_TASK", "PBS_NP", "LSB_DJOB_NUMPROC", "NSLOTS"):
+        try:
+            v = int(os.environ.get(name, ""))
+            if v > 0:
+                return v
+        except ValueError:
+            pass
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def csr_matvec(data, indices, indptr, x, n_rows, *, bf16=False, workers=1):
+    data, indices, indptr, x = (np.ascontiguousarray(a) for a in (data, indices, indptr, x))
+    y = np.empty(n_rows, dtype=data.dtype)
+    _check(lib().orc_csr_matvec(_vt(data, bf16), _IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr),
+                                _ptr(x), _ptr(y), n_rows, workers))
+    return y
+
+
+def csr_matmul(data, indices, indptr, rhs, n_rows, *, bf16=False, workers=1):
+    data, indices, indptr, rhs = (np.ascontiguousarray(a) for a in (data, indices, indptr, rhs))
+    k = rhs.shape[1]
+    out = np.empty((n_rows, k), dtype=data.dtype)
+    _check(lib().orc_csr_matmul(_vt(data, bf16), _IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr),
+                                _ptr(rhs), k, _ptr(out), n_rows, workers))
+    return out
+
+
+def csr_matmat(a, b, shape_a, shape_b, *, bf16=False):
+    """a, b: (data, indices, indptr). Returns (data, indices, indptr) with the
+    reference's output index dtype rule (csr_matmat.cpp:1354-1356)."""
+    ad, ai, ap = (np.ascontiguousarray(v) for v in a)
+    bd, bi, bp = (np.ascontiguousarray(v) for v in b)
+    L = lib()
+    h = L.orc_csr_matmat(_vt(ad, bf16), _IT[ai.dtype], _ptr(ad), _ptr(ai), _ptr(ap), _IT[bi.dtype], _ptr(bd),
+                         _ptr(bi), _ptr(bp), shape_a[0], shape_b[0], shape_b[1])
+    if not h:
+        raise ValueError(L.orc_last_error().decode())
+    try:
+        nnz = L.orc_matmat_nnz(h)
+        data = np.empty(nnz, dtype=ad.dtype)
+        idx = np.empty(nnz, dtype=np.int64)
+        ptr = np.empty(shape_a[0] + 1, dtype=np.int64)
+        L.orc_matmat_copy(h, _ptr(data), _ptr(idx), _ptr(ptr))
+    finally:
+        L.orc_matmat_free(h)
+    out_it = ai.dtype if ai.dtype == bi.dtype else np.dtype(np.int64)
+    return data, idx.astype(out_it), ptr.astype(out_it)
+
+
+def csr_cg(data, indices, indptr, b, x0, *, rtol, atol, maxiter):
+    data, indices, indptr, b, x0 = (np.ascontiguousarray(a) for a in (data, indices, indptr, b, x0))
+    n = b.shape[0]
+    x = np.empty(n, dtype=np.float32)
+    info, res, its = ctypes.c_int(), ctypes.c_float(), ctypes.c_int()
+    _check(lib().orc_csr_cg(_IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr), _ptr(b), _ptr(x0),
+                            _ptr(x), n, rtol, atol, maxiter, ctypes.byref(info), ctypes.byref(res),
+                            ctypes.byref(its)))
+    return x, info.value, res.value, its.value
+
+
+def csr_pcg_jacobi(data, indices, indptr, b, x0, inv_diag, *, rtol, atol, maxiter, stop_after=0):
+    data, indices, indptr, b, x0, inv_diag = (
+        np.ascontiguousarray(a) for a in (data, indices, indptr, b, x0, inv_diag))
+    n = b.shape[0]
+    x = np.empty(n, dtype=np.float32)
+    info, res, its = ctypes.c_int(), ctypes.c_float(), ctypes.c_int()
+    _check(lib().orc_csr_pcg_jacobi(_IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr), _ptr(b),
+                                    _ptr(x0), _ptr(inv_diag), _ptr(x), n, rtol, atol, maxiter, ctypes.byref(info),
+                                    ctypes.byref(res), ctypes.byref(its), stop_after))
+    return x, info.value, res.value, its.value
+
+
+def weighted_ranges(work, parts):
+    work = np.ascontiguousarray(work, dtype=np.int64)
+    out = np.empty(2 * max(parts, 1), dtype=np.int64)
+    n = lib().orc_weighted_ranges(_ptr(work), work.shape[0], parts, _ptr(out))
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n)]
+
+
+# ---- bf16 helpers (numpy has no bfloat16) -----------------------------------
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16 bit patterns (uint16)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_bits_to_f32(a: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(a, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)

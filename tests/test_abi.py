@@ -1,0 +1,83 @@
+"""C-ABI library checks that need no GPU: it loads, exports every symbol that
+include/msx_sparse.h declares, reports errors through status codes, and the
+Python layer validates metadata with the reference's messages."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    text = open(os.path.join(ROOT, "include", "msx_sparse.h")).read()
+    return sorted(set(re.findall(r"MSX_API\s+[\w\s\*]*?\b(msx_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    from mlx_sparse import _native
+
+    lib = _native.extension()
+    names = _declared_symbols()
+    assert "msx_csr_matvec" in names and "msx_csr_pcg_jacobi" in names
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_library_reports_invalid_arguments_without_gpu():
+    from mlx_sparse import _native
+
+    lib = _native.extension()
+    assert lib.msx_compiled_sm() == 100
+    # negative shape -> MSX_ERR_INVALID with the reference's message
+    rc = lib.msx_csr_matvec(0, 0, None, None, None, 0, None, None, -1, 3, None, None)
+    assert rc == 1
+    assert b"non-negative" in lib.msx_last_error()
+    # bad dtype code -> MSX_ERR_TYPE
+    rc = lib.msx_csr_matvec(7, 0, None, None, None, 0, None, None, 0, 0, None, None)
+    assert rc == 2
+    assert b"dtype must be one of" in lib.msx_last_error()
+    with pytest.raises(ValueError):
+        _native.check(1)
+
+
+def test_no_cpu_fallback():
+    from mlx_sparse import _native
+
+    t = torch.zeros(3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _native.require_cuda(t)
+
+
+def test_validation_messages_match_reference():
+    from mlx_sparse import _validation as v
+
+    d = torch.zeros(4)
+    i = torch.zeros(4, dtype=torch.int32)
+    p = torch.zeros(4, dtype=torch.int32)
+    v.validate_csr_metadata(d, i, p, (3, 4))
+    with pytest.raises(TypeError, match="dtype must be one"):
+        v.validate_csr_metadata(d.to(torch.float64), i, p, (3, 4))
+    with pytest.raises(TypeError, match="same dtype"):
+        v.validate_csr_metadata(d, i, p.to(torch.int64), (3, 4))
+    with pytest.raises(ValueError, match="n_rows"):
+        v.validate_csr_metadata(d, i, p, (4, 4))
+    with pytest.raises(ValueError, match="n_cols"):
+        v.validate_csr_matvec_inputs(d, i, p, torch.zeros(5), (3, 4))
+    with pytest.raises(TypeError, match="same dtype"):
+        v.validate_csr_matvec_inputs(d, i, p, torch.zeros(4, dtype=torch.float16), (3, 4))
+    with pytest.raises(ValueError, match="rank-2"):
+        v.validate_csr_matmul_inputs(d, i, p, torch.zeros(4), (3, 4))
+
+
+def test_solver_status_reasons():
+    from mlx_sparse.linalg.diagnostics import finish_solver_result, status_reason
+
+    assert status_reason(0)[0] == "converged"
+    assert status_reason(5)[0] == "iteration_limit"
+    assert status_reason(-2)[1] == "non_positive_preconditioned_inner_product"
+    x, info = finish_solver_result(None, -3, 1.0, 2, solver="cg", return_info=True)
+    assert info.status == -3 and not info.converged and int(info) == -3

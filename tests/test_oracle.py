@@ -1,0 +1,152 @@
+"""Pins the CPU oracle: reference known answers, SciPy, determinism.
+
+CPU only. The oracle is trusted as the GPU parity checker only because it
+reproduces every known-answer case of the reference's tests for this path
+(tests/golden/reference_cases.json) and agrees with SciPy on seeded inputs.
+"""
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+
+import workloads as wl
+
+
+def _arr(A, it=np.int32):
+    return (np.asarray(A["data"], np.float32), np.asarray(A["indices"], it), np.asarray(A["indptr"], it))
+
+
+@pytest.mark.parametrize("it", [np.int32, np.int64])
+def test_spmv_known_answers(orc, golden, it):
+    for name in ("spmv_hand", "spmv_scipy_456"):
+        c = golden[name]
+        d, i, p = _arr(c["A"], it)
+        y = orc.csr_matvec(d, i, p, np.asarray(c["x"], np.float32), c["A"]["shape"][0])
+        np.testing.assert_allclose(y, np.asarray(c["y"], np.float32), rtol=1e-5, atol=1e-5)
+
+
+def test_spmm_known_answers(orc, golden):
+    for name in ("spmm_hand", "spmm_scipy_789", "spmm_lowp"):
+        c = golden[name]
+        d, i, p = _arr(c["A"])
+        Y = orc.csr_matmul(d, i, p, np.asarray(c["B"], np.float32), c["A"]["shape"][0])
+        np.testing.assert_allclose(Y, np.asarray(c["Y"], np.float32), rtol=1e-5, atol=1e-5)
+
+
+def test_spmm_low_precision(orc, golden):
+    c = golden["spmm_lowp"]
+    d, i, p = _arr(c["A"])
+    B = np.asarray(c["B"], np.float32)
+    Y16 = orc.csr_matmul(d.astype(np.float16), i, p, B.astype(np.float16), 3)
+    np.testing.assert_allclose(Y16.astype(np.float32), c["Y"], rtol=5e-3, atol=5e-3)
+    Yb = orc.csr_matmul(orc.f32_to_bf16_bits(d), i, p, orc.f32_to_bf16_bits(B), 3, bf16=True)
+    np.testing.assert_allclose(orc.bf16_bits_to_f32(Yb), c["Y"], rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("name", ["spgemm_cancel", "spgemm_dense_ordered"])
+def test_spgemm_known_answers(orc, golden, name):
+    c = golden[name]
+    a, b = _arr(c["A"]), _arr(c["B"])
+    d, i, p = orc.csr_matmat(a, b, c["A"]["shape"], c["B"]["shape"])
+    np.testing.assert_array_equal(i, c["C"]["indices"])
+    np.testing.assert_array_equal(p, c["C"]["indptr"])
+    np.testing.assert_allclose(d, c["C"]["data"], rtol=1e-5, atol=1e-5)
+    assert np.all(d != 0)
+    assert i.dtype == np.int32
+
+
+def test_spgemm_mixed_index_dtype_gives_int64(orc, golden):
+    c = golden["spgemm_cancel"]
+    d, i, p = orc.csr_matmat(_arr(c["A"], np.int32), _arr(c["B"], np.int64), c["A"]["shape"], c["B"]["shape"])
+    assert i.dtype == np.int64 and p.dtype == np.int64
+
+
+def test_spgemm_matches_scipy_random(orc):
+    (ad, ai, ap), sa = wl.random_csr(50, 60, 0.08, seed=11)
+    (bd, bi, bp), sb = wl.random_csr(60, 70, 0.08, seed=12)
+    d, i, p = orc.csr_matmat((ad, ai, ap), (bd, bi, bp), sa, sb)
+    C = (sp.csr_matrix((ad, ai, ap), shape=sa) @ sp.csr_matrix((bd, bi, bp), shape=sb)).tocsr()
+    C.eliminate_zeros()
+    C.sort_indices()
+    np.testing.assert_array_equal(i, C.indices)
+    np.testing.assert_array_equal(p, C.indptr)
+    np.testing.assert_allclose(d, C.data, rtol=1e-5, atol=1e-6)
+
+
+def test_pcg_known_answers(orc, golden):
+    for name in ("pcg_2x2", "pcg_4x4", "pcg_scaled_poisson", "pcg_diag"):
+        c = golden[name]
+        d, i, p = _arr(c["A"])
+        n = c["A"]["shape"][0]
+        A = sp.csr_matrix((d, i, p), shape=(n, n))
+        inv = (1.0 / A.diagonal()).astype(np.float32)
+        b = np.asarray(c["b"], np.float32)
+        x, info, res, its = orc.csr_pcg_jacobi(d, i, p, b, np.zeros(n, np.float32), inv, rtol=c["rtol"],
+                                               atol=c["atol"], maxiter=c["maxiter"])
+        assert info == 0, name
+        tol = c.get("x_tol", 1e-4)
+        np.testing.assert_allclose(x, c["x"], rtol=tol, atol=tol)
+        if "max_iterations" in c:
+            assert its <= c["max_iterations"]
+            assert res == pytest.approx(np.linalg.norm(A @ x - b), abs=1e-4)
+
+
+def test_cg_matches_scipy(orc):
+    (d, i, p), (n, _) = wl.lap2d(12)
+    A = sp.csr_matrix((d, i, p), shape=(n, n))
+    b = wl.uniform_vector(n, 5)
+    x, info, res, its = orc.csr_cg(d, i, p, b, np.zeros(n, np.float32), rtol=1e-6, atol=0.0, maxiter=500)
+    assert info == 0 and its > 0
+    ref = np.linalg.solve(A.toarray().astype(np.float64), b.astype(np.float64))
+    np.testing.assert_allclose(x, ref, rtol=1e-4, atol=1e-4)
+    assert res == pytest.approx(np.linalg.norm(b - A @ x), rel=1e-2, abs=1e-5)
+
+
+def test_cg_status_codes(orc):
+    # maxiter exhausted -> info == maxiter; maxiter == 0 -> info == 1 (cg.cpp:150)
+    (d, i, p), (n, _) = wl.lap2d(10)
+    b = wl.uniform_vector(n, 1)
+    x0 = np.zeros(n, np.float32)
+    _, info, _, its = orc.csr_cg(d, i, p, b, x0, rtol=1e-12, atol=0.0, maxiter=3)
+    assert info == 3 and its == 3
+    _, info, _, its = orc.csr_cg(d, i, p, b, x0, rtol=1e-12, atol=0.0, maxiter=0)
+    assert info == 1 and its == 0
+    # non-finite b -> -3
+    bad = b.copy()
+    bad[3] = np.inf
+    _, info, _, _ = orc.csr_cg(d, i, p, bad, x0, rtol=1e-6, atol=0.0, maxiter=10)
+    assert info == -3
+    # indefinite preconditioner -> -2 (pcg.cpp:155-160)
+    inv = np.full(n, -0.25, np.float32)
+    _, info, _, _ = orc.csr_pcg_jacobi(d, i, p, b, x0, inv, rtol=1e-6, atol=0.0, maxiter=10)
+    assert info == -2
+
+
+@pytest.mark.parametrize("workers", [2, 3, 8])
+def test_parallel_equals_serial(orc, workers):
+    (d, i, p), (n, m) = wl.ragged_csr(3000, 400, seed=3, max_len=30, index_dtype=np.int64)
+    x = wl.uniform_vector(m, 4)
+    np.testing.assert_array_equal(orc.csr_matvec(d, i, p, x, n, workers=1),
+                                  orc.csr_matvec(d, i, p, x, n, workers=workers))
+    B = wl.uniform_matrix(m, 16, 6)
+    np.testing.assert_array_equal(orc.csr_matmul(d, i, p, B, n, workers=1),
+                                  orc.csr_matmul(d, i, p, B, n, workers=workers))
+
+
+def test_weighted_ranges_balance(orc):
+    work = np.array([1, 1, 1, 100, 1, 1, 1, 1], dtype=np.int64)
+    r = orc.weighted_ranges(work, 3)
+    assert r[0][0] == 0 and r[-1][1] == work.size
+    assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+    assert len(orc.weighted_ranges(work, 1)) == 1
+
+
+def test_workload_generators_are_canonical():
+    for (d, i, p), shape in (wl.lap2d(16), wl.poisson3d(6), wl.random_k_per_row(100, 1000, 8, 2),
+                             wl.power_law(500, 3), wl.ragged_csr(200, 100, 1, 10)):
+        assert p[0] == 0 and p[-1] == d.size == i.size
+        assert np.all(np.diff(p) >= 0)
+        for r in range(shape[0]):
+            row = i[p[r]:p[r + 1]]
+            assert np.all(np.diff(row) > 0)
+            assert row.size == 0 or (row[0] >= 0 and row[-1] < shape[1])

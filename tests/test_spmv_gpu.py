@@ -1,0 +1,142 @@
+"""SpMV parity: CUDA path (through the C ABI) vs the CPU oracle.
+
+Tolerance (fp32): per row |y - y_ref| <= 1e-5 * max(|y_ref|, sum_j |a_ij x_j|),
+the north-star's 1e-5 relative per-row bound made safe for rows that cancel;
+fp16/bf16 (fp32 accumulation): 1e-2 of the same scale.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import workloads as wl
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _csr(ms, d, i, p, shape, dtype=torch.float32):
+    return ms.csr_array((_dev(d).to(dtype), _dev(i), _dev(p)), shape=shape, canonical=True)
+
+
+def _row_scale(orc, d, i, p, x, n):
+    return np.maximum(np.abs(orc.csr_matvec(np.abs(d), i, p, np.abs(x), n, workers=8)), 1e-30)
+
+
+def _check(y, y_ref, scale, tol):
+    err = np.abs(y.astype(np.float64) - y_ref.astype(np.float64))
+    bound = tol * np.maximum(np.abs(y_ref), scale) + 1e-30
+    bad = np.nonzero(err > bound)[0]
+    assert bad.size == 0, f"{bad.size} rows out of tolerance, first {bad[:5]}, err {err[bad[:5]]}"
+
+
+@pytest.fixture(scope="module")
+def ms():
+    import mlx_sparse
+
+    assert torch.cuda.is_available()
+    return mlx_sparse
+
+
+@pytest.mark.parametrize("it", [np.int32, np.int64])
+def test_golden(ms, golden, it):
+    for name in ("spmv_hand", "spmv_scipy_456"):
+        c = golden[name]
+        A = _csr(ms, np.asarray(c["A"]["data"], np.float32), np.asarray(c["A"]["indices"], it),
+                 np.asarray(c["A"]["indptr"], it), c["A"]["shape"])
+        y = (A @ _dev(np.asarray(c["x"], np.float32))).cpu().numpy()
+        np.testing.assert_allclose(y, c["y"], rtol=1e-5, atol=1e-5)
+
+
+CASES = [
+    ("lap2d_64", lambda it: wl.lap2d(64, it)),
+    ("random_k16", lambda it: wl.random_k_per_row(3000, 2500, 16, 7, it)),
+    ("ragged_split_rows", lambda it: wl.ragged_csr(5000, 3000, 9, 40, it)),
+    ("power_law_small", lambda it: wl.power_law(20000, 3, it)),
+    ("one_long_row", lambda it: wl.ragged_csr(1, 70000, 2, 1, it, empty_frac=0.0)),
+]
+
+
+@pytest.mark.parametrize("it", [np.int32, np.int64])
+@pytest.mark.parametrize("name,make", CASES, ids=[c[0] for c in CASES])
+def test_parity_fp32(ms, orc, it, name, make):
+    (d, i, p), shape = make(it)
+    x = wl.uniform_vector(shape[1], 1)
+    y_ref = orc.csr_matvec(d, i, p, x, shape[0], workers=8)
+    A = _csr(ms, d, i, p, shape)
+    y = (A @ _dev(x)).cpu().numpy()
+    _check(y, y_ref, _row_scale(orc, d, i, p, x, shape[0]), 1e-5)
+    # no plan (stateless C-ABI call) gives identical bits
+    from mlx_sparse import _native
+
+    y2 = _native.csr_matvec(A.data, A.indices, A.indptr, _dev(x), A.shape).cpu().numpy()
+    np.testing.assert_array_equal(y, y2)
+
+
+def test_short_rows_match_reference_order_exactly(ms, orc):
+    # Rows of <= 2 thread shares are summed in the reference's order: bit-exact.
+    (d, i, p), shape = wl.lap2d(128)
+    x = wl.uniform_vector(shape[1], 0)
+    y = (_csr(ms, d, i, p, shape) @ _dev(x)).cpu().numpy()
+    y_ref = orc.csr_matvec(d, i, p, x, shape[0])
+    assert np.mean(y == y_ref) > 0.999
+
+
+def test_split_rows_present_and_deterministic(ms, orc):
+    (d, i, p), shape = wl.ragged_csr(2000, 5000, 4, 30)
+    A = _csr(ms, d, i, p, shape)
+    assert A.spmv_plan().n_split > 0
+    x = _dev(wl.uniform_vector(shape[1], 2))
+    y1 = (A @ x).cpu().numpy()
+    y2 = (A @ x).cpu().numpy()
+    np.testing.assert_array_equal(y1, y2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_half_types(ms, orc, dtype):
+    (d, i, p), shape = wl.ragged_csr(3000, 2000, 5, 25)
+    x = wl.uniform_vector(shape[1], 3)
+    A = _csr(ms, d, i, p, shape, dtype)
+    xt = _dev(x).to(dtype)
+    y = (A @ xt).float().cpu().numpy()
+    if dtype == torch.float16:
+        y_ref = orc.csr_matvec(d.astype(np.float16), i, p, x.astype(np.float16), shape[0]).astype(np.float32)
+    else:
+        y_ref = orc.bf16_bits_to_f32(orc.csr_matvec(orc.f32_to_bf16_bits(d), i, p, orc.f32_to_bf16_bits(x),
+                                                    shape[0], bf16=True))
+    _check(y, y_ref, _row_scale(orc, d, i, p, x, shape[0]), 1e-2)
+
+
+def test_edge_cases(ms):
+    # empty matrix, rows without nonzeros, nnz == 0
+    A = ms.csr_array((torch.zeros(0, device="cuda"), torch.zeros(0, dtype=torch.int32, device="cuda"),
+                      torch.zeros(1, dtype=torch.int32, device="cuda")), shape=(0, 5))
+    assert (A @ torch.ones(5, device="cuda")).shape == (0,)
+    A = ms.csr_array((torch.zeros(0, device="cuda"), torch.zeros(0, dtype=torch.int32, device="cuda"),
+                      torch.zeros(7, dtype=torch.int32, device="cuda")), shape=(6, 5))
+    y = A @ torch.ones(5, device="cuda")
+    assert torch.equal(y, torch.zeros(6, device="cuda"))
+    # leading/trailing empty rows around a single entry
+    A = ms.csr_array((torch.tensor([2.0], device="cuda"), torch.tensor([1], dtype=torch.int32, device="cuda"),
+                      torch.tensor([0, 0, 0, 1, 1, 1], dtype=torch.int32, device="cuda")), shape=(5, 3))
+    y = A @ torch.tensor([1.0, 3.0, 5.0], device="cuda")
+    assert y.cpu().tolist() == [0.0, 0.0, 6.0, 0.0, 0.0]
+
+
+def test_non_contiguous_inputs(ms):
+    (d, i, p), shape = wl.lap2d(16)
+    A = _csr(ms, d, i, p, shape)
+    x_full = torch.arange(2 * shape[1], dtype=torch.float32, device="cuda")
+    x = x_full[::2]
+    np.testing.assert_allclose((A @ x).cpu().numpy(), (A @ x.contiguous()).cpu().numpy())
+
+
+def test_full_size_lap2d(ms, orc):
+    (d, i, p), shape = wl.lap2d(1024)
+    x = wl.uniform_vector(shape[1], 0)
+    y = (_csr(ms, d, i, p, shape) @ _dev(x)).cpu().numpy()
+    y_ref = orc.csr_matvec(d, i, p, x, shape[0], workers=8)
+    _check(y, y_ref, _row_scale(orc, d, i, p, x, shape[0]), 1e-5)
