@@ -5,6 +5,7 @@
 #include <string>
 
 #include "msx_sparse.h"
+#include "cg.cuh"
 #include "ops.cuh"
 #include "spmv.cuh"
 
@@ -127,10 +128,10 @@ int msx_csr_matvec(int value_dtype, int index_dtype, const void *data, const voi
               "csr_matvec plan was built for a different matrix shape.");
       if (plan->n_split > 0) {
         Scratch carry(sizeof(float) * 2 * plan->n_tiles, s);
-        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, plan->dev, plan->n_tiles, true,
+        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, plan->dev, plan->n_tiles, true,
                  carry.as<float>(), s);
       } else {
-        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, plan->dev, plan->n_tiles, false,
+        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, plan->dev, plan->n_tiles, false,
                  nullptr, s);
       }
       return;
@@ -140,7 +141,7 @@ int msx_csr_matvec(int value_dtype, int index_dtype, const void *data, const voi
     Scratch scratch(plan_bytes + sizeof(float) * 2 * n_tiles, s);
     char *base = scratch.as<char>();
     spmv_build_plan(index_dtype, indptr, n_rows, nnz, base, n_tiles, s);
-    spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, base, n_tiles, true,
+    spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, base, n_tiles, true,
              reinterpret_cast<float *>(base + plan_bytes), s);
   });
 }
@@ -160,6 +161,115 @@ int msx_csr_matmul(int value_dtype, int index_dtype, const void *data, const voi
     check_ptr(out, n_rows * rhs_cols, "csr_matmul out");
     spmm_run(value_dtype, index_dtype, data, indices, indptr, rhs, rhs_cols, out, n_rows, n_cols,
              as_stream(stream));
+  });
+}
+
+static void check_matmat_args(int value_dtype, int lit, const void *ld, const void *li, const void *lp,
+                              int64_t lnnz, int rit, const void *rd, const void *ri, const void *rp, int64_t rnnz,
+                              int64_t m, int64_t k, int64_t rk, int64_t n, int out_it) {
+  require(m >= 0 && k >= 0 && rk >= 0 && n >= 0, MSX_ERR_INVALID, "csr_matmat shape dimensions must be non-negative.");
+  require(k == rk, MSX_ERR_INVALID, "CSR sparse-sparse matmul dimension mismatch.");
+  require(lnnz >= 0 && rnnz >= 0, MSX_ERR_INVALID, "csr_matmat nnz must be non-negative.");
+  require(n <= (int64_t)INT32_MAX, MSX_ERR_OVERFLOW, "csr_matmat n_cols exceeds supported limits.");
+  dispatch_value(value_dtype, [](auto) {});
+  dispatch_index(lit, [](auto) {});
+  dispatch_index(rit, [](auto) {});
+  dispatch_index(out_it, [](auto) {});
+  require(out_it == (lit == rit ? lit : (int)MSX_I64), MSX_ERR_TYPE,
+          "csr_matmat output index dtype must be the inputs' when they agree, else int64.");
+  check_ptr(ld, lnnz, "csr_matmat lhs_data");
+  check_ptr(li, lnnz, "csr_matmat lhs_indices");
+  check_ptr(lp, m + 1, "csr_matmat lhs_indptr");
+  check_ptr(rd, rnnz, "csr_matmat rhs_data");
+  check_ptr(ri, rnnz, "csr_matmat rhs_indices");
+  check_ptr(rp, rk + 1, "csr_matmat rhs_indptr");
+}
+
+int msx_csr_matmat_symbolic(int value_dtype, int lhs_index_dtype, const void *lhs_data, const void *lhs_indices,
+                            const void *lhs_indptr, int64_t lhs_nnz, int rhs_index_dtype, const void *rhs_data,
+                            const void *rhs_indices, const void *rhs_indptr, int64_t rhs_nnz, int64_t lhs_n_rows,
+                            int64_t lhs_n_cols, int64_t rhs_n_rows, int64_t rhs_n_cols, int out_index_dtype,
+                            void *out_indptr, int64_t *out_nnz, int prune_zeros, void *stream) {
+  return guarded([&] {
+    check_matmat_args(value_dtype, lhs_index_dtype, lhs_data, lhs_indices, lhs_indptr, lhs_nnz, rhs_index_dtype,
+                      rhs_data, rhs_indices, rhs_indptr, rhs_nnz, lhs_n_rows, lhs_n_cols, rhs_n_rows, rhs_n_cols,
+                      out_index_dtype);
+    require(out_nnz != nullptr, MSX_ERR_INVALID, "csr_matmat out_nnz must not be null.");
+    check_ptr(out_indptr, lhs_n_rows + 1, "csr_matmat out_indptr");
+    spgemm_run(false, value_dtype, lhs_index_dtype, lhs_data, lhs_indices, lhs_indptr, rhs_index_dtype, rhs_data,
+               rhs_indices, rhs_indptr, lhs_n_rows, rhs_n_rows, rhs_n_cols, out_index_dtype, out_indptr, nullptr,
+               nullptr, out_nnz, prune_zeros != 0, as_stream(stream));
+  });
+}
+
+int msx_csr_matmat_numeric(int value_dtype, int lhs_index_dtype, const void *lhs_data, const void *lhs_indices,
+                           const void *lhs_indptr, int64_t lhs_nnz, int rhs_index_dtype, const void *rhs_data,
+                           const void *rhs_indices, const void *rhs_indptr, int64_t rhs_nnz, int64_t lhs_n_rows,
+                           int64_t lhs_n_cols, int64_t rhs_n_rows, int64_t rhs_n_cols, int out_index_dtype,
+                           const void *out_indptr, int64_t out_nnz, void *out_data, void *out_indices,
+                           int prune_zeros, void *stream) {
+  return guarded([&] {
+    check_matmat_args(value_dtype, lhs_index_dtype, lhs_data, lhs_indices, lhs_indptr, lhs_nnz, rhs_index_dtype,
+                      rhs_data, rhs_indices, rhs_indptr, rhs_nnz, lhs_n_rows, lhs_n_cols, rhs_n_rows, rhs_n_cols,
+                      out_index_dtype);
+    require(out_nnz >= 0, MSX_ERR_INVALID, "csr_matmat out_nnz must be non-negative.");
+    check_ptr(out_indptr, lhs_n_rows + 1, "csr_matmat out_indptr");
+    check_ptr(out_data, out_nnz, "csr_matmat out_data");
+    check_ptr(out_indices, out_nnz, "csr_matmat out_indices");
+    int64_t unused = 0;
+    spgemm_run(true, value_dtype, lhs_index_dtype, lhs_data, lhs_indices, lhs_indptr, rhs_index_dtype, rhs_data,
+               rhs_indices, rhs_indptr, lhs_n_rows, rhs_n_rows, rhs_n_cols, out_index_dtype,
+               const_cast<void *>(out_indptr), out_indices, out_data, &unused, prune_zeros != 0, as_stream(stream));
+  });
+}
+
+static void check_solver_args(const char *op, int index_dtype, const float *data, const void *indices,
+                              const void *indptr, int64_t nnz, const float *b, const float *x0, float *x_out,
+                              int64_t n_rows, int64_t n_cols, int32_t maxiter, int32_t *info, float *residual,
+                              int32_t *iterations) {
+  const std::string o(op);
+  require(n_rows > 0 && n_cols > 0 && n_rows == n_cols, MSX_ERR_INVALID, o + " requires a non-empty square matrix.");
+  require(maxiter >= 0, MSX_ERR_INVALID, o + " maxiter must be non-negative.");
+  require(nnz >= 0, MSX_ERR_INVALID, o + " data and indices must have equal length.");
+  dispatch_index(index_dtype, [](auto) {});
+  check_ptr(data, nnz, (o + " data").c_str());
+  check_ptr(indices, nnz, (o + " indices").c_str());
+  check_ptr(indptr, n_rows + 1, (o + " indptr").c_str());
+  check_ptr(b, n_rows, (o + " b").c_str());
+  check_ptr(x0, n_cols, (o + " x0").c_str());
+  check_ptr(x_out, n_rows, (o + " x").c_str());
+  require(info && residual && iterations, MSX_ERR_INVALID, o + " result pointers must not be null.");
+}
+
+int msx_csr_cg(int index_dtype, const float *data, const void *indices, const void *indptr, int64_t nnz,
+               const float *b, const float *x0, float *x_out, int64_t n_rows, int64_t n_cols, float rtol, float atol,
+               int32_t maxiter, int32_t *info, float *residual, int32_t *iterations, void *stream) {
+  return guarded([&] {
+    check_solver_args("csr_cg", index_dtype, data, indices, indptr, nnz, b, x0, x_out, n_rows, n_cols, maxiter,
+                      info, residual, iterations);
+    CgProblem prob{index_dtype, data, indices, indptr, nnz, n_rows, n_cols, b, x0, nullptr, x_out, rtol, atol,
+                   maxiter};
+    CgResult r = cg_solve(prob, as_stream(stream));
+    *info = r.info;
+    *residual = r.residual;
+    *iterations = r.iterations;
+  });
+}
+
+int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *indices, const void *indptr, int64_t nnz,
+                       const float *b, const float *x0, const float *inv_diag, float *x_out, int64_t n_rows,
+                       int64_t n_cols, float rtol, float atol, int32_t maxiter, int32_t *info, float *residual,
+                       int32_t *iterations, void *stream) {
+  return guarded([&] {
+    check_solver_args("csr_pcg_jacobi", index_dtype, data, indices, indptr, nnz, b, x0, x_out, n_rows, n_cols,
+                      maxiter, info, residual, iterations);
+    check_ptr(inv_diag, n_rows, "csr_pcg_jacobi inv_diag");
+    CgProblem prob{index_dtype, data, indices, indptr, nnz, n_rows, n_cols, b, x0, inv_diag, x_out, rtol, atol,
+                   maxiter};
+    CgResult r = cg_solve(prob, as_stream(stream));
+    *info = r.info;
+    *residual = r.residual;
+    *iterations = r.iterations;
   });
 }
 

@@ -1,0 +1,56 @@
+// Conjugate-gradient solvers (plain CG and Jacobi PCG) on the device.
+#pragma once
+#include "common.cuh"
+
+namespace msx {
+
+constexpr int kStatusRunning = -2147483647 - 1;  // INT_MIN: loop still running
+
+// Device-resident solver state. Scalars never leave the GPU during the solve;
+// the host reads `status` once per batch of iterations.
+struct CgState {
+  double red[4];      // reduction results of the latest reduction kernel
+  double rr;          // plain CG: current r.r (double, cg.cpp:123-131)
+  double rr_pending;  // plain CG: r.r of the candidate update
+  double alpha_d;     // plain CG: step (double)
+  double beta_d;      // plain CG: direction update (double)
+  float tol;          // max(atol, rtol * ||b||)
+  float rho;          // PCG: r.z (float, pcg.cpp:136)
+  float alpha_f;      // PCG: step (float)
+  float beta_f;       // PCG: direction update (float)
+  float true_rr;      // PCG: float(r.r) of the last update
+  float residual;     // final residual norm reported to the caller
+  int status;         // kStatusRunning, or the final info code
+  int completed;      // iterations completed
+  int it;             // index of the iteration being run (1-based)
+  int maxiter;
+  unsigned int counter;  // last-block-done counter of the reductions
+  int pad[3];
+};
+
+struct CgProblem {
+  int index_dtype;
+  const float *data;
+  const void *indices;
+  const void *indptr;
+  int64_t nnz;
+  int64_t n;          // rows owned by this rank (== n_cols on one GPU)
+  int64_t n_cols;     // columns of the local matrix (owned + halo)
+  const float *b;
+  const float *x0;
+  const float *inv_diag;  // null for plain CG
+  float *x;
+  float rtol, atol;
+  int maxiter;
+};
+
+struct CgResult {
+  int info;
+  float residual;
+  int iterations;
+};
+
+// Single-GPU solve on `stream`; synchronises the stream at the end.
+CgResult cg_solve(const CgProblem &prob, cudaStream_t stream);
+
+}  // namespace msx

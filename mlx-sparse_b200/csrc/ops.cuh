@@ -7,4 +7,9 @@ namespace msx {
 void spmm_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
               const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, cudaStream_t stream);
 
+void spgemm_run(bool write, int value_dtype, int lhs_it, const void *ld, const void *li, const void *lp, int rhs_it,
+                const void *rd, const void *ri, const void *rp, int64_t m, int64_t rhs_rows, int64_t n_cols,
+                int out_it, void *out_indptr, void *out_idx, void *out_data, int64_t *out_nnz, bool prune,
+                cudaStream_t s);
+
 }  // namespace msx

@@ -116,42 +116,50 @@ void spmv_build_plan(int index_dtype, const void *indptr, int64_t n_rows, int64_
   MSX_CHECK_LAUNCH();
 }
 
-int spmv_grid(int64_t n_tiles) {
-  static thread_local int cached_dev = -1, cached_per_sm = 0, cached_sms = 0;
+namespace {
+__device__ int g_spmv_error;
+}
+
+int *spmv_error_flag() {
+  static thread_local int cached_dev = -1;
+  static thread_local int *ptr = nullptr;
   int dev = 0;
   MSX_CUDA(cudaGetDevice(&dev));
   if (dev != cached_dev) {
-    int per_sm = 0;
-    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, spmv_tiles_kernel<float, int32_t, NoEpilogue>, kSpmvThreads, 0));
-    cached_per_sm = per_sm > 0 ? per_sm : 1;
-    cached_sms = num_sms();
+    MSX_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_spmv_error));
     cached_dev = dev;
   }
-  const int64_t g = (int64_t)cached_per_sm * cached_sms;
-  return (int)(n_tiles < g ? n_tiles : g);
+  return ptr;
 }
 
+bool spmv_tma_ok(const void *data, const void *indices, const void *indptr) {
+  static const bool disabled = [] {
+    const char *e = getenv("MSX_SPMV_NO_TMA");
+    return e && *e && *e != '0';
+  }();
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return !disabled && al(data) && al(indices) && al(indptr);
+}
+
+int spmv_grid(int64_t n_tiles) { return spmv_grid_for<float, int32_t, NoEpilogue>(n_tiles, true); }
+
 void spmv_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
-              const void *x, void *y, int64_t n_rows, const void *plan_dev, int64_t n_tiles, bool launch_fixup,
-              float *carry_scratch, cudaStream_t stream) {
-  (void)n_rows;
+              const void *x, void *y, int64_t n_rows, int64_t nnz, const void *plan_dev, int64_t n_tiles,
+              bool launch_fixup, float *carry_scratch, cudaStream_t stream) {
   if (n_tiles == 0) return;
   int64_t *tile_row, *tile_nz;
   unsigned long long *n_split;
   spmv_plan_layout(const_cast<void *>(plan_dev), n_tiles, &tile_row, &tile_nz, &n_split);
   float *carry_head = carry_scratch;
   float *carry_tail = carry_scratch ? carry_scratch + n_tiles : nullptr;
-  const int grid = spmv_grid(n_tiles);
   dispatch_value(value_dtype, [&](auto vtyp) {
     using T = decltype(vtyp);
     dispatch_index(index_dtype, [&](auto ityp) {
       using I = decltype(ityp);
-      spmv_tiles_kernel<T, I, NoEpilogue><<<grid, kSpmvThreads, 0, stream>>>(
-          static_cast<const T *>(data), static_cast<const I *>(indices), static_cast<const I *>(indptr),
-          static_cast<const T *>(x), static_cast<T *>(y), tile_row, tile_nz, carry_head, carry_tail, n_tiles,
-          NoEpilogue{});
-      MSX_CHECK_LAUNCH();
+      launch_spmv_tiles<T, I, NoEpilogue>(static_cast<const T *>(data), static_cast<const I *>(indices),
+                                          static_cast<const I *>(indptr), static_cast<const T *>(x),
+                                          static_cast<T *>(y), tile_row, tile_nz, carry_head, carry_tail, n_tiles,
+                                          nnz, n_rows, NoEpilogue{}, stream);
       if (launch_fixup) {
         const int threads = 256;
         spmv_fixup_kernel<T, I><<<(unsigned)ceil_div(n_tiles, threads), threads, 0, stream>>>(

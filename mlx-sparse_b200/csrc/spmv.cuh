@@ -5,6 +5,15 @@
 // with nonzeros) of about kTileItems items. Tile boundaries are snapped back to
 // row starts unless the row is longer than kSplitRowLen, so short rows are
 // always finished inside one tile. See spmv.cu for the algorithm.
+//
+// Two staging variants feed the same tile walk:
+//  - TMA pipeline (default): a persistent CTA keeps two shared-memory stages;
+//    while it computes tile j, one elected thread has already issued bulk
+//    asynchronous copies (cp.async.bulk, completion on an mbarrier) of tile
+//    j+1's column indices, values and row offsets. Requires 16-byte aligned
+//    array bases.
+//  - direct: coalesced streaming loads into registers, used when a base
+//    pointer is not 16-byte aligned.
 #pragma once
 #include "common.cuh"
 
@@ -12,12 +21,18 @@ namespace msx {
 
 constexpr int kSpmvThreads = 256;
 // Path items (rows + nonzeros) per tile before snapping to row starts.
-constexpr int kTileItems = 1536;
+constexpr int kTileItems = 1280;
 // Rows longer than this are split between tiles; shorter rows never are.
-constexpr int kSplitRowLen = kTileItems / 2;
-// Upper bound on a tile's path length after snapping.
+constexpr int kSplitRowLen = 256;
+// Upper bound on a tile's path length after snapping (and so on its nonzeros
+// and on its rows).
 constexpr int kMaxTileItems = kTileItems + kSplitRowLen;
+constexpr int kPerThread = kMaxTileItems / kSpmvThreads;
 static_assert(kMaxTileItems % kSpmvThreads == 0, "tile staging assumes whole rounds");
+
+// Bound on mbarrier polling (a safety net; a bulk copy of valid memory
+// completes in microseconds).
+constexpr long long kMaxPolls = 1ll << 22;
 
 struct SegPair {
   int flag;  // 1 if the segment contains a row end (resets the running sum)
@@ -68,7 +83,6 @@ __device__ __forceinline__ SegPair block_exclusive_seg_scan(SegPair v, SegPair *
   } else {
     ex = warp > 0 ? seg_combine(warp_tot[warp - 1], prev_lanes) : prev_lanes;
   }
-  __syncthreads();  // warp_tot is reused by the next tile
   return ex;
 }
 
@@ -92,56 +106,40 @@ struct TileSmem {
   SegPair warp_tot[kSpmvThreads / 32];
 };
 
-// Epilogue that only stores y.
+// Epilogue that only stores y. Epilogues see every finished row (`row`), may
+// skip the whole launch (`skip`, evaluated by every thread at entry) and run a
+// block-wide `finish` after the CTA's last tile.
 struct NoEpilogue {
+  __device__ __forceinline__ bool skip() const { return false; }
   __device__ __forceinline__ void row(int64_t, float) {}
+  __device__ __forceinline__ void finish() {}
 };
 
-// Processes tile t: y[r] for every row finished in the tile, tile partials of
-// split rows into carry_head / carry_tail. Must be called by all kSpmvThreads.
+struct TileBounds {
+  int64_t r0, r1, k0, k1;
+  int R, K;
+};
+
+__device__ __forceinline__ TileBounds tile_bounds(int64_t t, const int64_t *tile_row, const int64_t *tile_nz) {
+  TileBounds b;
+  b.r0 = __ldg(tile_row + t);
+  b.r1 = __ldg(tile_row + t + 1);
+  b.k0 = __ldg(tile_nz + t);
+  b.k1 = __ldg(tile_nz + t + 1);
+  b.R = (int)(b.r1 - b.r0);
+  b.K = (int)(b.k1 - b.k0);
+  return b;
+}
+
+// Walks the staged tile (sm.prod[0..K), sm.row_end[0..R)) and writes rows.
 template <typename T, typename I, typename Epi>
-__device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict__ data, const I *__restrict__ indices,
-                                                  const I *__restrict__ indptr, const T *__restrict__ x,
-                                                  T *__restrict__ y, const int64_t *__restrict__ tile_row,
-                                                  const int64_t *__restrict__ tile_nz, float *__restrict__ carry_head,
-                                                  float *__restrict__ carry_tail, TileSmem &sm, Epi &epi) {
-  const int64_t r0 = tile_row[t], r1 = tile_row[t + 1];
-  const int64_t k0 = tile_nz[t], k1 = tile_nz[t + 1];
-  const int R = (int)(r1 - r0);  // rows whose end lies in this tile
-  const int K = (int)(k1 - k0);  // nonzeros in this tile
-  const int P = R + K;
+__device__ __forceinline__ void tile_walk(int64_t t, const TileBounds &tb, const I *__restrict__ indptr,
+                                          T *__restrict__ y, float *__restrict__ carry_head,
+                                          float *__restrict__ carry_tail, TileSmem &sm, Epi &epi) {
+  const int R = tb.R, K = tb.K, P = R + K;
   const int tid = threadIdx.x;
-  const int64_t head_start = (int64_t)__ldg(indptr + r0);
-  const int64_t tail_start = (int64_t)__ldg(indptr + r1);
-
-  // Stage products and row ends: every load of the tile is issued before any
-  // is consumed.
-  {
-    constexpr int kPer = kMaxTileItems / kSpmvThreads;
-    I col[kPer];
-    T val[kPer];
-#pragma unroll
-    for (int s = 0; s < kPer; ++s) {
-      const int k = tid + s * kSpmvThreads;
-      if (k < K) {
-        col[s] = ld_stream(indices + k0 + k);
-        val[s] = ld_stream(data + k0 + k);
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < kPer; ++s) {
-      const int k = tid + s * kSpmvThreads;
-      if (k < K) sm.prod[k] = mul_rn(VT<T>::load(val[s]), VT<T>::load(__ldg(x + col[s])));
-    }
-#pragma unroll
-    for (int s = 0; s < kPer; ++s) {
-      const int i = tid + s * kSpmvThreads;
-      if (i < R) sm.row_end[i] = (int)((int64_t)__ldg(indptr + r0 + i + 1) - k0);
-    }
-  }
-  __syncthreads();
-
-  const bool head_partial = (R > 0) && (k0 > head_start);
+  const bool head_partial = (R > 0) && (tb.k0 > (int64_t)__ldg(indptr + tb.r0));
+  const bool tail_partial = tb.k1 > (int64_t)__ldg(indptr + tb.r1);
   const int ipt = (P + kSpmvThreads - 1) / kSpmvThreads;
   const int d0 = min(tid * ipt, P);
   const int d1 = min(d0 + ipt, P);
@@ -167,7 +165,8 @@ __device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict
   }
   const SegPair carry = block_exclusive_seg_scan(mine, sm.warp_tot);
 
-  // Pass 2: re-walk from the carried-in partial and write the rows.
+  // Pass 2: re-walk from the carried-in partial and write the rows. A row
+  // spanning two threads is thereby summed strictly left to right.
   {
     int i = i0, j = j0;
     float acc = carry.val;
@@ -177,8 +176,8 @@ __device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict
           carry_head[t] = acc;
         } else {
           const T out = VT<T>::store(acc);
-          y[r0 + i] = out;
-          epi.row(r0 + i, VT<T>::load(out));
+          y[tb.r0 + i] = out;
+          epi.row(tb.r0 + i, VT<T>::load(out));
         }
         acc = 0.f;
         ++i;
@@ -189,8 +188,43 @@ __device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict
     }
     // The thread holding the last path item owns the tile's tail partial when
     // the tile ends inside a (split) row.
-    if (d0 < d1 && d1 == P && k1 > tail_start) carry_tail[t] = acc;
+    if (d0 < d1 && d1 == P && tail_partial) carry_tail[t] = acc;
   }
+}
+
+// ---- direct staging ----------------------------------------------------------
+template <typename T, typename I, typename Epi>
+__device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict__ data, const I *__restrict__ indices,
+                                                  const I *__restrict__ indptr, const T *__restrict__ x,
+                                                  T *__restrict__ y, const int64_t *__restrict__ tile_row,
+                                                  const int64_t *__restrict__ tile_nz, float *__restrict__ carry_head,
+                                                  float *__restrict__ carry_tail, TileSmem &sm, Epi &epi) {
+  const TileBounds tb = tile_bounds(t, tile_row, tile_nz);
+  const int tid = threadIdx.x;
+  {
+    I col[kPerThread];
+    T val[kPerThread];
+#pragma unroll
+    for (int s = 0; s < kPerThread; ++s) {
+      const int k = tid + s * kSpmvThreads;
+      if (k < tb.K) {
+        col[s] = ld_stream(indices + tb.k0 + k);
+        val[s] = ld_stream(data + tb.k0 + k);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < kPerThread; ++s) {
+      const int k = tid + s * kSpmvThreads;
+      if (k < tb.K) sm.prod[k] = mul_rn(VT<T>::load(val[s]), VT<T>::load(__ldg(x + col[s])));
+    }
+#pragma unroll
+    for (int s = 0; s < kPerThread; ++s) {
+      const int i = tid + s * kSpmvThreads;
+      if (i < tb.R) sm.row_end[i] = (int)((int64_t)__ldg(indptr + tb.r0 + i + 1) - tb.k0);
+    }
+  }
+  __syncthreads();
+  tile_walk<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm, epi);
   __syncthreads();  // smem reused by the next tile
 }
 
@@ -201,9 +235,190 @@ spmv_tiles_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
                   const int64_t *__restrict__ tile_nz, float *__restrict__ carry_head, float *__restrict__ carry_tail,
                   int64_t n_tiles, Epi epi) {
   __shared__ TileSmem sm;
+  if (epi.skip()) return;
   for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
     spmv_process_tile<T, I, Epi>(t, data, indices, indptr, x, y, tile_row, tile_nz, carry_head, carry_tail, sm, epi);
   }
+  epi.finish();
+}
+
+// ---- TMA bulk-copy pipeline ------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Global -> shared bulk copy (no multicast); completion counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// A 16-byte aligned byte window [lo, hi) of an array that covers elements
+// [e0, e1) as far as the array's end allows; elements past `covered` are read
+// from global memory instead.
+struct BulkWindow {
+  uint64_t lo;      // byte offset (from the array base) of the first copied byte
+  uint32_t bytes;   // multiple of 16
+  uint32_t skew;    // byte offset of element e0 inside the window
+  int64_t covered;  // first element index not in the window
+};
+
+__device__ __forceinline__ BulkWindow bulk_window(int64_t e0, int64_t e1, int elem, int64_t total_elems) {
+  BulkWindow w;
+  const uint64_t b0 = (uint64_t)e0 * elem, b1 = (uint64_t)e1 * elem;
+  const uint64_t total = (uint64_t)total_elems * elem;
+  w.lo = b0 & ~uint64_t(15);
+  uint64_t hi = (b1 + 15) & ~uint64_t(15);
+  if (hi > total) hi = total & ~uint64_t(15);
+  if (hi < w.lo) hi = w.lo;
+  w.bytes = (uint32_t)(hi - w.lo);
+  w.skew = (uint32_t)(b0 - w.lo);
+  const int64_t cov = (int64_t)(hi / elem);
+  w.covered = cov < e1 ? cov : e1;
+  if (w.covered < e0) w.covered = e0;
+  return w;
+}
+
+template <typename T, typename I>
+struct TmaStage {
+  // slack of 16 bytes for the alignment skew of the window start
+  alignas(16) unsigned char idx[kMaxTileItems * sizeof(I) + 32];
+  alignas(16) unsigned char val[kMaxTileItems * sizeof(T) + 32];
+  alignas(16) unsigned char ptr[kMaxTileItems * sizeof(I) + 32];
+};
+
+template <typename T, typename I>
+struct TmaSmem {
+  TmaStage<T, I> stage[2];
+  TileSmem tile;
+  alignas(8) uint64_t bar[2];
+};
+
+template <typename T, typename I>
+__device__ __forceinline__ void tma_issue(int64_t t, TmaStage<T, I> &st, uint64_t *bar, const T *data,
+                                          const I *indices, const I *indptr, int64_t nnz, int64_t n_rows,
+                                          const int64_t *tile_row, const int64_t *tile_nz) {
+  const TileBounds tb = tile_bounds(t, tile_row, tile_nz);
+  const BulkWindow wi = bulk_window(tb.k0, tb.k1, sizeof(I), nnz);
+  const BulkWindow wv = bulk_window(tb.k0, tb.k1, sizeof(T), nnz);
+  const BulkWindow wp = bulk_window(tb.r0 + 1, tb.r1 + 1, sizeof(I), n_rows + 1);
+  const uint32_t total = wi.bytes + wv.bytes + wp.bytes;
+  mbar_arrive_expect_tx(bar, total);
+  const char *bi = reinterpret_cast<const char *>(indices);
+  const char *bv = reinterpret_cast<const char *>(data);
+  const char *bp = reinterpret_cast<const char *>(indptr);
+  if (wi.bytes) bulk_g2s(st.idx, bi + wi.lo, wi.bytes, bar);
+  if (wv.bytes) bulk_g2s(st.val, bv + wv.lo, wv.bytes, bar);
+  if (wp.bytes) bulk_g2s(st.ptr, bp + wp.lo, wp.bytes, bar);
+}
+
+// Persistent CTA over tiles blockIdx.x, +gridDim.x, ... with a two-stage TMA
+// pipeline. `err` receives 1 if an mbarrier wait ever exceeds kMaxPolls.
+template <typename T, typename I, typename Epi>
+__global__ void __launch_bounds__(kSpmvThreads)
+spmv_tiles_tma_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                      const T *__restrict__ x, T *__restrict__ y, const int64_t *__restrict__ tile_row,
+                      const int64_t *__restrict__ tile_nz, float *__restrict__ carry_head,
+                      float *__restrict__ carry_tail, int64_t n_tiles, int64_t nnz, int64_t n_rows, Epi epi,
+                      int *__restrict__ err) {
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  TmaSmem<T, I> &sm = *reinterpret_cast<TmaSmem<T, I> *>(dyn_smem);
+  const int tid = threadIdx.x;
+  int64_t t = blockIdx.x;
+  if (t >= n_tiles || epi.skip()) return;
+  if (tid == 0) {
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_issue<T, I>(t, sm.stage[0], &sm.bar[0], data, indices, indptr, nnz, n_rows, tile_row, tile_nz);
+  }
+  __syncthreads();
+  uint32_t phase[2] = {0u, 0u};
+  for (int j = 0; t < n_tiles; ++j, t += gridDim.x) {
+    const int s = j & 1;
+    const int64_t t_next = t + gridDim.x;
+    if (tid == 0 && t_next < n_tiles) {
+      fence_proxy_async_smem();  // generic reads of the other stage precede its refill
+      tma_issue<T, I>(t_next, sm.stage[s ^ 1], &sm.bar[s ^ 1], data, indices, indptr, nnz, n_rows, tile_row,
+                      tile_nz);
+    }
+    long long polls = 0;
+    while (!mbar_try_wait(&sm.bar[s], phase[s])) {
+      if (++polls > kMaxPolls) {
+        if (tid == 0) atomicOr(err, 1);
+        return;
+      }
+    }
+    phase[s] ^= 1u;
+
+    const TileBounds tb = tile_bounds(t, tile_row, tile_nz);
+    const BulkWindow wi = bulk_window(tb.k0, tb.k1, sizeof(I), nnz);
+    const BulkWindow wv = bulk_window(tb.k0, tb.k1, sizeof(T), nnz);
+    const BulkWindow wp = bulk_window(tb.r0 + 1, tb.r1 + 1, sizeof(I), n_rows + 1);
+    const I *sidx = reinterpret_cast<const I *>(sm.stage[s].idx + wi.skew);
+    const T *sval = reinterpret_cast<const T *>(sm.stage[s].val + wv.skew);
+    const I *sptr = reinterpret_cast<const I *>(sm.stage[s].ptr + wp.skew);
+    const int cov_i = (int)(wi.covered - tb.k0), cov_v = (int)(wv.covered - tb.k0);
+    const int cov_p = (int)(wp.covered - (tb.r0 + 1));
+    {
+      I col[kPerThread];
+      T val[kPerThread];
+#pragma unroll
+      for (int q = 0; q < kPerThread; ++q) {
+        const int k = tid + q * kSpmvThreads;
+        if (k < tb.K) {
+          col[q] = k < cov_i ? sidx[k] : indices[tb.k0 + k];
+          val[q] = k < cov_v ? sval[k] : data[tb.k0 + k];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kPerThread; ++q) {
+        const int k = tid + q * kSpmvThreads;
+        if (k < tb.K) sm.tile.prod[k] = mul_rn(VT<T>::load(val[q]), VT<T>::load(__ldg(x + col[q])));
+      }
+#pragma unroll
+      for (int q = 0; q < kPerThread; ++q) {
+        const int i = tid + q * kSpmvThreads;
+        if (i < tb.R) {
+          const int64_t e = i < cov_p ? (int64_t)sptr[i] : (int64_t)indptr[tb.r0 + 1 + i];
+          sm.tile.row_end[i] = (int)(e - tb.k0);
+        }
+      }
+    }
+    __syncthreads();
+    tile_walk<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm.tile, epi);
+    __syncthreads();  // stage s and the tile arrays are free again
+  }
+  epi.finish();
+}
+
+template <typename T, typename I>
+constexpr size_t tma_smem_bytes() {
+  return sizeof(TmaSmem<T, I>);
 }
 
 int64_t spmv_num_tiles(int64_t n_rows, int64_t nnz);
@@ -212,14 +427,63 @@ void spmv_plan_layout(void *base, int64_t n_tiles, int64_t **tile_row, int64_t *
                       unsigned long long **n_split);
 void spmv_build_plan(int index_dtype, const void *indptr, int64_t n_rows, int64_t nnz, void *plan_dev,
                      int64_t n_tiles, cudaStream_t stream);
-// Persistent grid size for the tile kernel on the current device.
+// True when the TMA pipeline can be used for these base pointers.
+bool spmv_tma_ok(const void *data, const void *indices, const void *indptr);
+// Persistent grid size for the tile kernels on the current device.
+template <typename T, typename I, typename Epi>
+int spmv_grid_for(int64_t n_tiles, bool tma);
 int spmv_grid(int64_t n_tiles);
+// Device int the TMA kernels flag when an mbarrier wait times out (per device).
+int *spmv_error_flag();
 // carry_scratch: float[2*n_tiles] when launch_fixup, else may be null.
 void spmv_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
-              const void *x, void *y, int64_t n_rows, const void *plan_dev, int64_t n_tiles, bool launch_fixup,
-              float *carry_scratch, cudaStream_t stream);
+              const void *x, void *y, int64_t n_rows, int64_t nnz, const void *plan_dev, int64_t n_tiles,
+              bool launch_fixup, float *carry_scratch, cudaStream_t stream);
 // Fixup of split rows for fp32 y (used by the solvers).
 void spmv_fixup_f32(int index_dtype, const void *indptr, float *y, const void *plan_dev, int64_t n_tiles,
                     const float *carry_scratch, cudaStream_t stream);
+
+// Launches the tile kernel (TMA pipeline when the pointers allow) with an
+// epilogue; shared by spmv.cu and cg.cu.
+template <typename T, typename I, typename Epi>
+void launch_spmv_tiles(const T *data, const I *indices, const I *indptr, const T *x, T *y, const int64_t *tile_row,
+                       const int64_t *tile_nz, float *carry_head, float *carry_tail, int64_t n_tiles, int64_t nnz,
+                       int64_t n_rows, Epi epi, cudaStream_t stream) {
+  if (n_tiles == 0) return;
+  const bool tma = spmv_tma_ok(data, indices, indptr);
+  const int grid = spmv_grid_for<T, I, Epi>(n_tiles, tma);
+  if (tma) {
+    spmv_tiles_tma_kernel<T, I, Epi><<<grid, kSpmvThreads, tma_smem_bytes<T, I>(), stream>>>(
+        data, indices, indptr, x, y, tile_row, tile_nz, carry_head, carry_tail, n_tiles, nnz, n_rows, epi,
+        spmv_error_flag());
+  } else {
+    spmv_tiles_kernel<T, I, Epi><<<grid, kSpmvThreads, 0, stream>>>(data, indices, indptr, x, y, tile_row, tile_nz,
+                                                                    carry_head, carry_tail, n_tiles, epi);
+  }
+  MSX_CHECK_LAUNCH();
+}
+
+template <typename T, typename I, typename Epi>
+int spmv_grid_for(int64_t n_tiles, bool tma) {
+  static thread_local int cached_dev[2] = {-1, -1}, per_sm[2] = {0, 0}, sms = 0;
+  int dev = 0;
+  MSX_CUDA(cudaGetDevice(&dev));
+  const int v = tma ? 1 : 0;
+  if (dev != cached_dev[v]) {
+    int occ = 0;
+    if (tma) {
+      auto kern = spmv_tiles_tma_kernel<T, I, Epi>;
+      MSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tma_smem_bytes<T, I>()));
+      MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSpmvThreads, tma_smem_bytes<T, I>()));
+    } else {
+      MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_tiles_kernel<T, I, Epi>, kSpmvThreads, 0));
+    }
+    per_sm[v] = occ > 0 ? occ : 1;
+    sms = num_sms();
+    cached_dev[v] = dev;
+  }
+  const int64_t g = (int64_t)per_sm[v] * sms;
+  return (int)(n_tiles < g ? n_tiles : g);
+}
 
 }  // namespace msx
