@@ -267,7 +267,7 @@ class SpmvWorkload(Workload):
         self.h_x = torch.from_numpy(x).pin_memory()
         self.h_y = torch.empty(self.rows, dtype=torch.float32).pin_memory()
         self.dev = device
-        self.launches_per_step = 1 + (1 if self.plan.n_split > 0 else 0)
+        self.launches_per_step = 1 + (1 if self.plan.n_long > 0 else 0)
         self.h2d_bytes = d.nbytes + i.nbytes + p.nbytes + x.nbytes
         self.d2h_bytes = self.rows * 4
         self.local_bytes = d.size * (4 + ib) + ib * (self.rows + 1) + 4 * self.n + 4 * self.rows
@@ -326,6 +326,9 @@ def _measure(wk, steps, warmup, device):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for s in range(steps):
         flush.fill_(s & 0xFF)
+        # keep the GPU busy while the host enqueues the step, so host-side
+        # call overhead never shows up between the events
+        torch.cuda._sleep(200000)
         starts[s].record(stream)
         wk.step()
         ends[s].record(stream)

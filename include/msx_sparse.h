@@ -55,30 +55,31 @@ MSX_API int msx_version(void);
 MSX_API int msx_compiled_sm(void);
 
 /* ------------------------------------------------------------------------ */
-/* SpMV plan: nnz-balanced merge-path tile partition of a CSR matrix.        */
+/* SpMV plan: row-length bins of a CSR matrix.                              */
 /* ------------------------------------------------------------------------ */
-/* A plan caches the row-aligned, nnz-balanced tile partition that the SpMV
- * kernel walks, so repeated products with one matrix skip the partition
- * search. It depends only on `indptr`. The reference has no counterpart: its
- * CPU path recomputes nnz-weighted worker ranges on every call
- * (src/common/cpu_parallel.cpp:202-253, reached from
+/* A plan sorts the row ids once per matrix into bins by row length (1, 2, 4,
+ * ... 32 lanes per row, a CTA per row, or 8192-nonzero chunks of one row), so
+ * every product runs one balanced launch. It depends only on `indptr`. The
+ * reference has no counterpart: its CPU path recomputes nnz-weighted worker
+ * ranges on every call (src/common/cpu_parallel.cpp:202-253, reached from
  * src/sparse/csr_matvec/csr_matvec.cpp:156-166).
  * msx_spmv_plan_create allocates device memory (cudaMalloc) and synchronises
- * `stream` once; the plan is immutable afterwards and may be shared by
- * concurrent calls on any stream of the same device. */
+ * `stream`; the plan is immutable afterwards and may be shared by concurrent
+ * calls on any stream of the same device. */
 typedef struct msx_spmv_plan msx_spmv_plan;
 MSX_API int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows,
                          int64_t nnz, void *stream, msx_spmv_plan **out);
 MSX_API int msx_spmv_plan_destroy(msx_spmv_plan *plan);
-/* Number of tiles and of tile boundaries that fall inside a (long) row. */
-MSX_API int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_tiles,
-                       int64_t *n_split_boundaries);
+/* Blocks of one product launch, and rows split into several chunks. */
+MSX_API int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_blocks,
+                       int64_t *n_long_rows);
 
 /* y = A @ x. Replaces `csr_matvec(data, indices, indptr, x, n_rows, n_cols)`
  * (src/bindings.cpp:874-883 -> src/sparse/csr_matvec/csr_matvec.cpp:326-356,
- * CPU loop :79-168). `plan` may be NULL: the partition is then built in
- * stream-ordered scratch on every call. A plan must have been created for this
- * matrix's indptr, n_rows and nnz. fp16/bf16 accumulate in fp32. */
+ * CPU loop :79-168). With a plan the binned kernel runs; `plan` may be NULL,
+ * in which case an nnz-balanced merge-path partition is built in stream-ordered
+ * scratch on every call. A plan must have been created for this matrix's
+ * indptr, n_rows and nnz. fp16/bf16 accumulate in fp32. */
 MSX_API int msx_csr_matvec(int value_dtype, int index_dtype, const void *data,
                    const void *indices, const void *indptr, int64_t nnz,
                    const void *x, void *y, int64_t n_rows, int64_t n_cols,

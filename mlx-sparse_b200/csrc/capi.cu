@@ -8,6 +8,7 @@
 #include "cg.cuh"
 #include "ops.cuh"
 #include "spmv.cuh"
+#include "spmv_binned.cuh"
 
 namespace msx {
 
@@ -25,12 +26,9 @@ void check_ptr(const void *p, int64_t count, const char *name) {
 }  // namespace msx
 
 struct msx_spmv_plan {
-  void *dev = nullptr;
+  void *dev = nullptr;  // one cudaMalloc holding the binned plan's arrays
   int device = 0;
-  int64_t n_rows = 0;
-  int64_t nnz = 0;
-  int64_t n_tiles = 0;
-  int64_t n_split = 0;
+  msx::BinnedPlan bins;
 };
 
 using namespace msx;
@@ -58,27 +56,17 @@ int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows, in
     check_ptr(indptr, n_rows + 1, "csr_matvec indptr");
     dispatch_index(index_dtype, [](auto) {});
     auto *plan = new msx_spmv_plan();
-    plan->n_rows = n_rows;
-    plan->nnz = nnz;
-    plan->n_tiles = spmv_num_tiles(n_rows, nnz);
     MSX_CUDA(cudaGetDevice(&plan->device));
-    cudaError_t e = cudaMalloc(&plan->dev, spmv_plan_device_bytes(plan->n_tiles));
-    if (e != cudaSuccess) {
-      delete plan;
-      fail(MSX_ERR_CUDA, std::string("cudaMalloc for the SpMV plan failed: ") + cudaGetErrorString(e));
-    }
     try {
-      cudaStream_t s = as_stream(stream);
-      spmv_build_plan(index_dtype, indptr, n_rows, nnz, plan->dev, plan->n_tiles, s);
-      unsigned long long split = 0;
-      int64_t *tr, *tn;
-      unsigned long long *ns;
-      spmv_plan_layout(plan->dev, plan->n_tiles, &tr, &tn, &ns);
-      MSX_CUDA(cudaMemcpyAsync(&split, ns, sizeof(split), cudaMemcpyDeviceToHost, s));
-      MSX_CUDA(cudaStreamSynchronize(s));
-      plan->n_split = (int64_t)split;
+      auto alloc = [&](size_t bytes) -> void * {
+        cudaError_t e = cudaMalloc(&plan->dev, bytes);
+        if (e != cudaSuccess)
+          fail(MSX_ERR_CUDA, std::string("cudaMalloc for the SpMV plan failed: ") + cudaGetErrorString(e));
+        return plan->dev;
+      };
+      build_binned_plan(index_dtype, indptr, n_rows, nnz, as_stream(stream), alloc, plan->bins);
     } catch (...) {
-      cudaFree(plan->dev);
+      if (plan->dev) cudaFree(plan->dev);
       delete plan;
       throw;
     }
@@ -100,11 +88,11 @@ int msx_spmv_plan_destroy(msx_spmv_plan *plan) {
   });
 }
 
-int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_tiles, int64_t *n_split_boundaries) {
+int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_blocks, int64_t *n_long_rows) {
   return guarded([&] {
     require(plan != nullptr, MSX_ERR_INVALID, "plan must not be null.");
-    if (n_tiles) *n_tiles = plan->n_tiles;
-    if (n_split_boundaries) *n_split_boundaries = plan->n_split;
+    if (n_blocks) *n_blocks = binned_blocks(plan->bins);
+    if (n_long_rows) *n_long_rows = plan->bins.n_long;
   });
 }
 
@@ -124,16 +112,10 @@ int msx_csr_matvec(int value_dtype, int index_dtype, const void *data, const voi
     if (n_rows == 0) return;
     cudaStream_t s = as_stream(stream);
     if (plan) {
-      require(plan->n_rows == n_rows && plan->nnz == nnz, MSX_ERR_INVALID,
+      require(plan->bins.n_rows == n_rows && plan->bins.nnz == nnz, MSX_ERR_INVALID,
               "csr_matvec plan was built for a different matrix shape.");
-      if (plan->n_split > 0) {
-        Scratch carry(sizeof(float) * 2 * plan->n_tiles, s);
-        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, plan->dev, plan->n_tiles, true,
-                 carry.as<float>(), s);
-      } else {
-        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, plan->dev, plan->n_tiles, false,
-                 nullptr, s);
-      }
+      Scratch carry(sizeof(float) * plan->bins.n_chunks, s);
+      spmv_binned_run(value_dtype, index_dtype, plan->bins, data, indices, indptr, x, y, carry.as<float>(), s);
       return;
     }
     const int64_t n_tiles = spmv_num_tiles(n_rows, nnz);

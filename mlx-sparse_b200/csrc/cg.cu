@@ -10,8 +10,9 @@
 //              float vector updates, statuses 0 / maxiter / -1 / -2 / -3.
 //
 // B200 design: one iteration is three kernels:
-//   K1  SpMV p -> Ap on the merge-path tiles (spmv.cuh) with p.Ap, p.p, Ap.Ap
-//       fused into the row epilogue (the rows a thread writes are final);
+//   K1  SpMV p -> Ap with the row-length-binned kernel (spmv_binned.cuh) and
+//       p.Ap, p.p, Ap.Ap fused into its row epilogue (every row is written
+//       once, final);
 //   K2  the x/r(/z) update with r.r (and r.z) fused;
 //   K3  the direction update p = r + beta p (or z + beta p).
 // Each reduction writes one fp64 partial per CTA; the last CTA to finish
@@ -20,12 +21,14 @@
 // a device state block. Later kernels read the state and return at once when
 // the solve has stopped, so batches of iterations are captured in a CUDA graph
 // and launched back to back; the host reads the status once per batch.
-// Matrices whose plan splits long rows between tiles run the plain SpMV +
-// fixup and a separate dot kernel instead of the fused K1.
+// Matrices with rows longer than the CTA bin (split into chunks) run the plain
+// SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
 #include <vector>
 
 #include "cg.cuh"
 #include "spmv.cuh"
+#include "spmv_binned.cuh"
+#include <memory>
 
 namespace msx {
 
@@ -404,21 +407,31 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   MSX_CUDA(cudaEventRecord(ev, user_stream));
   MSX_CUDA(cudaStreamWaitEvent(s, ev, 0));
 
-  const int64_t n_tiles = spmv_num_tiles(n, prob.nnz);
+  // Row-length bins of the matrix (built once per solve, in stream scratch).
+  std::vector<std::unique_ptr<Scratch>> keep;
+  BinnedPlan plan;
+  build_binned_plan(prob.index_dtype, prob.indptr, n, prob.nnz, s,
+                    [&](size_t bytes) -> void * {
+                      keep.emplace_back(new Scratch(bytes, s));
+                      return keep.back()->ptr;
+                    },
+                    plan);
+  const bool fused = plan.n_long == 0;
   const int red_grid = elementwise_grid(n);
-  const int spmv_grid_n = std::max(spmv_grid_for<float, int32_t, DotsEpilogue>(n_tiles, true),
-                                   spmv_grid_for<float, int64_t, DotsEpilogue>(n_tiles, true));
-  const int max_grid = std::max(red_grid, std::max(spmv_grid_n, spmv_grid(n_tiles)));
+  int64_t spmv_grid_n = 0;
+  dispatch_index(prob.index_dtype, [&](auto ityp) {
+    using I = decltype(ityp);
+    spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(plan), binned_grid<float, I, NoEpilogue>(plan));
+  });
+  const int64_t max_grid = std::max<int64_t>(red_grid, spmv_grid_n);
 
   // scratch layout
   const size_t vec = sizeof(float) * (size_t)std::max<int64_t>(n, 1);
-  const size_t plan_bytes = spmv_plan_device_bytes(n_tiles);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   size_t off = 0;
   const size_t o_state = off; off += al(sizeof(CgState));
   const size_t o_part = off;  off += al(sizeof(double) * 4 * max_grid);
-  const size_t o_plan = off;  off += al(plan_bytes);
-  const size_t o_carry = off; off += al(sizeof(float) * 2 * std::max<int64_t>(n_tiles, 1));
+  const size_t o_carry = off; off += al(sizeof(float) * std::max<int64_t>(plan.n_chunks, 1));
   const size_t o_r = off;     off += al(vec);
   const size_t o_z = off;     off += al(kind == kPCG ? vec : 0);
   const size_t o_p = off;     off += al(sizeof(float) * (size_t)std::max<int64_t>(prob.n_cols, 1));
@@ -427,30 +440,21 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   char *base = scratch.as<char>();
   CgState *st = reinterpret_cast<CgState *>(base + o_state);
   double *partials = reinterpret_cast<double *>(base + o_part);
-  void *plan = base + o_plan;
   float *carry = reinterpret_cast<float *>(base + o_carry);
   float *r = reinterpret_cast<float *>(base + o_r);
   float *z = kind == kPCG ? reinterpret_cast<float *>(base + o_z) : nullptr;
   float *p = reinterpret_cast<float *>(base + o_p);
   float *ap = reinterpret_cast<float *>(base + o_ap);
 
-  spmv_build_plan(prob.index_dtype, prob.indptr, n, prob.nnz, plan, n_tiles, s);
-  int64_t *tile_row, *tile_nz;
-  unsigned long long *n_split_dev;
-  spmv_plan_layout(plan, n_tiles, &tile_row, &tile_nz, &n_split_dev);
-
   CgState init{};
   init.status = kStatusRunning;
   init.it = 1;
   init.maxiter = prob.maxiter;
-  unsigned long long n_split = 0;
   MSX_CUDA(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
-  MSX_CUDA(cudaMemcpyAsync(&n_split, n_split_dev, sizeof(n_split), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaMemcpyAsync(prob.x, prob.x0, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
 
   // r0 = b - A x0
-  spmv_run(MSX_F32, prob.index_dtype, prob.data, prob.indices, prob.indptr, prob.x, ap, n, prob.nnz, plan, n_tiles,
-           true, carry, s);
+  spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, prob.x, ap, carry, s);
   init_kernel<<<red_grid, kThreads, 0, s>>>(kind, prob.b, prob.x, ap, prob.inv_diag, r, z, p, n, partials, st,
                                             prob.rtol, prob.atol, true);
   MSX_CHECK_LAUNCH();
@@ -458,20 +462,17 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   CgState host{};
   MSX_CUDA(cudaMemcpyAsync(&host, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
-  const bool fused = (n_split == 0);
 
   auto enqueue_iteration = [&](cudaStream_t q) {
     if (fused) {
       dispatch_index(prob.index_dtype, [&](auto ityp) {
         using I = decltype(ityp);
         DotsEpilogue epi{p, partials, st, kind, true, 0.0, 0.0, 0.0, 0.0};
-        launch_spmv_tiles<float, I, DotsEpilogue>(prob.data, static_cast<const I *>(prob.indices),
-                                                  static_cast<const I *>(prob.indptr), p, ap, tile_row, tile_nz,
-                                                  nullptr, nullptr, n_tiles, prob.nnz, n, epi, q);
+        launch_spmv_binned<float, I, DotsEpilogue>(plan, prob.data, static_cast<const I *>(prob.indices),
+                                                   static_cast<const I *>(prob.indptr), p, ap, carry, epi, q);
       });
     } else {
-      spmv_run(MSX_F32, prob.index_dtype, prob.data, prob.indices, prob.indptr, p, ap, n, prob.nnz, plan, n_tiles,
-               true, carry, q);
+      spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, p, ap, carry, q);
       dots_kernel<<<red_grid, kThreads, 0, q>>>(kind, p, ap, n, partials, st, true);
       MSX_CHECK_LAUNCH();
     }

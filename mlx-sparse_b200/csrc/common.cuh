@@ -122,6 +122,15 @@ template <> __device__ __forceinline__ __nv_bfloat16 ld_stream<__nv_bfloat16>(co
   return __ushort_as_bfloat16(r);
 }
 
+// Epilogue that only stores y. Epilogues see every finished row (`row`), may
+// skip the whole launch (`skip`, evaluated by every thread at entry) and run a
+// block-wide `finish` after the CTA's last tile.
+struct NoEpilogue {
+  __device__ __forceinline__ bool skip() const { return false; }
+  __device__ __forceinline__ void row(int64_t, float) {}
+  __device__ __forceinline__ void finish() {}
+};
+
 // Dispatch helpers ----------------------------------------------------------
 template <typename Fn> void dispatch_value(int vt, Fn &&fn) {
   switch (vt) {

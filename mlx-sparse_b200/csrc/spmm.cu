@@ -19,10 +19,31 @@ namespace msx {
 
 namespace {
 
+// L2 eviction-priority policies: the RHS slab is gathered repeatedly and should
+// stay resident (evict_last); the matrix arrays and the output are touched once
+// per slab (evict_first).
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ float4 ld_v4_hint(const void *p, uint64_t pol) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+
 template <typename T, int V>
-__device__ __forceinline__ void load_vec(const T *p, float (&out)[V]) {
+__device__ __forceinline__ void load_vec(const T *p, float (&out)[V], uint64_t pol) {
   if constexpr (V * sizeof(T) == 16) {
-    const float4 raw = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 raw = ld_v4_hint(p, pol);
     const T *e = reinterpret_cast<const T *>(&raw);
 #pragma unroll
     for (int i = 0; i < V; ++i) out[i] = VT<T>::load(e[i]);
@@ -59,6 +80,7 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
   const int64_t slab0 = blockIdx.y * slab_cols;
   const int64_t slab1 = min(slab0 + slab_cols, k);
   const int64_t p0 = (int64_t)indptr[row], p1 = (int64_t)indptr[row + 1];
+  const uint64_t pol_rhs = policy_evict_last();
   for (int64_t c = slab0 + (int64_t)lane_in_row * V; c < slab1; c += (int64_t)L * V) {
     float acc[V];
 #pragma unroll
@@ -75,7 +97,7 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
       }
       float b[4][V];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) load_vec<T, V>(rhs + (int64_t)col[u] * k + c, b[u]);
+      for (int u = 0; u < 4; ++u) load_vec<T, V>(rhs + (int64_t)col[u] * k + c, b[u], pol_rhs);
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -85,7 +107,7 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
       const I col = ld_stream(indices + p);
       const float a = VT<T>::load(ld_stream(data + p));
       float b[V];
-      load_vec<T, V>(rhs + (int64_t)col * k + c, b);
+      load_vec<T, V>(rhs + (int64_t)col * k + c, b, pol_rhs);
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, b[i]));
     }
@@ -111,7 +133,7 @@ int64_t spmm_l2_budget() {
     int dev = 0, l2 = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) == cudaSuccess && l2 > 0)
-      return (int64_t)l2 / 2;
+      return (int64_t)l2 / 4;
     return (int64_t)48 << 20;
   }();
   return budget;

@@ -106,15 +106,6 @@ struct TileSmem {
   SegPair warp_tot[kSpmvThreads / 32];
 };
 
-// Epilogue that only stores y. Epilogues see every finished row (`row`), may
-// skip the whole launch (`skip`, evaluated by every thread at entry) and run a
-// block-wide `finish` after the CTA's last tile.
-struct NoEpilogue {
-  __device__ __forceinline__ bool skip() const { return false; }
-  __device__ __forceinline__ void row(int64_t, float) {}
-  __device__ __forceinline__ void finish() {}
-};
-
 struct TileBounds {
   int64_t r0, r1, k0, k1;
   int R, K;

@@ -1,0 +1,252 @@
+// Row-length-binned CSR SpMV (the planned path).
+//
+// Rows are sorted (stably, once per matrix) into bins by their length; one
+// launch serves every bin with a block range of its own:
+//   bin 0  len <= 8      1 lane per row (the row is summed sequentially, in the
+//                        reference's order; all 8 loads of a row in flight)
+//   bin 1  len <= 16     2 lanes per row
+//   bin 2  len <= 32     4 lanes
+//   bin 3  len <= 64     8 lanes
+//   bin 4  len <= 128    16 lanes
+//   bin 5  len <= 512    a warp per row
+//   bin 6  len <= 8192   a CTA per row
+//   bin 7  longer        8192-nonzero chunks, one CTA each; chunk partials are
+//                        added in chunk order by a small fixup kernel.
+// Within a bin rows keep ascending order; when a single bin holds every row the
+// row list is the identity and is not stored. Lanes of a group stride over the
+// row (coalesced within the group) and their partials are combined by a
+// shuffle tree, so results are deterministic.
+#pragma once
+#include <vector>
+
+#include "common.cuh"
+
+namespace msx {
+
+constexpr int kBins = 8;
+constexpr int kBinThreads = 256;
+constexpr int kLongChunk = 8192;
+
+struct BinInfo {
+  long long block_start[kBins + 1];  // cumulative block counts per bin
+  long long row_start[kBins];        // offset of the bin in the row list
+  long long count[kBins];            // rows per bin
+  int identity;                      // 1: the row list is 0..n-1 (not stored)
+  int single_bin;                    // bin holding every row when identity
+};
+
+// Device buffers of a binned plan (one allocation).
+struct BinnedPlan {
+  BinInfo info{};
+  int64_t n_rows = 0, nnz = 0;
+  int *rows = nullptr;             // row list (n_rows) unless identity
+  int64_t n_chunks = 0;            // bin-7 chunks
+  int64_t n_long = 0;              // bin-7 rows
+  int64_t *chunk_row = nullptr;    // per chunk: row
+  int64_t *chunk_lo = nullptr;     // per chunk: first nonzero
+  int64_t *chunk_hi = nullptr;     // per chunk: end nonzero
+  int64_t *long_first = nullptr;   // per long row: first chunk (n_long + 1)
+  int64_t max_len = 0;
+  size_t bytes = 0;
+};
+
+// Builds the plan; `alloc` returns device memory of the requested size that
+// outlives the plan's use. Synchronises `stream`.
+template <typename Alloc>
+void build_binned_plan(int index_dtype, const void *indptr, int64_t n_rows, int64_t nnz, cudaStream_t stream,
+                       Alloc alloc, BinnedPlan &plan);
+void build_binned_plan_impl(int index_dtype, const void *indptr, int64_t n_rows, int64_t nnz, cudaStream_t stream,
+                            void *(*alloc)(size_t, void *), void *ctx, BinnedPlan &plan);
+template <typename Alloc>
+void build_binned_plan(int index_dtype, const void *indptr, int64_t n_rows, int64_t nnz, cudaStream_t stream,
+                       Alloc alloc, BinnedPlan &plan) {
+  build_binned_plan_impl(
+      index_dtype, indptr, n_rows, nnz, stream,
+      [](size_t b, void *c) -> void * { return (*static_cast<Alloc *>(c))(b); }, &alloc, plan);
+}
+
+// Carry buffer (floats) the long-row chunks need: plan.n_chunks.
+
+template <typename T>
+__device__ __forceinline__ float group_sum(float v, int G) {
+  for (int off = G >> 1; off > 0; off >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+template <typename T, typename I, typename Epi>
+__global__ void __launch_bounds__(kBinThreads)
+spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                   const T *__restrict__ x, T *__restrict__ y, const int *__restrict__ rows, BinInfo info,
+                   const int64_t *__restrict__ chunk_row, const int64_t *__restrict__ chunk_lo,
+                   const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
+  __shared__ float red[kBinThreads / 32];
+  if (epi.skip()) return;
+  for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
+  int bin = 0;
+#pragma unroll
+  for (int k = 1; k < kBins; ++k)
+    if (b >= info.block_start[k]) bin = k;
+  const long long lb = b - info.block_start[bin];
+  const int tid = threadIdx.x;
+  if (bin <= 5) {
+    const int G = 1 << bin;
+    const long long group = (lb * kBinThreads + tid) >> bin;
+    const int lane_g = tid & (G - 1);
+    const bool active = group < info.count[bin];
+    int64_t row = 0;
+    float acc = 0.f;
+    if (active) {
+      const long long pos = info.row_start[bin] + group;
+      row = info.identity ? pos : (int64_t)rows[pos];
+      const int64_t p0 = (int64_t)__ldg(indptr + row), p1 = (int64_t)__ldg(indptr + row + 1);
+      if (G == 1) {
+        // <= 8 nonzeros: issue every load of the row at once, then sum in order
+        I c[8];
+        T v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (p0 + u < p1) {
+            c[u] = ld_stream(indices + p0 + u);
+            v[u] = ld_stream(data + p0 + u);
+          }
+        }
+        float xv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (p0 + u < p1) xv[u] = VT<T>::load(__ldg(x + c[u]));
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (p0 + u < p1) acc = add_rn(acc, mul_rn(VT<T>::load(v[u]), xv[u]));
+      } else {
+        int64_t p = p0 + lane_g;
+        for (; p + 3 * G < p1; p += 4 * G) {
+          I c[4];
+          T v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            c[u] = ld_stream(indices + p + u * G);
+            v[u] = ld_stream(data + p + u * G);
+          }
+          float xv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) xv[u] = VT<T>::load(__ldg(x + c[u]));
+#pragma unroll
+          for (int u = 0; u < 4; ++u) acc = add_rn(acc, mul_rn(VT<T>::load(v[u]), xv[u]));
+        }
+        for (; p < p1; p += G) acc = add_rn(acc, mul_rn(VT<T>::load(ld_stream(data + p)),
+                                                        VT<T>::load(__ldg(x + ld_stream(indices + p)))));
+      }
+    }
+    if (G > 1) acc = group_sum<T>(acc, G);
+    if (active && lane_g == 0) {
+      const T out = VT<T>::store(acc);
+      y[row] = out;
+      epi.row(row, VT<T>::load(out));
+    }
+  } else {
+    int64_t row, p0, p1;
+    if (bin == 6) {
+      row = info.identity ? info.row_start[6] + lb : (int64_t)rows[info.row_start[6] + lb];
+      p0 = (int64_t)__ldg(indptr + row);
+      p1 = (int64_t)__ldg(indptr + row + 1);
+    } else {
+      row = chunk_row[lb];
+      p0 = chunk_lo[lb];
+      p1 = chunk_hi[lb];
+    }
+    float acc = 0.f;
+    int64_t p = p0 + tid;
+    for (; p + 3 * kBinThreads < p1; p += 4 * kBinThreads) {
+      I c[4];
+      T v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        c[u] = ld_stream(indices + p + u * kBinThreads);
+        v[u] = ld_stream(data + p + u * kBinThreads);
+      }
+      float xv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) xv[u] = VT<T>::load(__ldg(x + c[u]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc = add_rn(acc, mul_rn(VT<T>::load(v[u]), xv[u]));
+    }
+    for (; p < p1; p += kBinThreads)
+      acc = add_rn(acc, mul_rn(VT<T>::load(ld_stream(data + p)), VT<T>::load(__ldg(x + ld_stream(indices + p)))));
+    acc = group_sum<T>(acc, 32);
+    if ((tid & 31) == 0) red[tid >> 5] = acc;
+    __syncthreads();
+    if (tid == 0) {
+      float s = red[0];
+#pragma unroll
+      for (int w = 1; w < kBinThreads / 32; ++w) s = add_rn(s, red[w]);
+      if (bin == 6) {
+        const T out = VT<T>::store(s);
+        y[row] = out;
+        epi.row(row, VT<T>::load(out));
+      } else {
+        carry[lb] = s;
+      }
+    }
+    __syncthreads();  // red[] is reused by the next virtual block
+  }
+  }
+  epi.finish();
+}
+
+// Long rows: y[row] = sum of its chunk partials in chunk order.
+template <typename T>
+__global__ void spmv_long_fixup_kernel(const int *__restrict__ rows, BinInfo info, const int64_t *__restrict__ first,
+                                       const float *__restrict__ carry, T *__restrict__ y, int64_t n_long) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n_long) return;
+  const long long pos = info.row_start[7] + i;
+  const int64_t row = info.identity ? pos : (int64_t)rows[pos];
+  float s = carry[first[i]];
+  for (int64_t c = first[i] + 1; c < first[i + 1]; ++c) s = add_rn(s, carry[c]);
+  y[row] = VT<T>::store(s);
+}
+
+inline int64_t binned_blocks(const BinnedPlan &plan) { return plan.info.block_start[kBins]; }
+
+// Persistent grid: at most `waves` full waves of resident CTAs; each CTA walks
+// virtual blocks blockIdx.x, +gridDim.x, ...
+template <typename T, typename I, typename Epi>
+int64_t binned_grid(const BinnedPlan &plan) {
+  static thread_local int cached_dev = -1, per_sm = 0, sms = 0;
+  int dev = 0;
+  MSX_CUDA(cudaGetDevice(&dev));
+  if (dev != cached_dev) {
+    int occ = 0;
+    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_binned_kernel<T, I, Epi>, kBinThreads, 0));
+    per_sm = occ > 0 ? occ : 1;
+    sms = num_sms();
+    cached_dev = dev;
+  }
+  const int64_t cap = (int64_t)per_sm * sms * 4;
+  const int64_t nb = binned_blocks(plan);
+  return nb < cap ? nb : cap;
+}
+
+template <typename T, typename I, typename Epi>
+void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices, const I *indptr, const T *x, T *y,
+                        float *carry, Epi epi, cudaStream_t stream) {
+  const int64_t grid = binned_grid<T, I, Epi>(plan);
+  if (grid == 0) return;
+  spmv_binned_kernel<T, I, Epi><<<(unsigned)grid, kBinThreads, 0, stream>>>(
+      data, indices, indptr, x, y, plan.rows, plan.info, plan.chunk_row, plan.chunk_lo, plan.chunk_hi, carry, epi);
+  MSX_CHECK_LAUNCH();
+}
+
+template <typename T>
+void launch_spmv_long_fixup(const BinnedPlan &plan, const float *carry, T *y, cudaStream_t stream) {
+  if (plan.n_long == 0) return;
+  spmv_long_fixup_kernel<T><<<(unsigned)ceil_div(plan.n_long, 128), 128, 0, stream>>>(
+      plan.rows, plan.info, plan.long_first, carry, y, plan.n_long);
+  MSX_CHECK_LAUNCH();
+}
+
+// Untyped front door used by the C ABI.
+void spmv_binned_run(int value_dtype, int index_dtype, const BinnedPlan &plan, const void *data, const void *indices,
+                     const void *indptr, const void *x, void *y, float *carry, cudaStream_t stream);
+
+}  // namespace msx

@@ -98,9 +98,9 @@ def _p(t) -> int:
 
 
 class SpmvPlan:
-    """Owns an ``msx_spmv_plan`` (nnz-balanced tile partition of one matrix)."""
+    """Owns an ``msx_spmv_plan`` (row-length bins of one matrix)."""
 
-    __slots__ = ("handle", "n_tiles", "n_split", "device", "__weakref__")
+    __slots__ = ("handle", "n_blocks", "n_long", "device", "__weakref__")
 
     def __init__(self, indptr: torch.Tensor, n_rows: int, nnz: int):
         L = extension()
@@ -112,7 +112,7 @@ class SpmvPlan:
         self.handle = h
         nt, ns = ctypes.c_int64(), ctypes.c_int64()
         check(L.msx_spmv_plan_info(h, ctypes.byref(nt), ctypes.byref(ns)))
-        self.n_tiles, self.n_split = nt.value, ns.value
+        self.n_blocks, self.n_long = nt.value, ns.value
 
     def __del__(self):
         try:
