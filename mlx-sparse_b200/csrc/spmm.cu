@@ -13,6 +13,8 @@
 // RHS stays resident in L2 while all rows stream past it, so each random RHS
 // row gather hits L2 instead of HBM; the matrix arrays are re-streamed once
 // per slab with evict-first loads.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace msx {
@@ -67,51 +69,59 @@ __device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
   }
 }
 
-// grid.x: row blocks, grid.y: column slabs. Each L-lane group handles one row
-// and W = L*V columns of slab blockIdx.y.
+// grid.x: row blocks, grid.y: column slabs. A group of L lanes handles one row
+// and W = L*V columns of slab blockIdx.y. The group loads up to L (index,
+// value) pairs of its row with one coalesced load, then broadcasts them by
+// shuffles and issues kUnroll independent RHS gathers per lane before
+// accumulating, so each lane keeps several 16-byte gathers in flight. The
+// nonzeros are still consumed strictly in order (the reference's order).
 template <typename T, typename I, int V, int L>
 __global__ void __launch_bounds__(256)
 spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
             const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
   constexpr int kRowsPerBlock = 256 / L;
+  constexpr int kUnroll = 8;
+  const int lane = threadIdx.x & 31;
   const int lane_in_row = threadIdx.x % L;
+  const unsigned gmask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
   const int64_t row = blockIdx.x * (int64_t)kRowsPerBlock + threadIdx.x / L;
-  if (row >= n_rows) return;
+  const bool row_ok = row < n_rows;
   const int64_t slab0 = blockIdx.y * slab_cols;
   const int64_t slab1 = min(slab0 + slab_cols, k);
-  const int64_t p0 = (int64_t)indptr[row], p1 = (int64_t)indptr[row + 1];
+  const int64_t p0 = row_ok ? (int64_t)indptr[row] : 0;
+  const int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
   const uint64_t pol_rhs = policy_evict_last();
-  for (int64_t c = slab0 + (int64_t)lane_in_row * V; c < slab1; c += (int64_t)L * V) {
+  for (int64_t c = slab0 + (int64_t)lane_in_row * V; c - (int64_t)lane_in_row * V < slab1; c += (int64_t)L * V) {
+    const bool col_ok = c < slab1;
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    int64_t p = p0;
-    // Unrolled by 4 so four RHS row gathers are in flight per lane.
-    for (; p + 4 <= p1; p += 4) {
-      I col[4];
-      float a[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        col[u] = ld_stream(indices + p + u);
-        a[u] = VT<T>::load(ld_stream(data + p + u));
+    for (int64_t base = p0; base < p1; base += L) {
+      const int64_t j = base + lane_in_row;
+      I my_col = 0;
+      float my_val = 0.f;
+      if (j < p1) {
+        my_col = ld_stream(indices + j);
+        my_val = VT<T>::load(ld_stream(data + j));
       }
-      float b[4][V];
+      const int cnt = (int)min((int64_t)L, p1 - base);
+      for (int q = 0; q < cnt; q += kUnroll) {
+        float a[kUnroll];
+        float b[kUnroll][V];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) load_vec<T, V>(rhs + (int64_t)col[u] * k + c, b[u], pol_rhs);
+        for (int u = 0; u < kUnroll; ++u) {
+          const I col = __shfl_sync(gmask, my_col, (q + u) & (L - 1), L);
+          a[u] = __shfl_sync(gmask, my_val, (q + u) & (L - 1), L);
+          if (q + u < cnt && col_ok) load_vec<T, V>(rhs + (int64_t)col * k + c, b[u], pol_rhs);
+        }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kUnroll; ++u)
+          if (q + u < cnt)
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a[u], b[u][i]));
+            for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a[u], b[u][i]));
+      }
     }
-    for (; p < p1; ++p) {
-      const I col = ld_stream(indices + p);
-      const float a = VT<T>::load(ld_stream(data + p));
-      float b[V];
-      load_vec<T, V>(rhs + (int64_t)col * k + c, b, pol_rhs);
-#pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, b[i]));
-    }
-    store_vec<T, V>(out + row * k + c, acc);
+    if (row_ok && col_ok) store_vec<T, V>(out + row * k + c, acc);
   }
 }
 
@@ -133,7 +143,7 @@ int64_t spmm_l2_budget() {
     int dev = 0, l2 = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) == cudaSuccess && l2 > 0)
-      return (int64_t)l2 / 4;
+      return (int64_t)l2 * 3 / 4;
     return (int64_t)48 << 20;
   }();
   return budget;
@@ -152,21 +162,23 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
       const bool vec_ok = (k % kVec == 0) && (reinterpret_cast<uintptr_t>(rhs) % 16 == 0) &&
                           (reinterpret_cast<uintptr_t>(out) % 16 == 0);
       const int64_t elem = sizeof(T);
-      // Number of column slabs so that one RHS slab (n_cols x slab) fits the
-      // L2 budget.
-      const int64_t budget = spmm_l2_budget();
-      int64_t n_slabs = 1;
-      if (n_cols > 0 && budget > 0) n_slabs = ceil_div(n_cols * k * elem, budget);
-      if (n_slabs < 1) n_slabs = 1;
       const T *d = static_cast<const T *>(data);
       const I *ix = static_cast<const I *>(indices);
       const I *ip = static_cast<const I *>(indptr);
       const T *b = static_cast<const T *>(rhs);
       T *o = static_cast<T *>(out);
+      // One pass over the rows when the whole RHS fits the L2 budget (or the
+      // env override forces it); otherwise column slabs of one 128-byte cache
+      // line per RHS row, so every line the gathers bring into L2 is used in
+      // full.
+      const int64_t budget = spmm_l2_budget();
+      const bool one_pass = n_cols * k * elem <= budget || k * elem <= 128;
       if (vec_ok) {
-        const int64_t kv = k / kVec;                     // 16-byte vectors per row
-        const int64_t slab_vecs = ceil_div(kv, n_slabs);  // >= 1
-        if (slab_vecs >= 8) {
+        const int64_t kv = k / kVec;  // 16-byte vectors per row
+        const int64_t slab_vecs = one_pass ? kv : 128 / 16;
+        if (slab_vecs >= 16) {
+          launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream);
+        } else if (slab_vecs >= 8) {
           launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream);
         } else if (slab_vecs >= 4) {
           launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream);
@@ -178,7 +190,7 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
       } else {
         // Scalar path for widths that are not a multiple of the 16-byte vector.
         if (k >= 16) {
-          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(ceil_div(k, n_slabs), 16) * 16, stream);
+          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, one_pass ? ceil_div(k, 16) * 16 : 32, stream);
         } else if (k >= 4) {
           launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream);
         } else {

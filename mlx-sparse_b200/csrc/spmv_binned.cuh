@@ -80,6 +80,9 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
                    const int64_t *__restrict__ chunk_row, const int64_t *__restrict__ chunk_lo,
                    const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
   __shared__ float red[kBinThreads / 32];
+  // bin-0 staging when the CTA's rows are consecutive (identity row list)
+  __shared__ I idx_s[kBinThreads * 8];
+  __shared__ T val_s[kBinThreads * 8];
   if (epi.skip()) return;
   for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
   int bin = 0;
@@ -88,6 +91,44 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
     if (b >= info.block_start[k]) bin = k;
   const long long lb = b - info.block_start[bin];
   const int tid = threadIdx.x;
+  if (bin == 0 && info.identity) {
+    // Consecutive short rows: stage the CTA's contiguous nonzero range with
+    // fully coalesced loads, then each thread sums its row from shared memory
+    // in the reference's order.
+    const long long first = lb * kBinThreads;
+    const long long left = info.count[0] - first;
+    const int nr = (int)(left < kBinThreads ? left : kBinThreads);
+    const int64_t r0 = info.row_start[0] + first;
+    const int64_t k0 = (int64_t)__ldg(indptr + r0);
+    const int K = (int)((int64_t)__ldg(indptr + r0 + nr) - k0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = tid + q * kBinThreads;
+      if (e < K) {
+        idx_s[e] = ld_stream(indices + k0 + e);
+        val_s[e] = ld_stream(data + k0 + e);
+      }
+    }
+    __syncthreads();
+    if (tid < nr) {
+      const int64_t row = r0 + tid;
+      const int q0 = (int)((int64_t)__ldg(indptr + row) - k0);
+      const int q1 = (int)((int64_t)__ldg(indptr + row + 1) - k0);
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[q0 + u]));
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[q0 + u]), xv[u]));
+      const T out = VT<T>::store(acc);
+      y[row] = out;
+      epi.row(row, VT<T>::load(out));
+    }
+    __syncthreads();
+    continue;
+  }
   if (bin <= 5) {
     const int G = 1 << bin;
     const long long group = (lb * kBinThreads + tid) >> bin;
