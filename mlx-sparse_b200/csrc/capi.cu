@@ -27,9 +27,24 @@ void check_ptr(const void *p, int64_t count, const char *name) {
 
 struct msx_spmv_plan {
   void *dev = nullptr;  // one cudaMalloc holding the binned plan's arrays
+  void *tiles = nullptr;  // merge-path tile boundaries
   int device = 0;
+  int64_t n_tiles = 0, n_split = 0;
+  bool use_tiles = true;
   msx::BinnedPlan bins;
 };
+
+namespace {
+// Kernel used by planned products: merge-path tiles (default) or row bins;
+// MSX_SPMV_KERNEL=binned selects the latter.
+bool planned_use_tiles() {
+  static const bool tiles = [] {
+    const char *e = getenv("MSX_SPMV_KERNEL");
+    return !(e && std::string(e) == "binned");
+  }();
+  return tiles;
+}
+}  // namespace
 
 using namespace msx;
 
@@ -65,8 +80,22 @@ int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows, in
         return plan->dev;
       };
       build_binned_plan(index_dtype, indptr, n_rows, nnz, as_stream(stream), alloc, plan->bins);
+      plan->use_tiles = planned_use_tiles();
+      plan->n_tiles = spmv_num_tiles(n_rows, nnz);
+      cudaError_t e = cudaMalloc(&plan->tiles, spmv_plan_device_bytes(plan->n_tiles));
+      if (e != cudaSuccess)
+        fail(MSX_ERR_CUDA, std::string("cudaMalloc for the SpMV plan failed: ") + cudaGetErrorString(e));
+      cudaStream_t s = as_stream(stream);
+      spmv_build_plan(index_dtype, indptr, n_rows, nnz, plan->tiles, plan->n_tiles, s);
+      int64_t *tr, *tn;
+      unsigned long long *ns, split = 0;
+      spmv_plan_layout(plan->tiles, plan->n_tiles, &tr, &tn, &ns);
+      MSX_CUDA(cudaMemcpyAsync(&split, ns, sizeof(split), cudaMemcpyDeviceToHost, s));
+      MSX_CUDA(cudaStreamSynchronize(s));
+      plan->n_split = (int64_t)split;
     } catch (...) {
       if (plan->dev) cudaFree(plan->dev);
+      if (plan->tiles) cudaFree(plan->tiles);
       delete plan;
       throw;
     }
@@ -77,11 +106,12 @@ int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows, in
 int msx_spmv_plan_destroy(msx_spmv_plan *plan) {
   return guarded([&] {
     if (!plan) return;
-    if (plan->dev) {
+    if (plan->dev || plan->tiles) {
       int cur = 0;
       cudaGetDevice(&cur);
       if (cur != plan->device) cudaSetDevice(plan->device);
-      cudaFree(plan->dev);
+      if (plan->dev) cudaFree(plan->dev);
+      if (plan->tiles) cudaFree(plan->tiles);
       if (cur != plan->device) cudaSetDevice(cur);
     }
     delete plan;
@@ -91,8 +121,8 @@ int msx_spmv_plan_destroy(msx_spmv_plan *plan) {
 int msx_spmv_plan_info(const msx_spmv_plan *plan, int64_t *n_blocks, int64_t *n_long_rows) {
   return guarded([&] {
     require(plan != nullptr, MSX_ERR_INVALID, "plan must not be null.");
-    if (n_blocks) *n_blocks = binned_blocks(plan->bins);
-    if (n_long_rows) *n_long_rows = plan->bins.n_long;
+    if (n_blocks) *n_blocks = plan->use_tiles ? plan->n_tiles : binned_blocks(plan->bins);
+    if (n_long_rows) *n_long_rows = plan->use_tiles ? plan->n_split : plan->bins.n_long;
   });
 }
 
@@ -114,6 +144,12 @@ int msx_csr_matvec(int value_dtype, int index_dtype, const void *data, const voi
     if (plan) {
       require(plan->bins.n_rows == n_rows && plan->bins.nnz == nnz, MSX_ERR_INVALID,
               "csr_matvec plan was built for a different matrix shape.");
+      if (plan->use_tiles) {
+        Scratch carry(plan->n_split > 0 ? sizeof(float) * 2 * plan->n_tiles : 0, s);
+        spmv_run(value_dtype, index_dtype, data, indices, indptr, x, y, n_rows, nnz, plan->tiles, plan->n_tiles,
+                 plan->n_split > 0, carry.as<float>(), s);
+        return;
+      }
       Scratch carry(sizeof(float) * plan->bins.n_chunks, s);
       spmv_binned_run(value_dtype, index_dtype, plan->bins, data, indices, indptr, x, y, carry.as<float>(), s);
       return;

@@ -7,19 +7,15 @@
 //
 // B200 design: the matrix is cut into row-aligned merge-path tiles of about
 // kTileItems path items (rows + nonzeros), so every tile streams about the same
-// number of bytes whatever the row-length distribution. A plan records the
-// tile boundaries once per matrix; a persistent grid (a few CTAs per SM) walks
-// the tiles. Inside a tile (spmv.cuh):
-//   1. all nonzeros are loaded with coalesced streaming loads and their
-//      products data*x[col] are staged in shared memory (all gathers in flight
-//      at once), together with the tile's row-end offsets;
-//   2. each thread walks an equal share of the tile's merge path, summing its
-//      products sequentially; a segmented block scan hands each thread the
-//      partial sum of the row it starts in, and a second walk writes the rows.
-// A row held by one thread, or split across two threads, is therefore summed
-// in exactly the reference's left-to-right order. Rows longer than half a tile
-// are split between tiles; their tile partials go to scratch and a small fixup
-// kernel adds them in tile order (deterministic, no atomics).
+// number of bytes whatever the row-length distribution. A persistent grid (a
+// few CTAs per SM) walks the tiles; each CTA double-buffers them in shared
+// memory with TMA bulk copies (spmv.cuh). Inside a tile the products
+// data*x[col] are formed with every gather in flight at once, then each row is
+// summed from shared memory: by one thread, left to right as the reference
+// does, for rows of up to 32 nonzeros, by a warp for longer rows. Rows longer
+// than kSplitRowLen are split between tiles; their tile partials go to scratch
+// and a small fixup kernel adds them in tile order (deterministic, no
+// atomics on values).
 #include "spmv.cuh"
 
 namespace msx {

@@ -34,58 +34,6 @@ static_assert(kMaxTileItems % kSpmvThreads == 0, "tile staging assumes whole rou
 // completes in microseconds).
 constexpr long long kMaxPolls = 1ll << 22;
 
-struct SegPair {
-  int flag;  // 1 if the segment contains a row end (resets the running sum)
-  float val;
-};
-
-__device__ __forceinline__ SegPair seg_combine(SegPair a, SegPair b) {
-  // a precedes b
-  SegPair r;
-  r.flag = a.flag | b.flag;
-  r.val = b.flag ? b.val : add_rn(a.val, b.val);
-  return r;
-}
-
-// Block-wide exclusive segmented scan over kSpmvThreads threads.
-__device__ __forceinline__ SegPair block_exclusive_seg_scan(SegPair v, SegPair *warp_tot) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  constexpr int kWarps = kSpmvThreads / 32;
-  SegPair inc = v;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    SegPair o;
-    o.flag = __shfl_up_sync(0xffffffffu, inc.flag, off);
-    o.val = __shfl_up_sync(0xffffffffu, inc.val, off);
-    if (lane >= off) inc = seg_combine(o, inc);
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    SegPair w = lane < kWarps ? warp_tot[lane] : SegPair{0, 0.f};
-#pragma unroll
-    for (int off = 1; off < kWarps; off <<= 1) {
-      SegPair o;
-      o.flag = __shfl_up_sync(0xffffffffu, w.flag, off);
-      o.val = __shfl_up_sync(0xffffffffu, w.val, off);
-      if (lane >= off) w = seg_combine(o, w);
-    }
-    if (lane < kWarps) warp_tot[lane] = w;  // inclusive prefixes over warps
-  }
-  __syncthreads();
-  SegPair prev_lanes;
-  prev_lanes.flag = __shfl_up_sync(0xffffffffu, inc.flag, 1);
-  prev_lanes.val = __shfl_up_sync(0xffffffffu, inc.val, 1);
-  SegPair ex;
-  if (lane == 0) {
-    ex = warp > 0 ? warp_tot[warp - 1] : SegPair{0, 0.f};
-  } else {
-    ex = warp > 0 ? seg_combine(warp_tot[warp - 1], prev_lanes) : prev_lanes;
-  }
-  return ex;
-}
-
 // Merge-path search: number of row ends consumed among the first `diag` path
 // items, where row i ends after nonzero row_end(i)-1 (Merrill & Garland).
 template <typename Load>
@@ -100,10 +48,15 @@ __device__ __forceinline__ int64_t merge_path_search(int64_t diag, int64_t n_a, 
   return lo;
 }
 
+// Rows longer than this inside a tile are summed by a warp; shorter rows by one
+// thread, sequentially, in the reference's order.
+constexpr int kThreadRowLen = 32;
+
 struct TileSmem {
   float prod[kMaxTileItems];
   int row_end[kMaxTileItems];
-  SegPair warp_tot[kSpmvThreads / 32];
+  int long_rows[kMaxTileItems / (kThreadRowLen + 1) + 2];
+  int n_long;
 };
 
 struct TileBounds {
@@ -122,64 +75,55 @@ __device__ __forceinline__ TileBounds tile_bounds(int64_t t, const int64_t *tile
   return b;
 }
 
-// Walks the staged tile (sm.prod[0..K), sm.row_end[0..R)) and writes rows.
+// Sums the rows of the staged tile (sm.prod[0..K), sm.row_end[0..R)): a thread
+// per row for rows of at most kThreadRowLen nonzeros (summed left to right),
+// a warp per longer row (lane-strided, shuffle-tree combine). Row i of the
+// tile spans prod[row_end[i-1] .. row_end[i]) (row 0 from 0); a tile that ends
+// inside a split row holds that row's head segment as pseudo-row R.
 template <typename T, typename I, typename Epi>
-__device__ __forceinline__ void tile_walk(int64_t t, const TileBounds &tb, const I *__restrict__ indptr,
+__device__ __forceinline__ void tile_rows(int64_t t, const TileBounds &tb, const I *__restrict__ indptr,
                                           T *__restrict__ y, float *__restrict__ carry_head,
                                           float *__restrict__ carry_tail, TileSmem &sm, Epi &epi) {
-  const int R = tb.R, K = tb.K, P = R + K;
+  const int R = tb.R, K = tb.K;
   const int tid = threadIdx.x;
   const bool head_partial = (R > 0) && (tb.k0 > (int64_t)__ldg(indptr + tb.r0));
   const bool tail_partial = tb.k1 > (int64_t)__ldg(indptr + tb.r1);
-  const int ipt = (P + kSpmvThreads - 1) / kSpmvThreads;
-  const int d0 = min(tid * ipt, P);
-  const int d1 = min(d0 + ipt, P);
-  const int i0 = (int)merge_path_search(d0, R, K, [&](int64_t i) { return (int64_t)sm.row_end[i]; });
-  const int j0 = d0 - i0;
-
-  // Pass 1: this thread's carry-out (sum after its last row end).
-  SegPair mine{0, 0.f};
-  {
-    int i = i0, j = j0;
-    float acc = 0.f;
-    for (int d = d0; d < d1; ++d) {
-      if (i < R && sm.row_end[i] <= j) {
-        mine.flag = 1;
-        acc = 0.f;
-        ++i;
-      } else {
-        acc = add_rn(acc, sm.prod[j]);
-        ++j;
-      }
+  const int n_items = R + (tail_partial ? 1 : 0);
+  if (tid == 0) sm.n_long = 0;
+  __syncthreads();
+  auto emit = [&](int i, float acc) {
+    if (i == R) {
+      carry_tail[t] = acc;
+    } else if (i == 0 && head_partial) {
+      carry_head[t] = acc;
+    } else {
+      const T out = VT<T>::store(acc);
+      y[tb.r0 + i] = out;
+      epi.row(tb.r0 + i, VT<T>::load(out));
     }
-    mine.val = acc;
+  };
+  for (int i = tid; i < n_items; i += kSpmvThreads) {
+    const int s = i == 0 ? 0 : sm.row_end[i - 1];
+    const int e = i == R ? K : sm.row_end[i];
+    if (e - s <= kThreadRowLen) {
+      float acc = 0.f;
+      for (int j = s; j < e; ++j) acc = add_rn(acc, sm.prod[j]);
+      emit(i, acc);
+    } else {
+      sm.long_rows[atomicAdd(&sm.n_long, 1)] = i;
+    }
   }
-  const SegPair carry = block_exclusive_seg_scan(mine, sm.warp_tot);
-
-  // Pass 2: re-walk from the carried-in partial and write the rows. A row
-  // spanning two threads is thereby summed strictly left to right.
-  {
-    int i = i0, j = j0;
-    float acc = carry.val;
-    for (int d = d0; d < d1; ++d) {
-      if (i < R && sm.row_end[i] <= j) {
-        if (i == 0 && head_partial) {
-          carry_head[t] = acc;
-        } else {
-          const T out = VT<T>::store(acc);
-          y[tb.r0 + i] = out;
-          epi.row(tb.r0 + i, VT<T>::load(out));
-        }
-        acc = 0.f;
-        ++i;
-      } else {
-        acc = add_rn(acc, sm.prod[j]);
-        ++j;
-      }
-    }
-    // The thread holding the last path item owns the tile's tail partial when
-    // the tile ends inside a (split) row.
-    if (d0 < d1 && d1 == P && tail_partial) carry_tail[t] = acc;
+  __syncthreads();
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int w = warp; w < sm.n_long; w += kSpmvThreads / 32) {
+    const int i = sm.long_rows[w];
+    const int s = i == 0 ? 0 : sm.row_end[i - 1];
+    const int e = i == R ? K : sm.row_end[i];
+    float acc = 0.f;
+    for (int j = s + lane; j < e; j += 32) acc = add_rn(acc, sm.prod[j]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = add_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+    if (lane == 0) emit(i, acc);
   }
 }
 
@@ -215,7 +159,7 @@ __device__ __forceinline__ void spmv_process_tile(int64_t t, const T *__restrict
     }
   }
   __syncthreads();
-  tile_walk<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm, epi);
+  tile_rows<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm, epi);
   __syncthreads();  // smem reused by the next tile
 }
 
@@ -401,7 +345,7 @@ spmv_tiles_tma_kernel(const T *__restrict__ data, const I *__restrict__ indices,
       }
     }
     __syncthreads();
-    tile_walk<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm.tile, epi);
+    tile_rows<T, I, Epi>(t, tb, indptr, y, carry_head, carry_tail, sm.tile, epi);
     __syncthreads();  // stage s and the tile arrays are free again
   }
   epi.finish();
