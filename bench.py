@@ -302,11 +302,174 @@ class SpmvWorkload(Workload):
         return self.local_bytes / med / 1e9, f"full matrix, median of {len(times)} runs"
 
 
+class PcgWorkload(Workload):
+    """Jacobi-PCG on the 3D 7-point Poisson matrix (256^3),
+    b = A x* with x* ~ U(-1, 1) from seed 1, x0 = 0, rtol 1e-6, maxiter 2000.
+    A step is one full solve; value = iterations per second."""
+
+    unit = "iters/s"
+    unit_scale = 1.0
+    dtype = "f32"
+    scaling = "strong"
+
+    def __init__(self, m=256):
+        self.m = m
+        self.name = "pcg_poisson3d"
+        self.bytes_per_iter = None
+
+    def config(self):
+        return {"workload": self.name, "matrix": f"3D 7-point Poisson {self.m}^3 (n={self.m ** 3})",
+                "solver": "Jacobi PCG, rtol 1e-6, maxiter 2000, x0 = 0", "index": "int32",
+                "l2": "inputs (1.2 GB) exceed L2"}
+
+    def setup(self, rank, world, device):
+        import torch
+        import mlx_sparse as ms
+
+        (d, i, p), (n, _) = wl.poisson3d(self.m)
+        xs = wl.uniform_vector(n, 1)
+        self.n, self.nnz, self.world, self.dev = n, d.size, world, device
+        self.bytes_per_iter = 8 * d.size + 4 * (n + 1) + 52 * n
+        self.host = (d, i, p, xs)
+        if world == 1:
+            self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
+                                   torch.from_numpy(p).to(device)), shape=(n, n), canonical=True)
+            self.b = self.A @ torch.from_numpy(xs).to(device)
+            self.M = ms.linalg.preconditioners.jacobi(self.A)
+            self.h_d, self.h_i, self.h_p = (torch.from_numpy(a).pin_memory() for a in (d, i, p))
+            self.h_b = self.b.cpu().pin_memory()
+            self.h_x = torch.empty(n, dtype=torch.float32).pin_memory()
+            self.h2d_bytes = d.nbytes + i.nbytes + p.nbytes + 4 * n
+            self.d2h_bytes = 4 * n
+        else:
+            from mlx_sparse import distributed as dd
+            from mlx_sparse import _native
+
+            slab = dd.build_slab(d, i, p, n, rank, world)
+            self.slab = dd.DeviceSlab(slab, device)
+            xl = np.concatenate([xs[slab.r0:slab.r1], xs[slab.halo_cols]]).astype(np.float32)
+            self.b = _native.csr_matvec(self.slab.data, self.slab.indices, self.slab.indptr,
+                                        torch.from_numpy(xl).to(device), (slab.n_owned, xl.size))
+            rows = np.repeat(np.arange(slab.n_owned), np.diff(slab.indptr.astype(np.int64)))
+            diag = np.zeros(slab.n_owned, np.float32)
+            own = slab.indices.astype(np.int64) == rows
+            np.add.at(diag, rows[own], slab.data[own])
+            self.inv = torch.from_numpy((np.float32(1.0) / diag).astype(np.float32)).to(device)
+            self.comm = dd.Communicator(rank, world, device)
+            self.h2d_bytes = slab.data.nbytes + slab.indices.nbytes + slab.indptr.nbytes + 4 * slab.n_owned
+            self.d2h_bytes = 4 * slab.n_owned
+        self.step()  # warm up and learn the (deterministic) iteration count
+        self.units_per_step = float(self.iterations)
+        self.local_bytes = self.bytes_per_iter * self.iterations / world
+        self.launches_per_step = 3 * self.iterations + 6
+
+    def step(self):
+        import mlx_sparse as ms
+
+        if self.world == 1:
+            _, info = ms.linalg.cg(self.A, self.b, M=self.M, rtol=1e-6, maxiter=2000, return_info=True)
+            self.iterations, self.info = info.iterations, info.status
+        else:
+            from mlx_sparse import distributed as dd
+
+            _, info, _, its = dd.dist_cg(self.comm, self.slab, self.b, inv_diag_local=self.inv, rtol=1e-6,
+                                         maxiter=2000)
+            self.iterations, self.info = its, info
+
+    def e2e_step(self):
+        import mlx_sparse as ms
+
+        if self.world > 1:
+            return self.step()
+        A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
+                          self.h_p.to(self.dev, non_blocking=True)), shape=(self.n, self.n), canonical=True)
+        x, _ = ms.linalg.cg(A, self.h_b.to(self.dev, non_blocking=True), M=ms.linalg.preconditioners.jacobi(A),
+                            rtol=1e-6, maxiter=2000)
+        self.h_x.copy_(x, non_blocking=True)
+
+    def cpu_sample(self, workers, budget_s=10.0):
+        from oracle import oracle
+
+        d, i, p, xs = self.host
+        b = oracle.csr_matvec(d, i, p, xs, self.n, workers=workers)
+        inv = np.full(self.n, np.float32(1.0) / np.float32(6.0), np.float32)
+        x0 = np.zeros(self.n, np.float32)
+        t0 = time.perf_counter()
+        oracle.csr_pcg_jacobi(d, i, p, b, x0, inv, rtol=1e-6, atol=0.0, maxiter=2000, stop_after=1)
+        t1 = time.perf_counter() - t0
+        k = int(max(2, min(2000, budget_s / max(t1, 1e-6))))
+        t0 = time.perf_counter()
+        _, _, _, its = oracle.csr_pcg_jacobi(d, i, p, b, x0, inv, rtol=1e-6, atol=0.0, maxiter=2000, stop_after=k)
+        dt = time.perf_counter() - t0
+        return its / dt, f"first {its} PCG iterations of the solve (serial loop, as the reference's)"
+
+
+class SpgemmWorkload(Workload):
+    """C = A @ A, A 2^18 x 2^18 with 8 uniform nonzeros per
+    row; value = GB/s of compulsory bytes (A read as both operands, C written)."""
+
+    unit = "GB/s"
+    dtype = "f32"
+
+    def __init__(self, n=1 << 18, per_row=8, seed=4):
+        self.n, self.per_row, self.seed = n, per_row, seed
+        self.name = "spgemm"
+
+    def config(self):
+        return {"workload": self.name, "matrix": f"{self.n}x{self.n}, {self.per_row} nnz/row uniform",
+                "output": "canonical CSR, exact zeros pruned", "index": "int32"}
+
+    def setup(self, rank, world, device):
+        import torch
+        import mlx_sparse as ms
+
+        (d, i, p), _ = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
+        self.host = (d, i, p)
+        self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
+                               torch.from_numpy(p).to(device)), shape=(self.n, self.n), canonical=True)
+        C = self.A @ self.A
+        nnz_a = d.size
+        self.products = int(np.sum(np.diff(p)[i]))
+        self.local_bytes = 2 * (8 * nnz_a + 4 * (self.n + 1)) + 8 * C.nnz + 4 * (self.n + 1)
+        self.problem_bytes = self.local_bytes
+        self.launches_per_step = 12
+        self.h2d_bytes = d.nbytes + i.nbytes + p.nbytes
+        self.d2h_bytes = 8 * C.nnz + 4 * (self.n + 1)
+        self.dev = device
+
+    def step(self):
+        self.C = self.A @ self.A
+
+    def e2e_step(self):
+        import mlx_sparse as ms
+        import torch
+
+        d, i, p = self.host
+        A = ms.csr_array((torch.from_numpy(d).to(self.dev), torch.from_numpy(i).to(self.dev),
+                          torch.from_numpy(p).to(self.dev)), shape=(self.n, self.n), canonical=True)
+        C = A @ A
+        C.data.cpu(), C.indices.cpu(), C.indptr.cpu()
+
+    def cpu_sample(self, workers, budget_s=10.0):
+        from oracle import oracle
+
+        d, i, p = self.host
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 2:
+            t0 = time.perf_counter()
+            oracle.csr_matmat((d, i, p), (d, i, p), (self.n, self.n), (self.n, self.n))
+            times.append(time.perf_counter() - t0)
+        return self.local_bytes / statistics.median(times) / 1e9, f"full product, median of {len(times)} runs, 1 thread"
+
+
 WORKLOADS = {
     "spmm_f32": lambda: SpmmWorkload(bf16=False),
     "spmm_bf16": lambda: SpmmWorkload(bf16=True),
     "spmv_lap2d": lambda: SpmvWorkload("lap2d"),
     "spmv_powerlaw": lambda: SpmvWorkload("powerlaw"),
+    "pcg_poisson3d": lambda: PcgWorkload(),
+    "spgemm": lambda: SpgemmWorkload(),
 }
 
 
@@ -393,8 +556,9 @@ def run_b200(args):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
 
-    problem_bytes = _problem_bytes(wk)
-    value = problem_bytes / (ms_step_max * 1e-3) / 1e9
+    problem_units = _units(wk)
+    scale = getattr(wk, "unit_scale", 1e9)
+    value = problem_units / (ms_step_max * 1e-3) / scale
     # roofline of the dominant kernel on this rank: its local algorithmic bytes
     local_bytes = getattr(wk, "local_bytes", None) or _local_bytes(wk)
     achieved = local_bytes / (ms_step * 1e-3) / 1e9
@@ -416,7 +580,7 @@ def run_b200(args):
                      "frac": round(achieved / peak, 4), "traffic": _traffic(wk.name),
                      "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else peak_kind},
-        "e2e": {"value": round(problem_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": wk.unit,
+        "e2e": {"value": round(problem_units / (e2e_ms * 1e-3) / scale, 3), "unit": wk.unit,
                 "h2d_bytes_per_step": int(wk.h2d_bytes), "d2h_bytes_per_step": int(wk.d2h_bytes),
                 "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": int(wk.launches_per_step * args.steps),
@@ -427,13 +591,16 @@ def run_b200(args):
         v, sample = wk.cpu_sample(workers, budget_s=args.cpu_budget)
         line["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
                                 "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop"}
-    if rank == 0 and world == 1 and not args.no_extras:
+    if not args.no_extras:
+        # every rank takes part in the multi-GPU extras; rank 0 reports
+        names = (["spmv_lap2d", "spmv_powerlaw", "spmm_bf16", "spmm_f32", "pcg_poisson3d", "spgemm"]
+                 if world == 1 else ["pcg_poisson3d"])
         extras = {}
-        for name in ("spmv_lap2d", "spmv_powerlaw", "spmm_bf16", "spmm_f32"):
+        for name in names:
             if name == args.workload:
                 continue
             try:
-                extras[name] = _extra(name, args, device, peak)
+                extras[name] = _extra(name, args, device, peak, rank, world)
             except Exception as exc:  # report, do not hide
                 extras[name] = {"error": f"{type(exc).__name__}: {exc}"}
         line["workloads"] = extras
@@ -443,8 +610,9 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
-def _problem_bytes(wk):
-    return wk.problem_bytes
+def _units(wk):
+    """Metric units one step processes: bytes, or solver iterations."""
+    return getattr(wk, "units_per_step", None) or wk.problem_bytes
 
 
 def _local_bytes(wk):
@@ -467,17 +635,33 @@ def _traffic(name):
     return _TRAFFIC.get(name)
 
 
-def _extra(name, args, device, peak):
+def _extra(name, args, device, peak, rank=0, world=1):
     import torch
+    import torch.distributed as dist
 
     wk = WORKLOADS[name]()
-    wk.setup(0, 1, device)
-    times = _measure(wk, max(3, args.steps), args.warmup, device)
+    wk.setup(rank, world, device)
+    steps = max(3, args.steps) if not isinstance(wk, PcgWorkload) else 3
+    times = _measure(wk, steps, min(args.warmup, 3), device)
     ms_step = sum(times) / len(times)
+    t = torch.tensor([ms_step], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
     b = _local_bytes(wk)
-    out = {"value": round(b / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms_step, 5),
-           "frac_of_peak": round(b / (ms_step * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes": int(b),
+    scale = getattr(wk, "unit_scale", 1e9)
+    out = {"value": round(_units(wk) / (ms_max * 1e-3) / scale, 2), "unit": wk.unit,
+           "ms_per_step": round(ms_max, 5), "n_gpus": world,
+           "hbm_gbs_per_gpu": round(b / (ms_step * 1e-3) / 1e9, 1),
+           "frac_of_peak": round(b / (ms_step * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes_per_gpu": int(b),
            "config": wk.config(), "dtype": wk.dtype}
+    if isinstance(wk, PcgWorkload):
+        out.update({"iterations": wk.iterations, "info": wk.info, "bytes_per_iteration": int(wk.bytes_per_iter)})
+    if isinstance(wk, SpgemmWorkload):
+        out["products_per_s"] = round(wk.products / (ms_max * 1e-3), 1)
+    if rank == 0 and world == 1 and getattr(args, "extra_cpu", False):
+        v, sample = wk.cpu_sample(len(os.sched_getaffinity(0)), budget_s=5.0)
+        out["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "sample": sample}
     del wk
     torch.cuda.empty_cache()
     return out
@@ -529,6 +713,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="spmm_f32", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--extra-cpu", action="store_true", help="also time the CPU oracle for every extra workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()

@@ -162,6 +162,40 @@ MSX_API int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *i
                        int32_t maxiter, int32_t *info, float *residual,
                        int32_t *iterations, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU CG over row slabs (one process per GPU, NCCL over NVLink).      */
+/* ------------------------------------------------------------------------ */
+/* No counterpart in the reference, which runs on one device only (its CPU
+ * threads split rows by nnz-weighted ranges, src/common/cpu_parallel.cpp:
+ * 202-253; the same partition is applied here to GPUs). A communicator is
+ * created collectively: rank 0 calls msx_dist_unique_id, the 128-byte id is
+ * broadcast by the caller, every rank calls msx_dist_comm_create on its
+ * current device. */
+MSX_API int msx_dist_unique_id(void *out, int64_t size);
+MSX_API int msx_dist_comm_create(const void *unique_id, int nranks, int rank,
+                                 void **comm);
+MSX_API int msx_dist_comm_destroy(void *comm);
+
+/* CG (inv_diag == NULL) or Jacobi PCG of the global system, called by every
+ * rank with its slab: rows [r0, r0 + n_owned) of A with local column ids
+ * (owned columns first, then n_halo halo columns in owner order), its owned
+ * entries of b, x0 and inv_diag, and the halo lists: for each of n_peers
+ * peers (host arrays) the number of owned entries it needs (send_counts, the
+ * owned indices concatenated in device array send_idx) and the number of halo
+ * entries received from it (recv_counts). Same recurrence, statuses and
+ * residual as msx_csr_cg / msx_csr_pcg_jacobi (src/linalg/cg/cg.cpp:75-256,
+ * src/preconditioners/pcg/pcg.cpp:70-230); the scalars returned are
+ * identical on every rank. */
+MSX_API int msx_dist_pcg(void *comm, int index_dtype, const float *data,
+                         const void *indices, const void *indptr, int64_t nnz,
+                         int64_t n_owned, int64_t n_halo, const float *b,
+                         const float *x0, const float *inv_diag, float *x_out,
+                         float rtol, float atol, int32_t maxiter, int n_peers,
+                         const int *peers, const int64_t *send_counts,
+                         const int64_t *recv_counts, const int *send_idx,
+                         int32_t *info, float *residual, int32_t *iterations,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,11 @@
 // C-ABI entry points (include/msx_sparse.h). Argument checks follow the
 // reference front-ends (e.g. src/sparse/csr_matvec/csr_matvec.cpp:326-356) and
 // map C++ exception kinds onto msx_status codes.
+#include <cstring>
 #include <mutex>
+#if defined(MSX_HAVE_NCCL)
+#include <nccl.h>
+#endif
 #include <string>
 
 #include "msx_sparse.h"
@@ -30,17 +34,17 @@ struct msx_spmv_plan {
   void *tiles = nullptr;  // merge-path tile boundaries
   int device = 0;
   int64_t n_tiles = 0, n_split = 0;
-  bool use_tiles = true;
+  bool use_tiles = false;
   msx::BinnedPlan bins;
 };
 
 namespace {
-// Kernel used by planned products: merge-path tiles (default) or row bins;
-// MSX_SPMV_KERNEL=binned selects the latter.
+// Kernel used by planned products: row-length bins (default) or merge-path
+// tiles (MSX_SPMV_KERNEL=tiles).
 bool planned_use_tiles() {
   static const bool tiles = [] {
     const char *e = getenv("MSX_SPMV_KERNEL");
-    return !(e && std::string(e) == "binned");
+    return e && std::string(e) == "tiles";
   }();
   return tiles;
 }
@@ -284,6 +288,84 @@ int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *indices, 
     check_ptr(inv_diag, n_rows, "csr_pcg_jacobi inv_diag");
     CgProblem prob{index_dtype, data, indices, indptr, nnz, n_rows, n_cols, b, x0, inv_diag, x_out, rtol, atol,
                    maxiter};
+    CgResult r = cg_solve(prob, as_stream(stream));
+    *info = r.info;
+    *residual = r.residual;
+    *iterations = r.iterations;
+  });
+}
+
+// ---- multi-GPU (NCCL) ---------------------------------------------------------
+int msx_dist_unique_id(void *out, int64_t size) {
+  return guarded([&] {
+#if defined(MSX_HAVE_NCCL)
+    require(out != nullptr && size >= (int64_t)sizeof(ncclUniqueId), MSX_ERR_INVALID,
+            "msx_dist_unique_id needs a buffer of at least 128 bytes.");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+#else
+    (void)out;
+    (void)size;
+    fail(MSX_ERR_RUNTIME, "this build has no NCCL.");
+#endif
+  });
+}
+
+int msx_dist_comm_create(const void *unique_id, int nranks, int rank, void **out) {
+  return guarded([&] {
+#if defined(MSX_HAVE_NCCL)
+    require(unique_id && out, MSX_ERR_INVALID, "msx_dist_comm_create: null argument.");
+    require(nranks > 0 && rank >= 0 && rank < nranks, MSX_ERR_INVALID, "msx_dist_comm_create: bad rank.");
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    ncclComm_t comm;
+    const ncclResult_t r = ncclCommInitRank(&comm, nranks, id, rank);
+    if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    *out = comm;
+#else
+    (void)unique_id;
+    (void)nranks;
+    (void)rank;
+    (void)out;
+    fail(MSX_ERR_RUNTIME, "this build has no NCCL.");
+#endif
+  });
+}
+
+int msx_dist_comm_destroy(void *comm) {
+  return guarded([&] {
+#if defined(MSX_HAVE_NCCL)
+    if (comm) ncclCommDestroy(static_cast<ncclComm_t>(comm));
+#else
+    (void)comm;
+#endif
+  });
+}
+
+int msx_dist_pcg(void *comm, int index_dtype, const float *data, const void *indices, const void *indptr,
+                 int64_t nnz, int64_t n_owned, int64_t n_halo, const float *b, const float *x0,
+                 const float *inv_diag, float *x_out, float rtol, float atol, int32_t maxiter, int n_peers,
+                 const int *peers, const int64_t *send_counts, const int64_t *recv_counts, const int *send_idx,
+                 int32_t *info, float *residual, int32_t *iterations, void *stream) {
+  return guarded([&] {
+    require(comm != nullptr, MSX_ERR_INVALID, "msx_dist_pcg: comm must not be null.");
+    require(n_owned > 0 && n_halo >= 0 && n_peers >= 0, MSX_ERR_INVALID, "msx_dist_pcg: bad sizes.");
+    require(maxiter >= 0, MSX_ERR_INVALID, "csr_cg maxiter must be non-negative.");
+    require(n_peers == 0 || (peers && send_counts && recv_counts), MSX_ERR_INVALID,
+            "msx_dist_pcg: peer lists must not be null.");
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(data, nnz, "csr_cg data");
+    check_ptr(indices, nnz, "csr_cg indices");
+    check_ptr(indptr, n_owned + 1, "csr_cg indptr");
+    check_ptr(b, n_owned, "csr_cg b");
+    check_ptr(x0, n_owned, "csr_cg x0");
+    check_ptr(x_out, n_owned, "csr_cg x");
+    require(info && residual && iterations, MSX_ERR_INVALID, "csr_cg result pointers must not be null.");
+    CgDist d{comm, n_peers, peers, send_counts, recv_counts, send_idx, n_halo};
+    CgProblem prob{index_dtype, data, indices, indptr, nnz, n_owned, n_owned + n_halo, b, x0, inv_diag, x_out,
+                   rtol, atol, maxiter, &d};
     CgResult r = cg_solve(prob, as_stream(stream));
     *info = r.info;
     *residual = r.residual;

@@ -24,6 +24,9 @@
 // Matrices with rows longer than the CTA bin (split into chunks) run the plain
 // SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
 #include <vector>
+#if defined(MSX_HAVE_NCCL)
+#include <nccl.h>
+#endif
 
 #include "cg.cuh"
 #include "spmv.cuh"
@@ -373,6 +376,24 @@ pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ 
   }
 }
 
+// Multi-GPU: the reductions leave local sums in st->red; after the NCCL
+// all-reduce one thread makes the decision every rank makes identically.
+__global__ void decide_kernel(CgState *st, int which, int kind, float rtol, float atol) {
+  if (which != 0 && st->status != kStatusRunning) return;
+  switch (which) {
+  case 0: decide_init(st, kind, rtol, atol); break;
+  case 1: decide_spmv(st, kind); break;
+  case 2: decide_update(st, kind); break;
+  default: decide_pupdate(st); break;
+  }
+}
+
+__global__ void halo_pack_kernel(const float *__restrict__ v, const int *__restrict__ idx, float *__restrict__ out,
+                                 int64_t n) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) out[i] = v[idx[i]];
+}
+
 int elementwise_grid(int64_t n) {
   static thread_local int dev_cached = -1, sms = 0;
   int dev = 0;
@@ -391,6 +412,11 @@ int elementwise_grid(int64_t n) {
 CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   const int kind = prob.inv_diag ? kPCG : kCG;
   const int64_t n = prob.n;
+  const CgDist *dist = prob.dist;
+  const bool decide = dist == nullptr;
+#if !defined(MSX_HAVE_NCCL)
+  if (dist) fail(MSX_ERR_RUNTIME, "this build has no NCCL: multi-GPU CG is unavailable.");
+#endif
   // A private stream: graphs cannot be captured on the legacy default stream.
   cudaStream_t s;
   MSX_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
@@ -436,6 +462,11 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   const size_t o_z = off;     off += al(kind == kPCG ? vec : 0);
   const size_t o_p = off;     off += al(sizeof(float) * (size_t)std::max<int64_t>(prob.n_cols, 1));
   const size_t o_ap = off;    off += al(vec);
+  int64_t n_send = 0;
+  if (dist)
+    for (int q = 0; q < dist->n_peers; ++q) n_send += dist->send_counts[q];
+  const size_t o_send = off;  off += al(sizeof(float) * (size_t)std::max<int64_t>(n_send, 1));
+  const size_t o_xh = off;    off += al(dist ? sizeof(float) * (size_t)std::max<int64_t>(prob.n_cols, 1) : 0);
   Scratch scratch(off, s);
   char *base = scratch.as<char>();
   CgState *st = reinterpret_cast<CgState *>(base + o_state);
@@ -445,6 +476,49 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   float *z = kind == kPCG ? reinterpret_cast<float *>(base + o_z) : nullptr;
   float *p = reinterpret_cast<float *>(base + o_p);
   float *ap = reinterpret_cast<float *>(base + o_ap);
+  float *sendbuf = reinterpret_cast<float *>(base + o_send);
+  float *xh = dist ? reinterpret_cast<float *>(base + o_xh) : nullptr;
+
+  // Multi-GPU plumbing (all ranks issue the same sequence of collectives).
+  auto exchange = [&](float *v, cudaStream_t q) {
+#if defined(MSX_HAVE_NCCL)
+    if (!dist) return;
+    if (n_send > 0) {
+      halo_pack_kernel<<<(unsigned)ceil_div(n_send, 256), 256, 0, q>>>(v, dist->send_idx, sendbuf, n_send);
+      MSX_CHECK_LAUNCH();
+    }
+    ncclComm_t comm = static_cast<ncclComm_t>(dist->comm);
+    auto nccl = [](ncclResult_t r) {
+      if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
+    };
+    nccl(ncclGroupStart());
+    int64_t so = 0, ro = 0;
+    for (int k = 0; k < dist->n_peers; ++k) {
+      if (dist->send_counts[k] > 0)
+        nccl(ncclSend(sendbuf + so, (size_t)dist->send_counts[k], ncclFloat, dist->peers[k], comm, q));
+      if (dist->recv_counts[k] > 0)
+        nccl(ncclRecv(v + n + ro, (size_t)dist->recv_counts[k], ncclFloat, dist->peers[k], comm, q));
+      so += dist->send_counts[k];
+      ro += dist->recv_counts[k];
+    }
+    nccl(ncclGroupEnd());
+#else
+    (void)v;
+    (void)q;
+#endif
+  };
+  auto reduce_decide = [&](int which, cudaStream_t q) {
+#if defined(MSX_HAVE_NCCL)
+    if (!dist) return;
+    ncclResult_t r = ncclAllReduce(st->red, st->red, 4, ncclDouble, ncclSum, static_cast<ncclComm_t>(dist->comm), q);
+    if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
+    decide_kernel<<<1, 1, 0, q>>>(st, which, kind, prob.rtol, prob.atol);
+    MSX_CHECK_LAUNCH();
+#else
+    (void)which;
+    (void)q;
+#endif
+  };
 
   CgState init{};
   init.status = kStatusRunning;
@@ -453,33 +527,44 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   MSX_CUDA(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
   MSX_CUDA(cudaMemcpyAsync(prob.x, prob.x0, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
 
-  // r0 = b - A x0
-  spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, prob.x, ap, carry, s);
+  // r0 = b - A x0 (the halo of x0 comes from its owners first)
+  const float *x_in = prob.x;
+  if (dist) {
+    MSX_CUDA(cudaMemcpyAsync(xh, prob.x0, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+    exchange(xh, s);
+    x_in = xh;
+  }
+  spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, x_in, ap, carry, s);
   init_kernel<<<red_grid, kThreads, 0, s>>>(kind, prob.b, prob.x, ap, prob.inv_diag, r, z, p, n, partials, st,
-                                            prob.rtol, prob.atol, true);
+                                            prob.rtol, prob.atol, decide);
   MSX_CHECK_LAUNCH();
+  reduce_decide(0, s);
 
   CgState host{};
   MSX_CUDA(cudaMemcpyAsync(&host, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
 
   auto enqueue_iteration = [&](cudaStream_t q) {
+    exchange(p, q);
     if (fused) {
       dispatch_index(prob.index_dtype, [&](auto ityp) {
         using I = decltype(ityp);
-        DotsEpilogue epi{p, partials, st, kind, true, 0.0, 0.0, 0.0, 0.0};
+        DotsEpilogue epi{p, partials, st, kind, decide, 0.0, 0.0, 0.0, 0.0};
         launch_spmv_binned<float, I, DotsEpilogue>(plan, prob.data, static_cast<const I *>(prob.indices),
                                                    static_cast<const I *>(prob.indptr), p, ap, carry, epi, q);
       });
     } else {
       spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, p, ap, carry, q);
-      dots_kernel<<<red_grid, kThreads, 0, q>>>(kind, p, ap, n, partials, st, true);
+      dots_kernel<<<red_grid, kThreads, 0, q>>>(kind, p, ap, n, partials, st, decide);
       MSX_CHECK_LAUNCH();
     }
-    update_kernel<<<red_grid, kThreads, 0, q>>>(kind, prob.x, r, z, p, ap, prob.inv_diag, n, partials, st, true);
+    reduce_decide(1, q);
+    update_kernel<<<red_grid, kThreads, 0, q>>>(kind, prob.x, r, z, p, ap, prob.inv_diag, n, partials, st, decide);
     MSX_CHECK_LAUNCH();
-    pupdate_kernel<<<red_grid, kThreads, 0, q>>>(kind, r, z, p, n, partials, st, true);
+    reduce_decide(2, q);
+    pupdate_kernel<<<red_grid, kThreads, 0, q>>>(kind, r, z, p, n, partials, st, decide);
     MSX_CHECK_LAUNCH();
+    if (kind == kCG) reduce_decide(3, q);
   };
 
   if (host.status == kStatusRunning) {

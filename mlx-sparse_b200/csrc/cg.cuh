@@ -28,6 +28,18 @@ struct CgState {
   int pad[3];
 };
 
+// Multi-GPU layout of one rank (row slab with halo columns; see
+// mlx_sparse/distributed.py). Host arrays except send_idx (device).
+struct CgDist {
+  void *comm;                 // ncclComm_t
+  int n_peers;
+  const int *peers;           // peer ranks
+  const int64_t *send_counts; // per peer: entries of the owned vector sent
+  const int64_t *recv_counts; // per peer: halo entries received (halo order)
+  const int *send_idx;        // device: concatenated owned indices to send
+  int64_t n_halo;
+};
+
 struct CgProblem {
   int index_dtype;
   const float *data;
@@ -42,6 +54,7 @@ struct CgProblem {
   float *x;
   float rtol, atol;
   int maxiter;
+  const CgDist *dist = nullptr;  // null: single GPU
 };
 
 struct CgResult {

@@ -64,6 +64,12 @@ def extension():
                                      p, p, p, p]
             L.msx_csr_pcg_jacobi.argtypes = [c_int, p, p, p, i64, p, p, p, p, i64, i64, c_float, c_float,
                                              ctypes.c_int32, p, p, p, p]
+        if hasattr(L, "msx_dist_pcg"):
+            L.msx_dist_unique_id.argtypes = [p, i64]
+            L.msx_dist_comm_create.argtypes = [p, c_int, c_int, ctypes.POINTER(p)]
+            L.msx_dist_comm_destroy.argtypes = [p]
+            L.msx_dist_pcg.argtypes = [p, c_int, p, p, p, i64, i64, i64, p, p, p, p, c_float, c_float,
+                                       ctypes.c_int32, c_int, p, p, p, p, p, p, p, p]
         _lib = L
     return _lib
 

@@ -1,0 +1,212 @@
+"""Row-sharded products and CG across the GPUs of one node.
+
+The reference scales only across CPU threads, by contiguous nnz-weighted row
+ranges (``src/common/cpu_parallel.cpp:202-253``). Here the same partition is
+applied to GPUs: rank ``r`` owns a contiguous slab of rows with about
+``nnz / world`` nonzeros. Its local matrix keeps the owned columns first
+(renumbered ``c - r0``) and appends the "halo" columns it reads from other
+ranks, sorted by owner and then by column. Each SpMV inside the solver first
+receives the halo entries of the input vector from their owners over NCCL
+(grouped send/recv), and each scalar reduction of CG is an NCCL all-reduce of
+a few fp64 partial sums, so every rank takes the same scalar decisions and the
+solve keeps the reference's recurrence and status codes.
+
+Host-side logic (partition, halo lists) is plain numpy and is tested on CPU
+with ``gloo`` ranks; the solve itself runs in the CUDA library
+(``msx_dist_*`` in ``include/msx_sparse.h``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+
+def partition_rows(indptr: np.ndarray, world: int) -> list[tuple[int, int]]:
+    """Contiguous row ranges with about nnz / world nonzeros each."""
+    indptr = np.asarray(indptr)
+    n = indptr.shape[0] - 1
+    nnz = int(indptr[-1])
+    bounds = [0]
+    for r in range(1, world):
+        target = (nnz * r) // world
+        b = int(np.searchsorted(indptr, target, side="left"))
+        bounds.append(min(max(b, bounds[-1]), n))
+    bounds.append(n)
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+@dataclass
+class RowSlab:
+    """One rank's rows of a square CSR matrix with local column numbering."""
+
+    rank: int
+    world: int
+    r0: int
+    r1: int
+    data: np.ndarray
+    indices: np.ndarray      # local columns: owned [0, n_owned), halo [n_owned, n_owned + n_halo)
+    indptr: np.ndarray
+    halo_cols: np.ndarray    # global column of each halo slot
+    peers: np.ndarray        # ranks this rank exchanges with (ascending)
+    send_counts: np.ndarray  # per peer: owned entries sent to it
+    recv_counts: np.ndarray  # per peer: halo entries received from it (in halo order)
+    send_idx: np.ndarray     # concatenated per peer: local owned indices to send
+
+    @property
+    def n_owned(self) -> int:
+        return self.r1 - self.r0
+
+    @property
+    def n_halo(self) -> int:
+        return int(self.halo_cols.shape[0])
+
+
+def _cols_needed(indices, indptr, a0, a1, lo, hi):
+    """Sorted unique columns in [lo, hi) referenced by rows [a0, a1)."""
+    c = indices[int(indptr[a0]):int(indptr[a1])]
+    c = c[(c >= lo) & (c < hi)]
+    return np.unique(c)
+
+
+def build_slab(data, indices, indptr, n: int, rank: int, world: int, ranges=None) -> RowSlab:
+    """Cuts rank ``rank``'s slab out of the global (host) CSR arrays."""
+    indptr = np.asarray(indptr)
+    indices = np.asarray(indices)
+    ranges = ranges or partition_rows(indptr, world)
+    r0, r1 = ranges[rank]
+    k0, k1 = int(indptr[r0]), int(indptr[r1])
+    cols = indices[k0:k1].astype(np.int64)
+    owned = (cols >= r0) & (cols < r1)
+    halo_cols = np.unique(cols[~owned])
+    local = np.empty(cols.shape[0], dtype=np.int64)
+    local[owned] = cols[owned] - r0
+    local[~owned] = (r1 - r0) + np.searchsorted(halo_cols, cols[~owned])
+    peers, send_counts, recv_counts, send_idx = [], [], [], []
+    for q in range(world):
+        if q == rank:
+            continue
+        q0, q1 = ranges[q]
+        lo, hi = np.searchsorted(halo_cols, q0), np.searchsorted(halo_cols, q1)
+        n_recv = int(hi - lo)
+        needed = _cols_needed(indices, indptr, q0, q1, r0, r1)
+        if n_recv == 0 and needed.size == 0:
+            continue
+        peers.append(q)
+        recv_counts.append(n_recv)
+        send_counts.append(int(needed.size))
+        send_idx.append((needed - r0).astype(np.int32))
+    it = indices.dtype
+    return RowSlab(
+        rank=rank, world=world, r0=r0, r1=r1,
+        data=np.ascontiguousarray(np.asarray(data)[k0:k1]),
+        indices=local.astype(it),
+        indptr=(indptr[r0:r1 + 1] - indptr[r0]).astype(it),
+        halo_cols=halo_cols,
+        peers=np.asarray(peers, dtype=np.int32),
+        send_counts=np.asarray(send_counts, dtype=np.int64),
+        recv_counts=np.asarray(recv_counts, dtype=np.int64),
+        send_idx=np.concatenate(send_idx) if send_idx else np.zeros(0, np.int32),
+    )
+
+
+# ---------------------------------------------------------------------------
+# NCCL communicator and the distributed solve (GPU)
+# ---------------------------------------------------------------------------
+class Communicator:
+    """An NCCL communicator owned by the CUDA library, one per rank.
+
+    Created collectively: rank 0 draws the NCCL unique id and every rank
+    receives it through the already initialised ``torch.distributed`` group
+    (any backend), then joins with ``ncclCommInitRank`` on its current device.
+    """
+
+    def __init__(self, rank: int, world: int, device):
+        import torch
+        import torch.distributed as dist
+
+        from mlx_sparse import _native
+
+        L = _native.extension()
+        buf = ctypes.create_string_buffer(128)
+        if rank == 0:
+            _native.check(L.msx_dist_unique_id(buf, 128))
+        obj = [bytes(buf.raw) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _native.check(L.msx_dist_comm_create(uid, world, rank, ctypes.byref(h)))
+        self.handle, self.rank, self.world, self.device = h, rank, world, device
+
+    def close(self):
+        if self.handle:
+            from mlx_sparse import _native
+
+            _native.extension().msx_dist_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DeviceSlab:
+    """A RowSlab uploaded to one GPU."""
+
+    def __init__(self, slab: RowSlab, device, dtype=None):
+        import torch
+
+        self.slab = slab
+        self.device = device
+        self.data = torch.from_numpy(np.ascontiguousarray(slab.data)).to(device)
+        if dtype is not None:
+            self.data = self.data.to(dtype)
+        self.indices = torch.from_numpy(np.ascontiguousarray(slab.indices)).to(device)
+        self.indptr = torch.from_numpy(np.ascontiguousarray(slab.indptr)).to(device)
+        self.send_idx = torch.from_numpy(np.ascontiguousarray(slab.send_idx, dtype=np.int32)).to(device)
+
+
+def dist_cg(comm: Communicator, A: DeviceSlab, b_local, *, x0_local=None, inv_diag_local=None, rtol=1e-5,
+            atol=0.0, maxiter=None):
+    """CG (or Jacobi PCG when ``inv_diag_local`` is given) over row slabs.
+
+    Every rank passes its slab and its owned entries of b / x0 / inv_diag and
+    gets back its owned entries of x plus the (identical) status, residual and
+    iteration count.
+    """
+    import torch
+
+    from mlx_sparse import _native
+
+    L = _native.extension()
+    s = A.slab
+    n = s.n_owned
+    dev = A.device
+    b = b_local.to(dev, torch.float32).contiguous()
+    x0 = (torch.zeros(n, dtype=torch.float32, device=dev) if x0_local is None
+          else x0_local.to(dev, torch.float32).contiguous())
+    inv = None if inv_diag_local is None else inv_diag_local.to(dev, torch.float32).contiguous()
+    if maxiter is None:
+        n_global = torch.tensor([n], dtype=torch.int64)
+        import torch.distributed as dist
+
+        dist.all_reduce(n_global)
+        maxiter = 10 * int(n_global.item())
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    info, res, its = ctypes.c_int32(), ctypes.c_float(), ctypes.c_int32()
+    peers = np.ascontiguousarray(s.peers, dtype=np.int32)
+    sc = np.ascontiguousarray(s.send_counts, dtype=np.int64)
+    rc = np.ascontiguousarray(s.recv_counts, dtype=np.int64)
+    with torch.cuda.device(dev):
+        _native.check(L.msx_dist_pcg(
+            comm.handle, _native.INDEX_CODES[A.indices.dtype], A.data.data_ptr(), A.indices.data_ptr(),
+            A.indptr.data_ptr(), A.data.numel(), n, s.n_halo, b.data_ptr(), x0.data_ptr(),
+            inv.data_ptr() if inv is not None else None, x.data_ptr(), float(rtol), float(atol), int(maxiter),
+            int(peers.shape[0]), peers.ctypes.data, sc.ctypes.data, rc.ctypes.data, A.send_idx.data_ptr(),
+            ctypes.addressof(info), ctypes.addressof(res), ctypes.addressof(its), _native.stream_ptr(dev)))
+    return x, info.value, res.value, its.value
