@@ -85,6 +85,23 @@ MSX_API int msx_csr_matvec(int value_dtype, int index_dtype, const void *data,
                    const void *x, void *y, int64_t n_rows, int64_t n_cols,
                    const msx_spmv_plan *plan, void *stream);
 
+/* y = A @ x without allocating any device memory. No counterpart in the
+ * reference: it exists for callers that cannot allocate at call time (a
+ * pre-reserved memory budget, an execution phase where allocation is
+ * forbidden, or all free memory already handed to the caller's own pool).
+ * Same algorithm and results as msx_csr_matvec with plan == NULL, but the
+ * tile partition and split-row partials live in one fixed 4 MiB device array
+ * per GPU (held from library load until exit), which limits n_rows + nnz to
+ * about 223 million; larger inputs return MSX_ERR_INVALID. The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress), so make
+ * it before any stream capture. All calls share the array: calls whose work
+ * overlaps on the GPU race and must be ordered on one stream. */
+MSX_API int msx_csr_matvec_noalloc(int value_dtype, int index_dtype,
+                                   const void *data, const void *indices,
+                                   const void *indptr, int64_t nnz,
+                                   const void *x, void *y, int64_t n_rows,
+                                   int64_t n_cols, void *stream);
+
 /* Y = A @ B for a row-major dense B[n_cols, k] -> Y[n_rows, k]. Replaces
  * `csr_matmul(data, indices, indptr, rhs, n_rows, n_cols)`
  * (src/bindings.cpp:965-975 -> src/sparse/csr_matmul/csr_matmul.cpp:383-418,
