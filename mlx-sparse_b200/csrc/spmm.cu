@@ -75,12 +75,11 @@ __device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
 // shuffles and issues kUnroll independent RHS gathers per lane before
 // accumulating, so each lane keeps several 16-byte gathers in flight. The
 // nonzeros are still consumed strictly in order (the reference's order).
-template <typename T, typename I, int V, int L>
-__global__ void __launch_bounds__(256)
+template <typename T, typename I, int V, int L, int kUnroll, int kMinBlocks>
+__global__ void __launch_bounds__(256, kMinBlocks)
 spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
             const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
   constexpr int kRowsPerBlock = 256 / L;
-  constexpr int kUnroll = 8;
   const int lane = threadIdx.x & 31;
   const int lane_in_row = threadIdx.x % L;
   const unsigned gmask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
@@ -131,7 +130,19 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   constexpr int kRowsPerBlock = 256 / L;
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
-  spmm_kernel<T, I, V, L><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
+  // MSX_SPMM_VARIANT=0..4; 0 is the default.
+  static const int variant = [] {
+    const char *e = getenv("MSX_SPMM_VARIANT");
+    return e && *e ? atoi(e) : 0;
+  }();
+  switch (variant) {
+  case 1: spmm_kernel<T, I, V, L, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
+  case 2: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
+  case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
+  case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
+  default: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  }
   MSX_CHECK_LAUNCH();
 }
 
