@@ -80,9 +80,6 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
                    const int64_t *__restrict__ chunk_row, const int64_t *__restrict__ chunk_lo,
                    const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
   __shared__ float red[kBinThreads / 32];
-  // bin-0 staging when the CTA's rows are consecutive (identity row list)
-  __shared__ I idx_s[kBinThreads * 8];
-  __shared__ T val_s[kBinThreads * 8];
   if (epi.skip()) return;
   for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
   int bin = 0;
@@ -91,44 +88,6 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
     if (b >= info.block_start[k]) bin = k;
   const long long lb = b - info.block_start[bin];
   const int tid = threadIdx.x;
-  if (bin == 0 && info.identity) {
-    // Consecutive short rows: stage the CTA's contiguous nonzero range with
-    // fully coalesced loads, then each thread sums its row from shared memory
-    // in the reference's order.
-    const long long first = lb * kBinThreads;
-    const long long left = info.count[0] - first;
-    const int nr = (int)(left < kBinThreads ? left : kBinThreads);
-    const int64_t r0 = info.row_start[0] + first;
-    const int64_t k0 = (int64_t)__ldg(indptr + r0);
-    const int K = (int)((int64_t)__ldg(indptr + r0 + nr) - k0);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int e = tid + q * kBinThreads;
-      if (e < K) {
-        idx_s[e] = ld_stream(indices + k0 + e);
-        val_s[e] = ld_stream(data + k0 + e);
-      }
-    }
-    __syncthreads();
-    if (tid < nr) {
-      const int64_t row = r0 + tid;
-      const int q0 = (int)((int64_t)__ldg(indptr + row) - k0);
-      const int q1 = (int)((int64_t)__ldg(indptr + row + 1) - k0);
-      float xv[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[q0 + u]));
-      float acc = 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[q0 + u]), xv[u]));
-      const T out = VT<T>::store(acc);
-      y[row] = out;
-      epi.row(row, VT<T>::load(out));
-    }
-    __syncthreads();
-    continue;
-  }
   if (bin <= 5) {
     const int G = 1 << bin;
     const long long group = (lb * kBinThreads + tid) >> bin;
@@ -247,12 +206,108 @@ __global__ void spmv_long_fixup_kernel(const int *__restrict__ rows, BinInfo inf
   y[row] = VT<T>::store(s);
 }
 
+// ---- consecutive short rows -----------------------------------------------------
+// Every row has at most 8 nonzeros and the row list is the identity (stencil
+// matrices such as the 2D Laplacian and 3D Poisson operators). A CTA takes 256
+// consecutive rows: it copies their row offsets and then their contiguous
+// nonzero range into shared memory with cp.async (4/8-byte async copies, so the
+// loads in flight hold no registers and 8 CTAs fit an SM), then each thread
+// sums its row left to right - the reference's order - with every x gather of
+// the row issued at once.
+__device__ __forceinline__ void cp_async_4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_8(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <typename V>
+__device__ __forceinline__ void stage_elem(V *dst, const V *src) {
+  if constexpr (sizeof(V) == 8) cp_async_8(dst, src);
+  else if constexpr (sizeof(V) == 4) cp_async_4(dst, src);
+  else *dst = ld_stream(src);
+}
+
+constexpr int kShortRowsPerBlock = 256;
+
+template <typename T, typename I, typename Epi>
+__global__ void __launch_bounds__(kShortRowsPerBlock, 8)
+spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                  const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
+  __shared__ I ptr_s[kShortRowsPerBlock + 1];
+  __shared__ I idx_s[kShortRowsPerBlock * 8];
+  __shared__ T val_s[kShortRowsPerBlock * 8];
+  if (epi.skip()) return;
+  const int tid = threadIdx.x;
+  const int64_t nblk = (n_rows + kShortRowsPerBlock - 1) / kShortRowsPerBlock;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int64_t r0 = blk * kShortRowsPerBlock;
+    const int nr = (int)min((int64_t)kShortRowsPerBlock, n_rows - r0);
+    if (tid < nr) stage_elem(&ptr_s[tid], indptr + r0 + tid);
+    if (tid == 0) stage_elem(&ptr_s[nr], indptr + r0 + nr);
+    cp_async_wait_all();
+    __syncthreads();
+    const int64_t k0 = (int64_t)ptr_s[0];
+    const int K = (int)((int64_t)ptr_s[nr] - k0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = tid + q * kShortRowsPerBlock;
+      if (e < K) {
+        stage_elem(&idx_s[e], indices + k0 + e);
+        stage_elem(&val_s[e], data + k0 + e);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (tid < nr) {
+      const int q0 = (int)((int64_t)ptr_s[tid] - k0);
+      const int q1 = (int)((int64_t)ptr_s[tid + 1] - k0);
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[q0 + u]));
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[q0 + u]), xv[u]));
+      const T out = VT<T>::store(acc);
+      y[r0 + tid] = out;
+      epi.row(r0 + tid, VT<T>::load(out));
+    }
+    __syncthreads();  // shared arrays are refilled for the next block
+  }
+  epi.finish();
+}
+
+inline bool short_rows_plan(const BinnedPlan &plan) { return plan.info.identity && plan.info.single_bin == 0; }
+
+template <typename T, typename I, typename Epi>
+int64_t short_grid(int64_t n_rows) {
+  static thread_local int cached_dev = -1, per_sm = 0, sms = 0;
+  int dev = 0;
+  MSX_CUDA(cudaGetDevice(&dev));
+  if (dev != cached_dev) {
+    int occ = 0;
+    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_short_kernel<T, I, Epi>, kShortRowsPerBlock, 0));
+    per_sm = occ > 0 ? occ : 1;
+    sms = num_sms();
+    cached_dev = dev;
+  }
+  const int64_t nb = ceil_div(n_rows, kShortRowsPerBlock);
+  const int64_t cap = (int64_t)per_sm * sms;
+  return nb < cap ? nb : cap;
+}
+
 inline int64_t binned_blocks(const BinnedPlan &plan) { return plan.info.block_start[kBins]; }
 
 // Persistent grid: at most `waves` full waves of resident CTAs; each CTA walks
 // virtual blocks blockIdx.x, +gridDim.x, ...
 template <typename T, typename I, typename Epi>
 int64_t binned_grid(const BinnedPlan &plan) {
+  if (short_rows_plan(plan)) return short_grid<T, I, Epi>(plan.n_rows);
   static thread_local int cached_dev = -1, per_sm = 0, sms = 0;
   int dev = 0;
   MSX_CUDA(cudaGetDevice(&dev));
@@ -273,6 +328,12 @@ void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices,
                         float *carry, Epi epi, cudaStream_t stream) {
   const int64_t grid = binned_grid<T, I, Epi>(plan);
   if (grid == 0) return;
+  if (short_rows_plan(plan)) {
+    spmv_short_kernel<T, I, Epi><<<(unsigned)grid, kShortRowsPerBlock, 0, stream>>>(data, indices, indptr, x, y,
+                                                                                  plan.n_rows, epi);
+    MSX_CHECK_LAUNCH();
+    return;
+  }
   spmv_binned_kernel<T, I, Epi><<<(unsigned)grid, kBinThreads, 0, stream>>>(
       data, indices, indptr, x, y, plan.rows, plan.info, plan.chunk_row, plan.chunk_lo, plan.chunk_hi, carry, epi);
   MSX_CHECK_LAUNCH();
