@@ -277,6 +277,7 @@ init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, 
 // Fuses p.Ap, p.p, Ap.Ap (and the non-finite count) into the SpMV row
 // epilogue; the last CTA makes the step decision.
 struct DotsEpilogue {
+  static constexpr int kMinBlocks = 6;  // room for the fp64 accumulators
   const float *p;
   double *partials;
   CgState *st;

@@ -126,6 +126,7 @@ template <> __device__ __forceinline__ __nv_bfloat16 ld_stream<__nv_bfloat16>(co
 // skip the whole launch (`skip`, evaluated by every thread at entry) and run a
 // block-wide `finish` after the CTA's last tile.
 struct NoEpilogue {
+  static constexpr int kMinBlocks = 8;  // resident CTAs/SM the kernels aim for
   __device__ __forceinline__ bool skip() const { return false; }
   __device__ __forceinline__ void row(int64_t, float) {}
   __device__ __forceinline__ void finish() {}

@@ -234,7 +234,7 @@ __device__ __forceinline__ void stage_elem(V *dst, const V *src) {
 constexpr int kShortRowsPerBlock = 256;
 
 template <typename T, typename I, typename Epi>
-__global__ void __launch_bounds__(kShortRowsPerBlock, 8)
+__global__ void __launch_bounds__(kShortRowsPerBlock, Epi::kMinBlocks)
 spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
                   const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
   __shared__ I ptr_s[kShortRowsPerBlock + 1];
