@@ -181,7 +181,7 @@ int msx_csr_matmul(int value_dtype, int index_dtype, const void *data, const voi
     check_ptr(indptr, n_rows + 1, "csr_matmul indptr");
     check_ptr(rhs, nnz > 0 ? n_cols * rhs_cols : 0, "csr_matmul rhs");
     check_ptr(out, n_rows * rhs_cols, "csr_matmul out");
-    spmm_run(value_dtype, index_dtype, data, indices, indptr, rhs, rhs_cols, out, n_rows, n_cols,
+    spmm_run(value_dtype, index_dtype, data, indices, indptr, rhs, rhs_cols, out, n_rows, n_cols, nnz,
              as_stream(stream));
   });
 }

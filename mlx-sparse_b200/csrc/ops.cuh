@@ -5,7 +5,8 @@
 namespace msx {
 
 void spmm_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
-              const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, cudaStream_t stream);
+              const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, int64_t nnz,
+              cudaStream_t stream);
 
 void spgemm_run(bool write, int value_dtype, int lhs_it, const void *ld, const void *li, const void *lp, int rhs_it,
                 const void *rd, const void *ri, const void *rp, int64_t m, int64_t rhs_rows, int64_t n_cols,

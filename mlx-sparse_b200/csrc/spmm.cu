@@ -19,6 +19,11 @@
 
 namespace msx {
 
+bool spmm_tma_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+                  const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, int64_t nnz,
+                  cudaStream_t stream);
+int64_t spmm_tma_max_row();
+
 namespace {
 
 // L2 eviction-priority policies: the RHS slab is gathered repeatedly and should
@@ -78,7 +83,8 @@ __device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
 template <typename T, typename I, int V, int L, int kUnroll, int kMinBlocks>
 __global__ void __launch_bounds__(256, kMinBlocks)
 spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
-            const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+            const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols,
+            int64_t skip_le) {
   constexpr int kRowsPerBlock = 256 / L;
   const int lane = threadIdx.x & 31;
   const int lane_in_row = threadIdx.x % L;
@@ -88,7 +94,8 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
   const int64_t slab0 = blockIdx.y * slab_cols;
   const int64_t slab1 = min(slab0 + slab_cols, k);
   const int64_t p0 = row_ok ? (int64_t)indptr[row] : 0;
-  const int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
+  int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
+  if (p1 - p0 <= skip_le) return;  // rows done by the TMA kernel (whole group shares the row)
   const uint64_t pol_rhs = policy_evict_last();
   for (int64_t c = slab0 + (int64_t)lane_in_row * V; c - (int64_t)lane_in_row * V < slab1; c += (int64_t)L * V) {
     const bool col_ok = c < slab1;
@@ -126,7 +133,7 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
 
 template <typename T, typename I, int V, int L>
 void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs, T *out, int64_t n_rows,
-                 int64_t k, int64_t slab_cols, cudaStream_t stream) {
+                 int64_t k, int64_t slab_cols, cudaStream_t stream, int64_t skip_le = -1) {
   constexpr int kRowsPerBlock = 256 / L;
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
@@ -137,11 +144,11 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
     return e && *e ? atoi(e) : 0;
   }();
   switch (variant) {
-  case 1: spmm_kernel<T, I, V, L, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
-  case 2: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
-  case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
-  case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols); break;
-  default: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  case 1: spmm_kernel<T, I, V, L, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 2: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  default: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
   }
   MSX_CHECK_LAUNCH();
 }
@@ -163,7 +170,8 @@ int64_t spmm_l2_budget() {
 }  // namespace
 
 void spmm_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
-              const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, cudaStream_t stream) {
+              const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, int64_t nnz,
+              cudaStream_t stream) {
   if (n_rows == 0 || k == 0) return;
   dispatch_value(value_dtype, [&](auto vtyp) {
     using T = decltype(vtyp);
@@ -182,30 +190,36 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
       // env override forces it); otherwise column slabs of one 128-byte cache
       // line per RHS row, so every line the gathers bring into L2 is used in
       // full.
+      // TMA row gathers when the RHS rows are whole 128/256-byte boxes; the
+      // register kernel then only takes the rows too long for a TMA stage.
+      int64_t skip_le = -1;
+      if (spmm_tma_run(value_dtype, index_dtype, data, indices, indptr, rhs, k, out, n_rows, n_cols, nnz,
+                       stream))
+        skip_le = spmm_tma_max_row();
       const int64_t budget = spmm_l2_budget();
       const bool one_pass = n_cols * k * elem <= budget || k * elem <= 128;
       if (vec_ok) {
         const int64_t kv = k / kVec;  // 16-byte vectors per row
         const int64_t slab_vecs = one_pass ? kv : 128 / 16;
         if (slab_vecs >= 16) {
-          launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream);
+          launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream, skip_le);
         } else if (slab_vecs >= 8) {
-          launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream);
+          launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream, skip_le);
         } else if (slab_vecs >= 4) {
-          launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream);
+          launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream, skip_le);
         } else if (slab_vecs >= 2) {
-          launch_spmm<T, I, kVec, 2>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 2) * 2 * kVec, stream);
+          launch_spmm<T, I, kVec, 2>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 2) * 2 * kVec, stream, skip_le);
         } else {
-          launch_spmm<T, I, kVec, 1>(d, ix, ip, b, o, n_rows, k, kVec, stream);
+          launch_spmm<T, I, kVec, 1>(d, ix, ip, b, o, n_rows, k, kVec, stream, skip_le);
         }
       } else {
         // Scalar path for widths that are not a multiple of the 16-byte vector.
         if (k >= 16) {
-          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, one_pass ? ceil_div(k, 16) * 16 : 32, stream);
+          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, one_pass ? ceil_div(k, 16) * 16 : 32, stream, skip_le);
         } else if (k >= 4) {
-          launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream);
+          launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream, skip_le);
         } else {
-          launch_spmm<T, I, 1, 1>(d, ix, ip, b, o, n_rows, k, k, stream);
+          launch_spmm<T, I, 1, 1>(d, ix, ip, b, o, n_rows, k, k, stream, skip_le);
         }
       }
     });
