@@ -179,6 +179,15 @@ MSX_API int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *i
                        int32_t maxiter, int32_t *info, float *residual,
                        int32_t *iterations, void *stream);
 
+/* Main diagonal of a CSR matrix into out[min(n_rows, n_cols)], duplicate
+ * entries summed in stored order (fp32 accumulation). Replaces the native
+ * `csr_diagonal` that mlx-sparse's preconditioners.jacobi() calls
+ * (mlx_sparse/linalg/preconditioners.py:1108 -> src/sparse/csr_diagonal). */
+MSX_API int msx_csr_diagonal(int value_dtype, int index_dtype, const void *data,
+                             const void *indices, const void *indptr,
+                             int64_t nnz, int64_t n_rows, int64_t n_cols,
+                             void *out, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Multi-GPU CG over row slabs (one process per GPU, NCCL over NVLink).      */
 /* ------------------------------------------------------------------------ */

@@ -295,6 +295,21 @@ int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *indices, 
   });
 }
 
+int msx_csr_diagonal(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+                     int64_t nnz, int64_t n_rows, int64_t n_cols, void *out, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0 && nnz >= 0, MSX_ERR_INVALID, "csr_diagonal sizes must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    const int64_t n_diag = n_rows < n_cols ? n_rows : n_cols;
+    check_ptr(data, nnz, "csr_diagonal data");
+    check_ptr(indices, nnz, "csr_diagonal indices");
+    check_ptr(indptr, n_rows + 1, "csr_diagonal indptr");
+    check_ptr(out, n_diag, "csr_diagonal out");
+    csr_diagonal_run(value_dtype, index_dtype, data, indices, indptr, n_diag, out, as_stream(stream));
+  });
+}
+
 // ---- multi-GPU (NCCL) ---------------------------------------------------------
 int msx_dist_unique_id(void *out, int64_t size) {
   return guarded([&] {

@@ -183,3 +183,34 @@ void spmv_fixup_f32(int index_dtype, const void *indptr, float *y, const void *p
 }
 
 }  // namespace msx
+
+// ---- diagonal extraction (setup of Jacobi preconditioners) ------------------
+namespace msx {
+namespace {
+template <typename T, typename I>
+__global__ void csr_diagonal_kernel(const T *__restrict__ data, const I *__restrict__ indices,
+                                    const I *__restrict__ indptr, int64_t n_diag, T *__restrict__ out) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n_diag) return;
+  float acc = 0.f;  // duplicates of the diagonal entry summed in stored order
+  for (int64_t p = (int64_t)indptr[r]; p < (int64_t)indptr[r + 1]; ++p)
+    if ((int64_t)indices[p] == r) acc = add_rn(acc, VT<T>::load(data[p]));
+  out[r] = VT<T>::store(acc);
+}
+}  // namespace
+
+void csr_diagonal_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+                      int64_t n_diag, void *out, cudaStream_t stream) {
+  if (n_diag == 0) return;
+  dispatch_value(value_dtype, [&](auto vt) {
+    using T = decltype(vt);
+    dispatch_index(index_dtype, [&](auto it) {
+      using I = decltype(it);
+      csr_diagonal_kernel<T, I><<<(unsigned)ceil_div(n_diag, 256), 256, 0, stream>>>(
+          static_cast<const T *>(data), static_cast<const I *>(indices), static_cast<const I *>(indptr), n_diag,
+          static_cast<T *>(out));
+    });
+  });
+  MSX_CHECK_LAUNCH();
+}
+}  // namespace msx

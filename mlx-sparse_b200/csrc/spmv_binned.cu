@@ -41,14 +41,20 @@ bin_count_kernel(const I *__restrict__ indptr, int64_t n_rows, int64_t nblk, lon
     const unsigned m = __ballot_sync(0xffffffffu, bin == k);
     if (lane == 0) wc[warp][k] = __popc(m);
   }
+  __shared__ unsigned long long wmax[kPlanThreads / 32];
   unsigned long long ml = (unsigned long long)len;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     const unsigned long long o = __shfl_xor_sync(0xffffffffu, ml, off);
     ml = o > ml ? o : ml;
   }
-  if (lane == 0 && ml > 0) atomicMax(max_len, ml);
+  if (lane == 0) wmax[warp] = ml;
   __syncthreads();
+  if (threadIdx.x == 0) {  // one atomic per CTA, not per warp
+    unsigned long long m = 0;
+    for (int w = 0; w < kPlanThreads / 32; ++w) m = wmax[w] > m ? wmax[w] : m;
+    if (m > 0) atomicMax(max_len, m);
+  }
   if (threadIdx.x < kBins) {
     long long c = 0;
     for (int w = 0; w < kPlanThreads / 32; ++w) c += wc[w][threadIdx.x];

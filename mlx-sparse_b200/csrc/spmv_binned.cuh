@@ -233,91 +233,52 @@ __device__ __forceinline__ void stage_elem(V *dst, const V *src) {
 
 constexpr int kShortRowsPerBlock = 256;
 
-// Shared-memory layout of the short-row kernel: 3 row-offset buffers, then 2
-// index and 2 value buffers.
-template <typename I>
-constexpr size_t short_ptr_bytes() {
-  return ((3 * (kShortRowsPerBlock + 1) * sizeof(I)) + 15) & ~size_t(15);
-}
-template <typename T, typename I>
-constexpr size_t short_smem_bytes() {
-  return short_ptr_bytes<I>() + 2 * kShortRowsPerBlock * 8 * (sizeof(I) + sizeof(T));
-}
-
 template <typename T, typename I, typename Epi>
 __global__ void __launch_bounds__(kShortRowsPerBlock, Epi::kMinBlocks)
 spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
                   const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
-  // Software pipeline over this CTA's blocks b0, b0 + G, b0 + 2G, ...: while
-  // block j is summed from shared memory, block j+1's nonzeros and block
-  // j+2's row offsets are already in flight (cp.async groups).
-  extern __shared__ __align__(16) unsigned char short_smem[];
-  using PtrBuf = I[kShortRowsPerBlock + 1];
-  using IdxBuf = I[kShortRowsPerBlock * 8];
-  using ValBuf = T[kShortRowsPerBlock * 8];
-  PtrBuf *ptr_s = reinterpret_cast<PtrBuf *>(short_smem);
-  IdxBuf *idx_s = reinterpret_cast<IdxBuf *>(short_smem + short_ptr_bytes<I>());
-  ValBuf *val_s = reinterpret_cast<ValBuf *>(short_smem + short_ptr_bytes<I>() + 2 * sizeof(IdxBuf));
+  __shared__ I ptr_s[kShortRowsPerBlock + 1];
+  __shared__ I idx_s[kShortRowsPerBlock * 8];
+  __shared__ T val_s[kShortRowsPerBlock * 8];
   if (epi.skip()) return;
   const int tid = threadIdx.x;
   const int64_t nblk = (n_rows + kShortRowsPerBlock - 1) / kShortRowsPerBlock;
-  auto rows_of = [&](int64_t blk) { return (int)min((int64_t)kShortRowsPerBlock, n_rows - blk * kShortRowsPerBlock); };
-  auto load_ptr = [&](int64_t blk, int buf) {
-    if (blk >= nblk) return;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
     const int64_t r0 = blk * kShortRowsPerBlock;
-    const int nr = rows_of(blk);
-    if (tid < nr) stage_elem(&ptr_s[buf][tid], indptr + r0 + tid);
-    if (tid == 0) stage_elem(&ptr_s[buf][nr], indptr + r0 + nr);
-  };
-  auto load_data = [&](int64_t blk, int pbuf, int dbuf) {
-    if (blk >= nblk) return;
-    const int nr = rows_of(blk);
-    const int64_t k0 = (int64_t)ptr_s[pbuf][0];
-    const int K = (int)((int64_t)ptr_s[pbuf][nr] - k0);
+    const int nr = (int)min((int64_t)kShortRowsPerBlock, n_rows - r0);
+    if (tid < nr) stage_elem(&ptr_s[tid], indptr + r0 + tid);
+    if (tid == 0) stage_elem(&ptr_s[nr], indptr + r0 + nr);
+    cp_async_wait_all();
+    __syncthreads();
+    const int64_t k0 = (int64_t)ptr_s[0];
+    const int K = (int)((int64_t)ptr_s[nr] - k0);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int e = tid + q * kShortRowsPerBlock;
       if (e < K) {
-        stage_elem(&idx_s[dbuf][e], indices + k0 + e);
-        stage_elem(&val_s[dbuf][e], data + k0 + e);
+        stage_elem(&idx_s[e], indices + k0 + e);
+        stage_elem(&val_s[e], data + k0 + e);
       }
     }
-  };
-  const int64_t G = gridDim.x;
-  int64_t blk = blockIdx.x;
-  // prologue: offsets of blocks j=0 and j=1, nonzeros of block 0
-  load_ptr(blk, 0);
-  cp_async_wait_all();
-  __syncthreads();
-  load_data(blk, 0, 0);
-  load_ptr(blk + G, 1);
-  for (int j = 0; blk < nblk; ++j, blk += G) {
-    const int pc = j % 3, pn = (j + 1) % 3, pnn = (j + 2) % 3, dc = j & 1, dn = dc ^ 1;
     cp_async_wait_all();
-    __syncthreads();  // block j's nonzeros and block j+1's offsets have landed
-    load_data(blk + G, pn, dn);
-    load_ptr(blk + 2 * G, pnn);
-    const int64_t r0 = blk * kShortRowsPerBlock;
-    const int nr = rows_of(blk);
+    __syncthreads();
     if (tid < nr) {
-      const int64_t k0 = (int64_t)ptr_s[pc][0];
-      const int q0 = (int)((int64_t)ptr_s[pc][tid] - k0);
-      const int q1 = (int)((int64_t)ptr_s[pc][tid + 1] - k0);
+      const int q0 = (int)((int64_t)ptr_s[tid] - k0);
+      const int q1 = (int)((int64_t)ptr_s[tid + 1] - k0);
       float xv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[dc][q0 + u]));
+        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[q0 + u]));
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[dc][q0 + u]), xv[u]));
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[q0 + u]), xv[u]));
       const T out = VT<T>::store(acc);
       y[r0 + tid] = out;
       epi.row(r0 + tid, VT<T>::load(out));
     }
-    __syncthreads();  // buffers of block j are refilled two steps later
+    __syncthreads();  // shared arrays are refilled for the next block
   }
-  cp_async_wait_all();
   epi.finish();
 }
 
@@ -330,9 +291,7 @@ int64_t short_grid(int64_t n_rows) {
   MSX_CUDA(cudaGetDevice(&dev));
   if (dev != cached_dev) {
     int occ = 0;
-    auto kern = spmv_short_kernel<T, I, Epi>;
-    MSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)short_smem_bytes<T, I>()));
-    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kShortRowsPerBlock, short_smem_bytes<T, I>()));
+    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_short_kernel<T, I, Epi>, kShortRowsPerBlock, 0));
     per_sm = occ > 0 ? occ : 1;
     sms = num_sms();
     cached_dev = dev;
@@ -370,8 +329,8 @@ void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices,
   const int64_t grid = binned_grid<T, I, Epi>(plan);
   if (grid == 0) return;
   if (short_rows_plan(plan)) {
-    spmv_short_kernel<T, I, Epi><<<(unsigned)grid, kShortRowsPerBlock, short_smem_bytes<T, I>(), stream>>>(
-        data, indices, indptr, x, y, plan.n_rows, epi);
+    spmv_short_kernel<T, I, Epi><<<(unsigned)grid, kShortRowsPerBlock, 0, stream>>>(data, indices, indptr, x, y,
+                                                                                  plan.n_rows, epi);
     MSX_CHECK_LAUNCH();
     return;
   }

@@ -100,16 +100,8 @@ class CSRArray:
         return CSRArray(data, indices, indptr, self.shape, sorted_indices=True, has_canonical_format=True)
 
     def diagonal(self) -> torch.Tensor:
-        """Main diagonal (duplicates summed) as a dense vector."""
-        csr = self.canonicalize()
-        n = min(csr.shape)
-        rows = torch.repeat_interleave(
-            torch.arange(csr.shape[0], device=csr.device), torch.diff(csr.indptr.to(torch.int64))
-        )
-        mask = (rows == csr.indices.to(torch.int64)) & (rows < n)
-        out = torch.zeros(n, dtype=csr.data.dtype, device=csr.device)
-        out.index_put_((rows[mask],), csr.data[mask], accumulate=True)
-        return out
+        """Main diagonal as a dense vector (duplicate entries summed)."""
+        return _native.csr_diagonal(self.data, self.indices, self.indptr, self.shape)
 
     def todense(self) -> torch.Tensor:
         rows = torch.repeat_interleave(

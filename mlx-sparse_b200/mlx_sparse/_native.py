@@ -64,6 +64,7 @@ def extension():
                                      p, p, p, p]
             L.msx_csr_pcg_jacobi.argtypes = [c_int, p, p, p, i64, p, p, p, p, i64, i64, c_float, c_float,
                                              ctypes.c_int32, p, p, p, p]
+        L.msx_csr_diagonal.argtypes = [c_int, c_int, p, p, p, i64, i64, i64, p, p]
         if hasattr(L, "msx_dist_pcg"):
             L.msx_dist_unique_id.argtypes = [p, i64]
             L.msx_dist_comm_create.argtypes = [p, c_int, c_int, ctypes.POINTER(p)]
@@ -177,6 +178,17 @@ def csr_matmat(lhs, rhs, *, prune_zeros: bool = True):
         check(L.msx_csr_matmat_numeric(*args, _p(out_indptr), nnz.value, _p(out_data), _p(out_indices),
                                        int(prune_zeros), s))
     return out_data, out_indices, out_indptr
+
+
+def csr_diagonal(data, indices, indptr, shape):
+    L = extension()
+    dev = require_cuda(data, indices, indptr)
+    data, indices, indptr = (t.contiguous() for t in (data, indices, indptr))
+    out = torch.empty(min(shape), dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_diagonal(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                                 _p(indptr), data.numel(), shape[0], shape[1], _p(out), stream_ptr(dev)))
+    return out
 
 
 def _solver_outputs(dev, n):

@@ -131,3 +131,11 @@ def test_split_row_matrix(ms, orc):
     xr, info_r, _, its_r = orc.csr_cg(d, i, p, b, np.zeros(n, np.float32), rtol=1e-6, atol=0.0, maxiter=500)
     assert info.status == info_r == 0 and abs(info.iterations - its_r) <= 2
     np.testing.assert_allclose(x.cpu().numpy(), xr, rtol=1e-3, atol=1e-4)
+
+
+def test_diagonal_sums_duplicates(ms):
+    d = np.array([1.0, 2.0, 3.0, 4.0, 5.0], np.float32)
+    i = np.array([0, 0, 1, 1, 0], np.int32)
+    p = np.array([0, 2, 4, 5], np.int32)
+    A = ms.csr_array((_dev(d), _dev(i), _dev(p)), shape=(3, 2))
+    assert A.diagonal().cpu().tolist() == [3.0, 4.0]
