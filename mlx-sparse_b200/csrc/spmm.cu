@@ -145,10 +145,10 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   }();
   switch (variant) {
   case 1: spmm_kernel<T, I, V, L, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 2: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 2: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  default: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
+  default: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
   }
   MSX_CHECK_LAUNCH();
 }

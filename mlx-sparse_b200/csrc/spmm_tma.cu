@@ -10,9 +10,9 @@
 // whole RHS rows (one 128- or 256-byte box row each) into shared memory,
 // completing on the stage's mbarrier. Eight consumer warps wait on the stage,
 // and a group of 16-byte lanes per output row multiplies the staged RHS rows by
-// the row's values in nonzero order, then releases the stage. With two stages
-// per CTA the TMA keeps a full stage of gathers in flight while the previous
-// one is consumed, independently of register pressure.
+// the row's values in nonzero order, then releases the stage. With four
+// stages per CTA the TMA keeps several stages of gathers in flight while
+// another is consumed, independently of register pressure.
 //
 // Rows with more than kSlots nonzeros are skipped here and finished by the
 // register kernel (spmm.cu) restricted to them. TMA rules observed: the
@@ -33,8 +33,8 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
-constexpr int kStages = 2;
-constexpr int kSlots = 256;  // gathered RHS rows per stage
+constexpr int kStages = 4;
+constexpr int kSlots = 128;  // gathered RHS rows per stage
 constexpr long long kPollLimit = 1ll << 22;
 
 struct StageDesc {
@@ -200,13 +200,19 @@ spmm_tma_kernel(const __grid_constant__ CUtensorMap map, const T *__restrict__ d
       float acc[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
-      for (int64_t p = p0; p < p1; ++p) {
-        const float a = VT<T>::load(__ldg(data + p));
-        const float4 raw =
-            *reinterpret_cast<const float4 *>(buf + (size_t)(p - d.k0) * kBoxBytes + (size_t)lane_g * 16);
-        const T *e = reinterpret_cast<const T *>(&raw);
+      const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
+      for (int64_t base = p0; base < p1; base += G) {
+        // one coalesced load of up to G values, broadcast by shuffles
+        const float my_val = base + lane_g < p1 ? VT<T>::load(__ldg(data + base + lane_g)) : 0.f;
+        const int cnt = (int)min((int64_t)G, p1 - base);
+        const unsigned char *src = buf + (size_t)(base - d.k0) * kBoxBytes + (size_t)lane_g * 16;
+        for (int q = 0; q < cnt; ++q) {
+          const float a = __shfl_sync(gmask, my_val, q, G);
+          const float4 raw = *reinterpret_cast<const float4 *>(src + (size_t)q * kBoxBytes);
+          const T *e = reinterpret_cast<const T *>(&raw);
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, VT<T>::load(e[i])));
+          for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, VT<T>::load(e[i])));
+        }
       }
       const int64_t c = (int64_t)col0 + (int64_t)lane_g * V;
       if (c < k) {
