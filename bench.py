@@ -355,13 +355,20 @@ class PcgWorkload(Workload):
             own = slab.indices.astype(np.int64) == rows
             np.add.at(diag, rows[own], slab.data[own])
             self.inv = torch.from_numpy((np.float32(1.0) / diag).astype(np.float32)).to(device)
-            self.comm = dd.Communicator(rank, world, device)
-            self.h2d_bytes = slab.data.nbytes + slab.indices.nbytes + slab.indptr.nbytes + 4 * slab.n_owned
+            self.mode = os.environ.get("MSX_DIST_COMM", "p2p")
+            self.solver = dd.DistCG(self.slab, preconditioned=True, comm=self.mode)
+            self.h_b = self.b.cpu().pin_memory()
+            self.h_x = torch.empty(slab.n_owned, dtype=torch.float32).pin_memory()
+            self.h2d_bytes = 4 * slab.n_owned
             self.d2h_bytes = 4 * slab.n_owned
         self.step()  # warm up and learn the (deterministic) iteration count
         self.units_per_step = float(self.iterations)
         self.local_bytes = self.bytes_per_iter * self.iterations / world
-        self.launches_per_step = 3 * self.iterations + 6
+        # per iteration: SpMV(+dots), update, direction update, plus at N>1
+        # the halo exchange and the scalar reductions (peer memory: push +
+        # wait + 2 all-reduce kernels; NCCL: pack + 2 decide kernels)
+        per_it = 3 if world == 1 else (7 if self.mode == "p2p" else 6)
+        self.launches_per_step = per_it * self.iterations + 6
 
     def step(self):
         import mlx_sparse as ms
@@ -370,17 +377,19 @@ class PcgWorkload(Workload):
             _, info = ms.linalg.cg(self.A, self.b, M=self.M, rtol=1e-6, maxiter=2000, return_info=True)
             self.iterations, self.info = info.iterations, info.status
         else:
-            from mlx_sparse import distributed as dd
-
-            _, info, _, its = dd.dist_cg(self.comm, self.slab, self.b, inv_diag_local=self.inv, rtol=1e-6,
-                                         maxiter=2000)
+            _, info, _, its = self.solver.solve(self.b, inv_diag_local=self.inv, rtol=1e-6, maxiter=2000)
             self.iterations, self.info = its, info
 
     def e2e_step(self):
         import mlx_sparse as ms
 
         if self.world > 1:
-            return self.step()
+            # the matrix slabs stay resident in the persistent solver; each
+            # step uploads this rank's b and reads back its x
+            x, *_ = self.solver.solve(self.h_b.to(self.dev, non_blocking=True), inv_diag_local=self.inv,
+                                      rtol=1e-6, maxiter=2000)
+            self.h_x.copy_(x, non_blocking=True)
+            return
         A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
                           self.h_p.to(self.dev, non_blocking=True)), shape=(self.n, self.n), canonical=True)
         x, _ = ms.linalg.cg(A, self.h_b.to(self.dev, non_blocking=True), M=ms.linalg.preconditioners.jacobi(A),

@@ -222,6 +222,41 @@ MSX_API int msx_dist_pcg(void *comm, int index_dtype, const float *data,
                          int32_t *info, float *residual, int32_t *iterations,
                          void *stream);
 
+/* Persistent CG solver for one matrix (and one rank): the row bins, work
+ * buffers and the CUDA graph of a batch of iterations are built once and reused
+ * by every msx_cg_context_solve, so repeated solves skip all setup. No
+ * counterpart in the reference (its csr_cg / csr_pcg_jacobi primitives,
+ * src/linalg/cg/cg.cpp:338-379, src/preconditioners/pcg/pcg.cpp:317-366,
+ * rebuild everything per call); the solve itself is the same recurrence.
+ * comm_mode: 0 single GPU, 1 NCCL (nccl_comm from msx_dist_comm_create),
+ * 2 peer memory over NVLink: every rank exports two IPC handles
+ * (msx_cg_context_ipc_handles), the caller gathers them in rank order and
+ * passes all of them to msx_cg_context_connect before the first solve;
+ * peer_dst_offset[k] is where this rank's entries for peer k start in that
+ * peer's p vector (its owned length plus the offset of this rank's block in
+ * its halo). All ranks must call solve together; peer waits are bounded and a
+ * lost peer ends the solve with an error instead of hanging. */
+typedef struct msx_cg_context msx_cg_context;
+MSX_API int msx_cg_context_create(int index_dtype, const float *data,
+                                  const void *indices, const void *indptr,
+                                  int64_t nnz, int64_t n_owned, int64_t n_halo,
+                                  int preconditioned, int comm_mode, int rank,
+                                  int world, void *nccl_comm, int n_peers,
+                                  const int *peers, const int64_t *send_counts,
+                                  const int64_t *recv_counts, const int *send_idx,
+                                  const int64_t *peer_dst_offset, void *stream,
+                                  msx_cg_context **out);
+MSX_API int msx_cg_context_ipc_handles(msx_cg_context *ctx, void *out,
+                                       int64_t size);
+MSX_API int msx_cg_context_connect(msx_cg_context *ctx, const void *all_handles,
+                                   int64_t size);
+MSX_API int msx_cg_context_solve(msx_cg_context *ctx, const float *b,
+                                 const float *x0, const float *inv_diag,
+                                 float *x_out, float rtol, float atol,
+                                 int32_t maxiter, int32_t *info, float *residual,
+                                 int32_t *iterations, void *stream);
+MSX_API int msx_cg_context_destroy(msx_cg_context *ctx);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,7 +2,9 @@
 // reference front-ends (e.g. src/sparse/csr_matvec/csr_matvec.cpp:326-356) and
 // map C++ exception kinds onto msx_status codes.
 #include <cstring>
+#include <memory>
 #include <mutex>
+#include <vector>
 #if defined(MSX_HAVE_NCCL)
 #include <nccl.h>
 #endif
@@ -49,6 +51,15 @@ bool planned_use_tiles() {
   return tiles;
 }
 }  // namespace
+
+// A persistent CG solver (one matrix, one rank) with copies of its peer lists.
+struct msx_cg_context {
+  msx::CgEngine *engine = nullptr;
+  std::vector<int> peers;
+  std::vector<int64_t> send_counts, recv_counts, dst_offset;
+  int world = 1;
+  ~msx_cg_context() { msx::cg_engine_destroy(engine); }
+};
 
 using namespace msx;
 
@@ -386,6 +397,91 @@ int msx_dist_pcg(void *comm, int index_dtype, const float *data, const void *ind
     *residual = r.residual;
     *iterations = r.iterations;
   });
+}
+
+// ---- persistent CG contexts ------------------------------------------------------
+int msx_cg_context_create(int index_dtype, const float *data, const void *indices, const void *indptr, int64_t nnz,
+                          int64_t n_owned, int64_t n_halo, int preconditioned, int comm_mode, int rank, int world,
+                          void *nccl_comm, int n_peers, const int *peers, const int64_t *send_counts,
+                          const int64_t *recv_counts, const int *send_idx, const int64_t *peer_dst_offset,
+                          void *stream, msx_cg_context **out) {
+  return guarded([&] {
+    require(out != nullptr, MSX_ERR_INVALID, "msx_cg_context_create: out must not be null.");
+    *out = nullptr;
+    require(n_owned > 0 && n_halo >= 0 && nnz >= 0, MSX_ERR_INVALID, "csr_cg requires a non-empty square matrix.");
+    require(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world, MSX_ERR_INVALID, "bad rank / world.");
+    require(comm_mode >= kCommNone && comm_mode <= kCommP2p, MSX_ERR_INVALID, "bad comm mode.");
+    require(world == 1 || comm_mode != kCommNone, MSX_ERR_INVALID, "multi-rank contexts need a comm mode.");
+    require(comm_mode != kCommNccl || nccl_comm, MSX_ERR_INVALID, "NCCL mode needs a communicator.");
+    require(n_peers >= 0 && n_peers < kMaxRanks, MSX_ERR_INVALID, "bad peer count.");
+    require(n_peers == 0 || (peers && send_counts && recv_counts), MSX_ERR_INVALID, "peer lists must not be null.");
+    require(comm_mode != kCommP2p || n_peers == 0 || peer_dst_offset, MSX_ERR_INVALID,
+            "P2P mode needs the landing offsets.");
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(data, nnz, "csr_cg data");
+    check_ptr(indices, nnz, "csr_cg indices");
+    check_ptr(indptr, n_owned + 1, "csr_cg indptr");
+    std::unique_ptr<msx_cg_context> ctx(new msx_cg_context());
+    ctx->world = world;
+    ctx->peers.assign(peers, peers + n_peers);
+    ctx->send_counts.assign(send_counts, send_counts + n_peers);
+    ctx->recv_counts.assign(recv_counts, recv_counts + n_peers);
+    if (peer_dst_offset) ctx->dst_offset.assign(peer_dst_offset, peer_dst_offset + n_peers);
+    CgEngineConfig cfg{};
+    cfg.index_dtype = index_dtype;
+    cfg.data = data;
+    cfg.indices = indices;
+    cfg.indptr = indptr;
+    cfg.nnz = nnz;
+    cfg.n = n_owned;
+    cfg.n_halo = n_halo;
+    cfg.preconditioned = preconditioned != 0;
+    cfg.comm = comm_mode;
+    cfg.rank = rank;
+    cfg.world = world;
+    cfg.nccl_comm = nccl_comm;
+    cfg.n_peers = n_peers;
+    cfg.peers = ctx->peers.data();
+    cfg.send_counts = ctx->send_counts.data();
+    cfg.recv_counts = ctx->recv_counts.data();
+    cfg.send_idx = send_idx;
+    cfg.peer_dst_offset = ctx->dst_offset.empty() ? nullptr : ctx->dst_offset.data();
+    ctx->engine = cg_engine_create(cfg, as_stream(stream));
+    *out = ctx.release();
+  });
+}
+
+int msx_cg_context_ipc_handles(msx_cg_context *ctx, void *out, int64_t size) {
+  return guarded([&] {
+    require(ctx && out && size >= 128, MSX_ERR_INVALID, "msx_cg_context_ipc_handles needs a 128-byte buffer.");
+    cg_engine_ipc_handles(ctx->engine, out);
+  });
+}
+
+int msx_cg_context_connect(msx_cg_context *ctx, const void *all_handles, int64_t size) {
+  return guarded([&] {
+    require(ctx && all_handles, MSX_ERR_INVALID, "msx_cg_context_connect: null argument.");
+    require(size >= 128 * (int64_t)ctx->world, MSX_ERR_INVALID, "msx_cg_context_connect: need world x 128 bytes.");
+    cg_engine_connect(ctx->engine, all_handles);
+  });
+}
+
+int msx_cg_context_solve(msx_cg_context *ctx, const float *b, const float *x0, const float *inv_diag, float *x_out,
+                         float rtol, float atol, int32_t maxiter, int32_t *info, float *residual, int32_t *iterations,
+                         void *stream) {
+  return guarded([&] {
+    require(ctx != nullptr, MSX_ERR_INVALID, "context must not be null.");
+    require(maxiter >= 0, MSX_ERR_INVALID, "csr_cg maxiter must be non-negative.");
+    require(b && x0 && x_out && info && residual && iterations, MSX_ERR_INVALID, "csr_cg: null argument.");
+    CgResult r = cg_engine_solve(ctx->engine, b, x0, inv_diag, x_out, rtol, atol, maxiter, as_stream(stream));
+    *info = r.info;
+    *residual = r.residual;
+    *iterations = r.iterations;
+  });
+}
+
+int msx_cg_context_destroy(msx_cg_context *ctx) {
+  return guarded([&] { delete ctx; });
 }
 
 }  // extern "C"

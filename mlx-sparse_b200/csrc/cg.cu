@@ -23,6 +23,7 @@
 // and launched back to back; the host reads the status once per batch.
 // Matrices with rows longer than the CTA bin (split into chunks) run the plain
 // SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
+#include <cstring>
 #include <vector>
 #if defined(MSX_HAVE_NCCL)
 #include <nccl.h>
@@ -434,6 +435,123 @@ __global__ void halo_pack_kernel(const float *__restrict__ v, const int *__restr
   if (i < n) out[i] = v[idx[i]];
 }
 
+// ---- peer-memory communication (one node, NVLink) -------------------------------
+constexpr long long kPeerPollLimit = 1ll << 24;
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// All-reduce of st->red (4 doubles) over `world` ranks through their mailboxes,
+// then the decision `which`. One warp; thread q talks to rank q. The sum runs
+// in rank order, so every rank computes identical scalars.
+__global__ void p2p_allreduce_decide_kernel(CgState *st, CommState *cs, Mailbox *mine, Mailbox *const *peers,
+                                            int rank, int world, int which, int kind, float rtol, float atol) {
+  if (which != 0 && st->status != kStatusRunning) return;  // identical on every rank
+  __shared__ unsigned long long epoch;
+  __shared__ int timed_out;
+  const int q = threadIdx.x;
+  if (q == 0) {
+    epoch = cs->ar_epoch + 1;
+    cs->ar_epoch = epoch;
+    timed_out = 0;
+  }
+  __syncwarp();
+  const int slot = (int)(epoch & 1);
+  if (q < world) {
+    Mailbox *pm = q == rank ? mine : peers[q];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) pm->red[slot][rank][c] = st->red[c];
+    __threadfence_system();
+    st_release_sys(&pm->red_epoch[rank], epoch);
+  }
+  __syncwarp();
+  if (q < world) {
+    long long polls = 0;
+    while (ld_acquire_sys(&mine->red_epoch[q]) < epoch) {
+      if (++polls > kPeerPollLimit) {
+        timed_out = 1;
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  if (q == 0) {
+    if (timed_out) {
+      cs->error = 1;
+      st->status = -4;  // communication timeout (not a reference status)
+      return;
+    }
+    double sum[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int r = 0; r < world; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sum[c] += *((volatile double *)&mine->red[slot][r][c]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) st->red[c] = sum[c];
+    switch (which) {
+    case 0: decide_init(st, kind, rtol, atol); break;
+    case 1: decide_spmv(st, kind); break;
+    case 2: decide_update(st, kind); break;
+    default: decide_pupdate(st); break;
+    }
+  }
+}
+
+struct PeerSend {
+  float *dst[kMaxRanks];      // peer p buffer + landing offset
+  long long off[kMaxRanks + 1];  // prefix of send counts
+  int peer[kMaxRanks];
+  int n_peers;
+};
+
+// Writes this rank's halo entries straight into the peers' p buffers, then
+// (last CTA) raises this rank's halo flag in every peer's mailbox.
+__global__ void p2p_halo_push_kernel(const CgState *st, CommState *cs, const float *__restrict__ v,
+                                     const int *__restrict__ idx, PeerSend ps, Mailbox *const *peers, int rank) {
+  if (st->status != kStatusRunning) return;
+  const long long n = ps.off[ps.n_peers];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int k = 0;
+    while (k + 1 < ps.n_peers && i >= ps.off[k + 1]) ++k;
+    ps.dst[k][i - ps.off[k]] = v[idx[i]];
+  }
+  __threadfence_system();
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&cs->halo_counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    cs->halo_counter = 0;
+    const unsigned long long epoch = cs->halo_epoch + 1;
+    cs->halo_epoch = epoch;
+    __threadfence_system();
+    for (int k = 0; k < ps.n_peers; ++k) st_release_sys(&peers[ps.peer[k]]->halo_epoch[rank], epoch);
+  }
+}
+
+// Waits until every peer this rank receives halo entries from has pushed
+// this iteration's entries (epoch flags), bounded.
+__global__ void p2p_halo_wait_kernel(CgState *st, CommState *cs, const Mailbox *mine, const int *recv_peers,
+                                     int n_recv) {
+  if (st->status != kStatusRunning) return;
+  const unsigned long long epoch = cs->halo_epoch;  // pushed by this rank just before
+  for (int k = 0; k < n_recv; ++k) {
+    long long polls = 0;
+    while (ld_acquire_sys(&mine->halo_epoch[recv_peers[k]]) < epoch) {
+      if (++polls > kPeerPollLimit) {
+        cs->error = 1;
+        st->status = -4;
+        return;
+      }
+    }
+  }
+}
+
 int elementwise_grid(int64_t n) {
   static thread_local int dev_cached = -1, sms = 0;
   int dev = 0;
@@ -449,222 +567,378 @@ int elementwise_grid(int64_t n) {
 
 }  // namespace
 
-CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
-  const int kind = prob.inv_diag ? kPCG : kCG;
-  const int64_t n = prob.n;
-  const CgDist *dist = prob.dist;
-  const bool decide = dist == nullptr;
-#if !defined(MSX_HAVE_NCCL)
-  if (dist) fail(MSX_ERR_RUNTIME, "this build has no NCCL: multi-GPU CG is unavailable.");
-#endif
-  // A private stream: graphs cannot be captured on the legacy default stream.
-  cudaStream_t s;
-  MSX_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-  struct StreamGuard {
-    cudaStream_t s;
-    ~StreamGuard() { cudaStreamDestroy(s); }
-  } sguard{s};
-  cudaEvent_t ev;
-  MSX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  struct EventGuard {
-    cudaEvent_t e;
-    ~EventGuard() { cudaEventDestroy(e); }
-  } eguard{ev};
-  MSX_CUDA(cudaEventRecord(ev, user_stream));
-  MSX_CUDA(cudaStreamWaitEvent(s, ev, 0));
-
-  // Row-length bins of the matrix (built once per solve, in stream scratch).
-  std::vector<std::unique_ptr<Scratch>> keep;
+struct CgEngine {
+  CgEngineConfig cfg{};
+  int kind = kCG;
+  int64_t n = 0, n_cols = 0;
+  int device = 0;
   BinnedPlan plan;
-  build_binned_plan(prob.index_dtype, prob.indptr, n, prob.nnz, s,
-                    [&](size_t bytes) -> void * {
-                      keep.emplace_back(new Scratch(bytes, s));
-                      return keep.back()->ptr;
-                    },
-                    plan);
-  const bool fused = plan.n_long == 0;
-  const int red_grid = elementwise_grid(n);
-  int64_t spmv_grid_n = 0;
-  dispatch_index(prob.index_dtype, [&](auto ityp) {
-    using I = decltype(ityp);
-    spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(plan), binned_grid<float, I, NoEpilogue>(plan));
-  });
-  const int64_t max_grid = std::max<int64_t>(red_grid, spmv_grid_n);
-
-  // scratch layout
-  const size_t vec = sizeof(float) * (size_t)std::max<int64_t>(n, 1);
-  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
-  size_t off = 0;
-  const size_t o_state = off; off += al(sizeof(CgState));
-  const size_t o_part = off;  off += al(sizeof(double) * 4 * max_grid);
-  const size_t o_carry = off; off += al(sizeof(float) * std::max<int64_t>(plan.n_chunks, 1));
-  const size_t o_r = off;     off += al(vec);
-  const size_t o_z = off;     off += al(kind == kPCG ? vec : 0);
-  const size_t o_p = off;     off += al(sizeof(float) * (size_t)std::max<int64_t>(prob.n_cols, 1));
-  const size_t o_ap = off;    off += al(vec);
+  bool fused = true;
+  int red_grid = 1;
+  void *plan_mem = nullptr;
+  void *mem = nullptr;       // state, partials, vectors (one allocation)
+  float *p = nullptr;        // own allocation (IPC-exported in P2P mode)
+  Mailbox *mbox = nullptr;   // own allocation (IPC-exported in P2P mode)
+  CgState *st = nullptr;
+  CommState *cs = nullptr;
+  double *partials = nullptr;
+  float *carry = nullptr, *r = nullptr, *z = nullptr, *ap = nullptr, *x = nullptr, *b = nullptr, *inv = nullptr;
+  float *sendbuf = nullptr;
   int64_t n_send = 0;
-  if (dist)
-    for (int q = 0; q < dist->n_peers; ++q) n_send += dist->send_counts[q];
-  const size_t o_send = off;  off += al(sizeof(float) * (size_t)std::max<int64_t>(n_send, 1));
-  const size_t o_xh = off;    off += al(dist ? sizeof(float) * (size_t)std::max<int64_t>(prob.n_cols, 1) : 0);
-  Scratch scratch(off, s);
-  char *base = scratch.as<char>();
-  CgState *st = reinterpret_cast<CgState *>(base + o_state);
-  double *partials = reinterpret_cast<double *>(base + o_part);
-  float *carry = reinterpret_cast<float *>(base + o_carry);
-  float *r = reinterpret_cast<float *>(base + o_r);
-  float *z = kind == kPCG ? reinterpret_cast<float *>(base + o_z) : nullptr;
-  float *p = reinterpret_cast<float *>(base + o_p);
-  float *ap = reinterpret_cast<float *>(base + o_ap);
-  float *sendbuf = reinterpret_cast<float *>(base + o_send);
-  float *xh = dist ? reinterpret_cast<float *>(base + o_xh) : nullptr;
+  // P2P
+  Mailbox **peer_mbox_dev = nullptr;  // device array [world]
+  int *recv_peers_dev = nullptr;
+  int n_recv_peers = 0;
+  void *opened[2 * kMaxRanks] = {};
+  PeerSend ps{};
+  bool connected = false;
+  cudaStream_t s = nullptr;
+  cudaEvent_t ev = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int batch = 4;
+  int *status_host = nullptr;
+};
 
-  // Multi-GPU plumbing (all ranks issue the same sequence of collectives).
-  auto exchange = [&](float *v, cudaStream_t q) {
-#if defined(MSX_HAVE_NCCL)
-    if (!dist) return;
-    if (n_send > 0) {
-      halo_pack_kernel<<<(unsigned)ceil_div(n_send, 256), 256, 0, q>>>(v, dist->send_idx, sendbuf, n_send);
-      MSX_CHECK_LAUNCH();
-    }
-    ncclComm_t comm = static_cast<ncclComm_t>(dist->comm);
-    auto nccl = [](ncclResult_t r) {
-      if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
-    };
-    nccl(ncclGroupStart());
-    int64_t so = 0, ro = 0;
-    for (int k = 0; k < dist->n_peers; ++k) {
-      if (dist->send_counts[k] > 0)
-        nccl(ncclSend(sendbuf + so, (size_t)dist->send_counts[k], ncclFloat, dist->peers[k], comm, q));
-      if (dist->recv_counts[k] > 0)
-        nccl(ncclRecv(v + n + ro, (size_t)dist->recv_counts[k], ncclFloat, dist->peers[k], comm, q));
-      so += dist->send_counts[k];
-      ro += dist->recv_counts[k];
-    }
-    nccl(ncclGroupEnd());
-#else
-    (void)v;
-    (void)q;
-#endif
-  };
-  auto reduce_decide = [&](int which, cudaStream_t q) {
-#if defined(MSX_HAVE_NCCL)
-    if (!dist) return;
-    ncclResult_t r = ncclAllReduce(st->red, st->red, 4, ncclDouble, ncclSum, static_cast<ncclComm_t>(dist->comm), q);
-    if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
-    decide_kernel<<<1, 1, 0, q>>>(st, which, kind, prob.rtol, prob.atol);
+namespace {
+
+void engine_exchange(CgEngine *e, float *v, cudaStream_t q) {
+  const CgEngineConfig &c = e->cfg;
+  if (c.comm == kCommP2p) {
+    if (!e->connected) fail(MSX_ERR_RUNTIME, "CG context: peers are not connected.");
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(std::max<int64_t>(e->n_send, 1), 256), 256));
+    p2p_halo_push_kernel<<<grid, 256, 0, q>>>(e->st, e->cs, v, c.send_idx, e->ps, e->peer_mbox_dev, c.rank);
     MSX_CHECK_LAUNCH();
-#else
-    (void)which;
-    (void)q;
-#endif
+    p2p_halo_wait_kernel<<<1, 1, 0, q>>>(e->st, e->cs, e->mbox, e->recv_peers_dev, e->n_recv_peers);
+    MSX_CHECK_LAUNCH();
+    return;
+  }
+#if defined(MSX_HAVE_NCCL)
+  if (c.comm != kCommNccl) return;
+  if (e->n_send > 0) {
+    halo_pack_kernel<<<(unsigned)ceil_div(e->n_send, 256), 256, 0, q>>>(v, c.send_idx, e->sendbuf, e->n_send);
+    MSX_CHECK_LAUNCH();
+  }
+  ncclComm_t comm = static_cast<ncclComm_t>(c.nccl_comm);
+  auto nccl = [](ncclResult_t r) {
+    if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
   };
+  nccl(ncclGroupStart());
+  int64_t so = 0, ro = 0;
+  for (int k = 0; k < c.n_peers; ++k) {
+    if (c.send_counts[k] > 0)
+      nccl(ncclSend(e->sendbuf + so, (size_t)c.send_counts[k], ncclFloat, c.peers[k], comm, q));
+    if (c.recv_counts[k] > 0)
+      nccl(ncclRecv(v + e->n + ro, (size_t)c.recv_counts[k], ncclFloat, c.peers[k], comm, q));
+    so += c.send_counts[k];
+    ro += c.recv_counts[k];
+  }
+  nccl(ncclGroupEnd());
+#else
+  (void)v;
+  (void)q;
+  if (c.comm == kCommNccl) fail(MSX_ERR_RUNTIME, "this build has no NCCL.");
+#endif
+}
 
+// After a reduction kernel left local sums in st->red: combine over ranks and
+// decide. Single GPU: the kernel's last CTA already decided.
+void engine_reduce_decide(CgEngine *e, int which, float rtol, float atol, cudaStream_t q) {
+  const CgEngineConfig &c = e->cfg;
+  if (c.comm == kCommP2p) {
+    p2p_allreduce_decide_kernel<<<1, 32, 0, q>>>(e->st, e->cs, e->mbox, e->peer_mbox_dev, c.rank, c.world, which,
+                                                 e->kind, rtol, atol);
+    MSX_CHECK_LAUNCH();
+    return;
+  }
+#if defined(MSX_HAVE_NCCL)
+  if (c.comm != kCommNccl) return;
+  ncclResult_t r = ncclAllReduce(e->st->red, e->st->red, 4, ncclDouble, ncclSum, static_cast<ncclComm_t>(c.nccl_comm), q);
+  if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
+  decide_kernel<<<1, 1, 0, q>>>(e->st, which, e->kind, rtol, atol);
+  MSX_CHECK_LAUNCH();
+#else
+  (void)which;
+  (void)rtol;
+  (void)atol;
+  (void)q;
+#endif
+}
+
+void engine_iteration(CgEngine *e, cudaStream_t q) {
+  const CgEngineConfig &c = e->cfg;
+  const bool decide = c.comm == kCommNone;
+  const int kind = e->kind;
+  engine_exchange(e, e->p, q);
+  if (e->fused) {
+    dispatch_index(c.index_dtype, [&](auto ityp) {
+      using I = decltype(ityp);
+      DotsEpilogue epi{e->p, e->partials, e->st, kind, decide, 0.0, 0.0, 0.0, 0.0};
+      launch_spmv_binned<float, I, DotsEpilogue>(e->plan, c.data, static_cast<const I *>(c.indices),
+                                                 static_cast<const I *>(c.indptr), e->p, e->ap, e->carry, epi, q);
+    });
+  } else {
+    spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p, e->ap, e->carry, q);
+    dots_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->p, e->ap, e->n, e->partials, e->st, decide);
+    MSX_CHECK_LAUNCH();
+  }
+  engine_reduce_decide(e, 1, 0.f, 0.f, q);
+  update_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->x, e->r, e->z, e->p, e->ap, e->inv, e->n, e->partials, e->st,
+                                                 decide);
+  MSX_CHECK_LAUNCH();
+  engine_reduce_decide(e, 2, 0.f, 0.f, q);
+  pupdate_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->r, e->z, e->p, e->n, e->partials, e->st, decide);
+  MSX_CHECK_LAUNCH();
+  if (kind == kCG) engine_reduce_decide(e, 3, 0.f, 0.f, q);
+}
+
+template <typename T> T *bump(char *&cur, size_t count) {
+  T *p = reinterpret_cast<T *>(cur);
+  cur += (sizeof(T) * count + 255) & ~size_t(255);
+  return p;
+}
+
+}  // namespace
+
+CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) {
+  if (cfg.world > kMaxRanks) fail(MSX_ERR_INVALID, "CG: at most 8 ranks (one node).");
+#if !defined(MSX_HAVE_NCCL)
+  if (cfg.comm == kCommNccl) fail(MSX_ERR_RUNTIME, "this build has no NCCL: multi-GPU CG over NCCL is unavailable.");
+#endif
+  // destroyed (buffers freed) if anything below throws
+  std::unique_ptr<CgEngine, void (*)(CgEngine *)> e(new CgEngine(), cg_engine_destroy);
+  CgEngine *E = e.get();
+  E->cfg = cfg;
+  E->kind = cfg.preconditioned ? kPCG : kCG;
+  E->n = cfg.n;
+  E->n_cols = cfg.n + cfg.n_halo;
+  MSX_CUDA(cudaGetDevice(&E->device));
+  MSX_CUDA(cudaStreamCreateWithFlags(&E->s, cudaStreamNonBlocking));
+  MSX_CUDA(cudaEventCreateWithFlags(&E->ev, cudaEventDisableTiming));
+  MSX_CUDA(cudaEventRecord(E->ev, user_stream));
+  MSX_CUDA(cudaStreamWaitEvent(E->s, E->ev, 0));
+  cudaStream_t s = E->s;
+  build_binned_plan(cfg.index_dtype, cfg.indptr, E->n, cfg.nnz, s,
+                    [&](size_t bytes) -> void * {
+                      MSX_CUDA(cudaMalloc(&E->plan_mem, bytes));
+                      return E->plan_mem;
+                    },
+                    E->plan);
+  E->fused = E->plan.n_long == 0;
+  E->red_grid = elementwise_grid(E->n);
+  int64_t spmv_grid_n = 0;
+  dispatch_index(cfg.index_dtype, [&](auto ityp) {
+    using I = decltype(ityp);
+    spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(E->plan), binned_grid<float, I, NoEpilogue>(E->plan));
+  });
+  const int64_t max_grid = std::max<int64_t>(E->red_grid, spmv_grid_n);
+  for (int k = 0; k < cfg.n_peers; ++k) E->n_send += cfg.send_counts[k];
+  const size_t vec = (size_t)std::max<int64_t>(E->n, 1);
+  size_t bytes = 0;
+  auto sz = [](size_t b) { return (b + 255) & ~size_t(255); };
+  bytes += sz(sizeof(CgState)) + sz(sizeof(CommState)) + sz(sizeof(double) * 4 * max_grid) +
+           sz(sizeof(float) * std::max<int64_t>(E->plan.n_chunks, 1)) + 6 * sz(sizeof(float) * vec) +
+           sz(sizeof(float) * std::max<int64_t>(E->n_send, 1)) + sz(sizeof(Mailbox *) * kMaxRanks) +
+           sz(sizeof(int) * kMaxRanks);
+  MSX_CUDA(cudaMalloc(&E->mem, bytes));
+  MSX_CUDA(cudaMemsetAsync(E->mem, 0, bytes, s));
+  char *cur = static_cast<char *>(E->mem);
+  E->st = bump<CgState>(cur, 1);
+  E->cs = bump<CommState>(cur, 1);
+  E->partials = bump<double>(cur, 4 * max_grid);
+  E->carry = bump<float>(cur, std::max<int64_t>(E->plan.n_chunks, 1));
+  E->r = bump<float>(cur, vec);
+  E->z = bump<float>(cur, vec);
+  E->ap = bump<float>(cur, vec);
+  E->x = bump<float>(cur, vec);
+  E->b = bump<float>(cur, vec);
+  E->inv = bump<float>(cur, vec);
+  E->sendbuf = bump<float>(cur, std::max<int64_t>(E->n_send, 1));
+  E->peer_mbox_dev = bump<Mailbox *>(cur, kMaxRanks);
+  E->recv_peers_dev = bump<int>(cur, kMaxRanks);
+  MSX_CUDA(cudaMalloc(&E->p, sizeof(float) * (size_t)std::max<int64_t>(E->n_cols, 1)));
+  MSX_CUDA(cudaMemsetAsync(E->p, 0, sizeof(float) * (size_t)std::max<int64_t>(E->n_cols, 1), s));
+  MSX_CUDA(cudaMalloc(&E->mbox, sizeof(Mailbox)));
+  MSX_CUDA(cudaMemsetAsync(E->mbox, 0, sizeof(Mailbox), s));
+  if (!cfg.preconditioned) E->z = nullptr, E->inv = nullptr;
+  MSX_CUDA(cudaMallocHost(&E->status_host, sizeof(int)));
+  // receive peers (P2P halo waits)
+  if (cfg.comm == kCommP2p) {
+    int recv[kMaxRanks];
+    for (int k = 0; k < cfg.n_peers; ++k)
+      if (cfg.recv_counts[k] > 0) recv[E->n_recv_peers++] = cfg.peers[k];
+    MSX_CUDA(cudaMemcpyAsync(E->recv_peers_dev, recv, sizeof(int) * E->n_recv_peers, cudaMemcpyHostToDevice, s));
+  }
+  // Iterations per graph launch: about a millisecond of work per batch (even).
+  const double bytes_per_iter = 8.0 * cfg.nnz + 56.0 * E->n;
+  int batch = (int)std::max(1.0, std::min(64.0, 5.0e9 * 1e-3 / std::max(bytes_per_iter, 1.0)));
+  E->batch = std::max(4, batch);
+  MSX_CUDA(cudaStreamSynchronize(s));
+  return e.release();
+}
+
+void cg_engine_destroy(CgEngine *e) {
+  if (!e) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != e->device) cudaSetDevice(e->device);
+  if (e->s) cudaStreamSynchronize(e->s);
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  for (void *p : e->opened)
+    if (p) cudaIpcCloseMemHandle(p);
+  if (e->status_host) cudaFreeHost(e->status_host);
+  if (e->p) cudaFree(e->p);
+  if (e->mbox) cudaFree(e->mbox);
+  if (e->mem) cudaFree(e->mem);
+  if (e->plan_mem) cudaFree(e->plan_mem);
+  if (e->ev) cudaEventDestroy(e->ev);
+  if (e->s) cudaStreamDestroy(e->s);
+  if (cur != e->device) cudaSetDevice(cur);
+  delete e;
+}
+
+void cg_engine_ipc_handles(CgEngine *e, void *out128) {
+  cudaIpcMemHandle_t h[2];
+  MSX_CUDA(cudaIpcGetMemHandle(&h[0], e->p));
+  MSX_CUDA(cudaIpcGetMemHandle(&h[1], e->mbox));
+  std::memcpy(out128, h, sizeof(h));
+}
+
+void cg_engine_connect(CgEngine *e, const void *all_handles) {
+  const CgEngineConfig &c = e->cfg;
+  const auto *hs = static_cast<const cudaIpcMemHandle_t *>(all_handles);
+  Mailbox *mboxes[kMaxRanks] = {};
+  float *ps[kMaxRanks] = {};
+  for (int q = 0; q < c.world; ++q) {
+    if (q == c.rank) {
+      mboxes[q] = e->mbox;
+      ps[q] = e->p;
+      continue;
+    }
+    void *pp = nullptr, *mb = nullptr;
+    MSX_CUDA(cudaIpcOpenMemHandle(&pp, hs[2 * q], cudaIpcMemLazyEnablePeerAccess));
+    e->opened[2 * q] = pp;
+    MSX_CUDA(cudaIpcOpenMemHandle(&mb, hs[2 * q + 1], cudaIpcMemLazyEnablePeerAccess));
+    e->opened[2 * q + 1] = mb;
+    mboxes[q] = static_cast<Mailbox *>(mb);
+    ps[q] = static_cast<float *>(pp);
+  }
+  MSX_CUDA(cudaMemcpyAsync(e->peer_mbox_dev, mboxes, sizeof(mboxes), cudaMemcpyHostToDevice, e->s));
+  PeerSend ps_{};
+  long long off = 0;
+  int np = 0;
+  for (int k = 0; k < c.n_peers; ++k) {
+    if (c.send_counts[k] == 0) continue;
+    ps_.dst[np] = ps[c.peers[k]] + c.peer_dst_offset[k];
+    ps_.peer[np] = c.peers[k];
+    ps_.off[np] = off;
+    off += c.send_counts[k];
+    ++np;
+  }
+  ps_.off[np] = off;
+  ps_.n_peers = np;
+  // every halo peer is flagged, also those that get nothing from this rank
+  // (their wait lists only contain ranks that send to them, so this is enough)
+  e->ps = ps_;
+  MSX_CUDA(cudaStreamSynchronize(e->s));
+  e->connected = true;
+}
+
+CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, const float *inv_in, float *x_out,
+                         float rtol, float atol, int maxiter, cudaStream_t user_stream) {
+  const CgEngineConfig &c = e->cfg;
+  cudaStream_t s = e->s;
+  const int64_t n = e->n;
+  MSX_CUDA(cudaEventRecord(e->ev, user_stream));
+  MSX_CUDA(cudaStreamWaitEvent(s, e->ev, 0));
+  MSX_CUDA(cudaMemcpyAsync(e->b, b_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  MSX_CUDA(cudaMemcpyAsync(e->x, x0_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  MSX_CUDA(cudaMemcpyAsync(e->p, x0_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  if (e->kind == kPCG) MSX_CUDA(cudaMemcpyAsync(e->inv, inv_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   CgState init{};
   init.status = kStatusRunning;
   init.it = 1;
-  init.maxiter = prob.maxiter;
-  MSX_CUDA(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
-  MSX_CUDA(cudaMemcpyAsync(prob.x, prob.x0, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  init.maxiter = maxiter;
+  MSX_CUDA(cudaMemcpyAsync(e->st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
 
-  // r0 = b - A x0 (the halo of x0 comes from its owners first)
-  const float *x_in = prob.x;
-  if (dist) {
-    MSX_CUDA(cudaMemcpyAsync(xh, prob.x0, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
-    exchange(xh, s);
-    x_in = xh;
-  }
-  spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, x_in, ap, carry, s);
-  init_kernel<<<red_grid, kThreads, 0, s>>>(kind, prob.b, prob.x, ap, prob.inv_diag, r, z, p, n, partials, st,
-                                            prob.rtol, prob.atol, decide);
+  // r0 = b - A x0 (x0 staged in p, whose halo the exchange fills)
+  engine_exchange(e, e->p, s);
+  spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p, e->ap, e->carry, s);
+  const bool decide = c.comm == kCommNone;
+  init_kernel<<<e->red_grid, kThreads, 0, s>>>(e->kind, e->b, e->x, e->ap, e->inv, e->r, e->z, e->p, n, e->partials,
+                                               e->st, rtol, atol, decide);
   MSX_CHECK_LAUNCH();
-  reduce_decide(0, s);
-
+  engine_reduce_decide(e, 0, rtol, atol, s);
   CgState host{};
-  MSX_CUDA(cudaMemcpyAsync(&host, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
+  MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
 
-  auto enqueue_iteration = [&](cudaStream_t q) {
-    exchange(p, q);
-    if (fused) {
-      dispatch_index(prob.index_dtype, [&](auto ityp) {
-        using I = decltype(ityp);
-        DotsEpilogue epi{p, partials, st, kind, decide, 0.0, 0.0, 0.0, 0.0};
-        launch_spmv_binned<float, I, DotsEpilogue>(plan, prob.data, static_cast<const I *>(prob.indices),
-                                                   static_cast<const I *>(prob.indptr), p, ap, carry, epi, q);
-      });
-    } else {
-      spmv_binned_run(MSX_F32, prob.index_dtype, plan, prob.data, prob.indices, prob.indptr, p, ap, carry, q);
-      dots_kernel<<<red_grid, kThreads, 0, q>>>(kind, p, ap, n, partials, st, decide);
-      MSX_CHECK_LAUNCH();
-    }
-    reduce_decide(1, q);
-    update_kernel<<<red_grid, kThreads, 0, q>>>(kind, prob.x, r, z, p, ap, prob.inv_diag, n, partials, st, decide);
-    MSX_CHECK_LAUNCH();
-    reduce_decide(2, q);
-    pupdate_kernel<<<red_grid, kThreads, 0, q>>>(kind, r, z, p, n, partials, st, decide);
-    MSX_CHECK_LAUNCH();
-    if (kind == kCG) reduce_decide(3, q);
-  };
-
   if (host.status == kStatusRunning) {
-    // Iterations per graph launch: about a millisecond of work per batch.
-    const double bytes_per_iter = 8.0 * prob.nnz + 56.0 * n;
-    int batch = (int)std::max(1.0, std::min(64.0, 5.0e9 * 1e-3 / std::max(bytes_per_iter, 1.0)));
-    batch = std::max(4, batch);
-    batch = std::min(batch, std::max(prob.maxiter, 1));
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    MSX_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    try {
-      for (int k = 0; k < batch; ++k) enqueue_iteration(s);
-    } catch (...) {
-      cudaStreamEndCapture(s, &graph);
-      if (graph) cudaGraphDestroy(graph);
-      throw;
-    }
-    MSX_CUDA(cudaStreamEndCapture(s, &graph));
-    struct GraphGuard {
-      cudaGraph_t g;
-      cudaGraphExec_t e;
-      ~GraphGuard() {
-        if (e) cudaGraphExecDestroy(e);
+    if (!e->exec) {
+      MSX_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      try {
+        for (int k = 0; k < e->batch; ++k) engine_iteration(e, s);
+      } catch (...) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(s, &g);
         if (g) cudaGraphDestroy(g);
+        throw;
       }
-    } gguard{graph, nullptr};
-    MSX_CUDA(cudaGraphInstantiate(&exec, graph, 0));
-    gguard.e = exec;
-    int *status_host = nullptr;
-    MSX_CUDA(cudaMallocHost(&status_host, sizeof(int)));
-    struct HostGuard {
-      int *p;
-      ~HostGuard() { cudaFreeHost(p); }
-    } hguard{status_host};
+      MSX_CUDA(cudaStreamEndCapture(s, &e->graph));
+      MSX_CUDA(cudaGraphInstantiate(&e->exec, e->graph, 0));
+    }
     int64_t launched = 0;
     while (true) {
-      MSX_CUDA(cudaGraphLaunch(exec, s));
-      launched += batch;
-      MSX_CUDA(cudaMemcpyAsync(status_host, &st->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+      MSX_CUDA(cudaGraphLaunch(e->exec, s));
+      launched += e->batch;
+      MSX_CUDA(cudaMemcpyAsync(e->status_host, &e->st->status, sizeof(int), cudaMemcpyDeviceToHost, s));
       MSX_CUDA(cudaStreamSynchronize(s));
-      if (*status_host != kStatusRunning || launched >= prob.maxiter) break;
+      if (*e->status_host != kStatusRunning || launched >= maxiter) break;
     }
-    MSX_CUDA(cudaMemcpyAsync(&host, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
+    MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
     MSX_CUDA(cudaStreamSynchronize(s));
   }
-
+  MSX_CUDA(cudaMemcpyAsync(x_out, e->x, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  MSX_CUDA(cudaEventRecord(e->ev, s));
+  MSX_CUDA(cudaStreamWaitEvent(user_stream, e->ev, 0));
+  if (host.status == kStatusRunning) fail(MSX_ERR_RUNTIME, "CG solve ended without a status (internal error).");
+  if (host.status == -4) fail(MSX_ERR_RUNTIME, "CG: a peer did not answer (communication timeout).");
   CgResult res{};
   res.info = host.status;
   res.iterations = host.completed;
-  if (kind == kCG) {
-    res.residual = (float)std::sqrt(std::max(host.rr, 0.0));
-  } else {
-    res.residual = std::sqrt(std::max(host.true_rr, 0.0f));
-  }
-  if (host.status == kStatusRunning) fail(MSX_ERR_RUNTIME, "CG solve ended without a status (internal error).");
-  // order the caller's stream after the solve
-  MSX_CUDA(cudaEventRecord(ev, s));
-  MSX_CUDA(cudaStreamWaitEvent(user_stream, ev, 0));
+  res.residual = e->kind == kCG ? (float)std::sqrt(std::max(host.rr, 0.0)) : std::sqrt(std::max(host.true_rr, 0.0f));
   return res;
+}
+
+CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
+  CgEngineConfig cfg{};
+  cfg.index_dtype = prob.index_dtype;
+  cfg.data = prob.data;
+  cfg.indices = prob.indices;
+  cfg.indptr = prob.indptr;
+  cfg.nnz = prob.nnz;
+  cfg.n = prob.n;
+  cfg.n_halo = prob.n_cols - prob.n;
+  cfg.preconditioned = prob.inv_diag != nullptr;
+  cfg.comm = kCommNone;
+  cfg.rank = 0;
+  cfg.world = 1;
+  if (prob.dist) {
+    cfg.comm = kCommNccl;
+    cfg.nccl_comm = prob.dist->comm;
+    cfg.n_peers = prob.dist->n_peers;
+    cfg.peers = prob.dist->peers;
+    cfg.send_counts = prob.dist->send_counts;
+    cfg.recv_counts = prob.dist->recv_counts;
+    cfg.send_idx = prob.dist->send_idx;
+  }
+  CgEngine *e = cg_engine_create(cfg, user_stream);
+  struct Guard {
+    CgEngine *e;
+    ~Guard() { cg_engine_destroy(e); }
+  } guard{e};
+  return cg_engine_solve(e, prob.b, prob.x0, prob.inv_diag, prob.x, prob.rtol, prob.atol, prob.maxiter, user_stream);
 }
 
 }  // namespace msx

@@ -28,6 +28,26 @@ struct CgState {
   int pad[3];
 };
 
+constexpr int kMaxRanks = 8;  // one node
+
+// Peer-memory mailbox of one rank (IPC-exported): the fp64 partial sums every
+// rank sends it (two slots, alternating by epoch) and the epoch flags of the
+// all-reduce and halo exchanges, written by the senders.
+struct Mailbox {
+  double red[2][kMaxRanks][4];
+  unsigned long long red_epoch[kMaxRanks];
+  unsigned long long halo_epoch[kMaxRanks];
+};
+
+// Counters that persist across solves of one context (never reset, so flags
+// in peers' mailboxes stay monotonic).
+struct CommState {
+  unsigned long long ar_epoch;
+  unsigned long long halo_epoch;
+  unsigned int halo_counter;
+  int error;  // 1: a peer wait timed out
+};
+
 // Multi-GPU layout of one rank (row slab with halo columns; see
 // mlx_sparse/distributed.py). Host arrays except send_idx (device).
 struct CgDist {
@@ -54,7 +74,7 @@ struct CgProblem {
   float *x;
   float rtol, atol;
   int maxiter;
-  const CgDist *dist = nullptr;  // null: single GPU
+  const CgDist *dist = nullptr;  // null: single GPU (NCCL when set)
 };
 
 struct CgResult {
@@ -62,6 +82,39 @@ struct CgResult {
   float residual;
   int iterations;
 };
+
+enum CommMode { kCommNone = 0, kCommNccl = 1, kCommP2p = 2 };
+
+// A persistent solver for one matrix (and one rank): plan, buffers and the
+// captured iteration graph are built once and reused by every solve.
+struct CgEngine;
+struct CgEngineConfig {
+  int index_dtype;
+  const float *data;
+  const void *indices;
+  const void *indptr;
+  int64_t nnz;
+  int64_t n;       // owned rows
+  int64_t n_halo;  // halo columns
+  bool preconditioned;
+  int comm;        // CommMode
+  int rank, world;
+  void *nccl_comm;
+  int n_peers;
+  const int *peers;
+  const int64_t *send_counts;
+  const int64_t *recv_counts;
+  const int *send_idx;             // device
+  const int64_t *peer_dst_offset;  // host, P2P: where this rank's entries land in each peer's p
+};
+CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t stream);
+void cg_engine_destroy(CgEngine *e);
+// P2P: 2 IPC handles (p buffer, mailbox), 64 bytes each.
+void cg_engine_ipc_handles(CgEngine *e, void *out128);
+void cg_engine_connect(CgEngine *e, const void *all_handles /* world x 128 bytes */);
+CgResult cg_engine_solve(CgEngine *e, const float *b, const float *x0, const float *inv_diag, float *x_out,
+                         float rtol, float atol, int maxiter, cudaStream_t stream);
+
 
 // Single-GPU solve on `stream`; synchronises the stream at the end.
 CgResult cg_solve(const CgProblem &prob, cudaStream_t stream);

@@ -42,6 +42,7 @@ class CSRArray:
     sorted_indices: bool = False
     has_canonical_format: bool = False
     _plan: list = field(default_factory=list, repr=False, compare=False)
+    _solvers: dict = field(default_factory=dict, repr=False, compare=False)
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "shape", normalize_shape(self.shape))
@@ -73,6 +74,14 @@ class CSRArray:
         if not self._plan:
             self._plan.append(_native.SpmvPlan(self.indptr.contiguous(), self.shape[0], self.nnz))
         return self._plan[0]
+
+    def cg_context(self, preconditioned: bool) -> "_native.CgContext":
+        """The cached persistent CG solver of this matrix (built on first use)."""
+        key = bool(preconditioned)
+        if key not in self._solvers:
+            self._solvers[key] = _native.CgContext(self.data.contiguous(), self.indices.contiguous(),
+                                                   self.indptr.contiguous(), self.shape[0], 0, key)
+        return self._solvers[key]
 
     def canonicalize(self) -> "CSRArray":
         """Sorted indices, duplicates summed; ``self`` if already canonical."""

@@ -65,6 +65,12 @@ def extension():
             L.msx_csr_pcg_jacobi.argtypes = [c_int, p, p, p, i64, p, p, p, p, i64, i64, c_float, c_float,
                                              ctypes.c_int32, p, p, p, p]
         L.msx_csr_diagonal.argtypes = [c_int, c_int, p, p, p, i64, i64, i64, p, p]
+        L.msx_cg_context_create.argtypes = [c_int, p, p, p, i64, i64, i64, c_int, c_int, c_int, c_int, p, c_int, p,
+                                            p, p, p, p, p, ctypes.POINTER(p)]
+        L.msx_cg_context_ipc_handles.argtypes = [p, p, i64]
+        L.msx_cg_context_connect.argtypes = [p, p, i64]
+        L.msx_cg_context_solve.argtypes = [p, p, p, p, p, c_float, c_float, ctypes.c_int32, p, p, p, p]
+        L.msx_cg_context_destroy.argtypes = [p]
         if hasattr(L, "msx_dist_pcg"):
             L.msx_dist_unique_id.argtypes = [p, i64]
             L.msx_dist_comm_create.argtypes = [p, c_int, c_int, ctypes.POINTER(p)]
@@ -189,6 +195,71 @@ def csr_diagonal(data, indices, indptr, shape):
         check(L.msx_csr_diagonal(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
                                  _p(indptr), data.numel(), shape[0], shape[1], _p(out), stream_ptr(dev)))
     return out
+
+
+class CgContext:
+    """A persistent CG solver (``msx_cg_context``): row bins, work buffers and
+    the CUDA graph of the iterations are built once, then every ``solve``
+    only runs the iterations. The matrix arrays are borrowed and must outlive
+    the context."""
+
+    COMM_NONE, COMM_NCCL, COMM_P2P = 0, 1, 2
+
+    def __init__(self, data, indices, indptr, n_owned, n_halo, preconditioned, *, comm=0, rank=0, world=1,
+                 nccl_comm=None, peers=None, send_counts=None, recv_counts=None, send_idx=None,
+                 dst_offset=None):
+        import numpy as np
+
+        L = extension()
+        self.device = data.device
+        self._keep = (data, indices, indptr, send_idx)
+        self._peers = np.ascontiguousarray(peers if peers is not None else [], dtype=np.int32)
+        self._sc = np.ascontiguousarray(send_counts if send_counts is not None else [], dtype=np.int64)
+        self._rc = np.ascontiguousarray(recv_counts if recv_counts is not None else [], dtype=np.int64)
+        self._off = np.ascontiguousarray(dst_offset if dst_offset is not None else [], dtype=np.int64)
+        self.n = int(n_owned)
+        self.world = world
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(L.msx_cg_context_create(
+                INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(), n_owned, n_halo,
+                int(bool(preconditioned)), comm, rank, world, nccl_comm, int(self._peers.shape[0]),
+                self._peers.ctypes.data, self._sc.ctypes.data, self._rc.ctypes.data,
+                _p(send_idx) if send_idx is not None else None,
+                self._off.ctypes.data if self._off.size else None, stream_ptr(self.device), ctypes.byref(h)))
+        self.handle = h
+
+    def ipc_handles(self) -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(extension().msx_cg_context_ipc_handles(self.handle, buf, 128))
+        return bytes(buf.raw)
+
+    def connect(self, all_handles: list) -> None:
+        blob = b"".join(all_handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        with torch.cuda.device(self.device):
+            check(extension().msx_cg_context_connect(self.handle, buf, len(blob)))
+
+    def solve(self, b, x0, inv_diag, *, rtol, atol, maxiter):
+        dev = self.device
+        b = b.to(dev, torch.float32).contiguous()
+        x0 = x0.to(dev, torch.float32).contiguous()
+        inv = None if inv_diag is None else inv_diag.to(dev, torch.float32).contiguous()
+        x = torch.empty(self.n, dtype=torch.float32, device=dev)
+        info, res, its = ctypes.c_int32(), ctypes.c_float(), ctypes.c_int32()
+        with torch.cuda.device(dev):
+            check(extension().msx_cg_context_solve(self.handle, _p(b), _p(x0), _p(inv), _p(x), float(rtol),
+                                                   float(atol), int(maxiter), ctypes.addressof(info),
+                                                   ctypes.addressof(res), ctypes.addressof(its), stream_ptr(dev)))
+        return x, info.value, res.value, its.value
+
+    def __del__(self):
+        try:
+            if self.handle:
+                extension().msx_cg_context_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass
 
 
 def _solver_outputs(dev, n):

@@ -54,6 +54,7 @@ class RowSlab:
     send_counts: np.ndarray  # per peer: owned entries sent to it
     recv_counts: np.ndarray  # per peer: halo entries received from it (in halo order)
     send_idx: np.ndarray     # concatenated per peer: local owned indices to send
+    dst_offset: np.ndarray   # per peer: where this rank's entries start in that peer's local vector
 
     @property
     def n_owned(self) -> int:
@@ -84,7 +85,7 @@ def build_slab(data, indices, indptr, n: int, rank: int, world: int, ranges=None
     local = np.empty(cols.shape[0], dtype=np.int64)
     local[owned] = cols[owned] - r0
     local[~owned] = (r1 - r0) + np.searchsorted(halo_cols, cols[~owned])
-    peers, send_counts, recv_counts, send_idx = [], [], [], []
+    peers, send_counts, recv_counts, send_idx, dst_offset = [], [], [], [], []
     for q in range(world):
         if q == rank:
             continue
@@ -98,6 +99,11 @@ def build_slab(data, indices, indptr, n: int, rank: int, world: int, ranges=None
         recv_counts.append(n_recv)
         send_counts.append(int(needed.size))
         send_idx.append((needed - r0).astype(np.int32))
+        # Peer q's halo is sorted by global column, so this rank's entries
+        # sit after q's owned rows and its halo columns below r0.
+        qc = np.unique(indices[int(indptr[q0]):int(indptr[q1])])
+        below = int(np.count_nonzero((qc < r0) & ((qc < q0) | (qc >= q1))))
+        dst_offset.append((q1 - q0) + below)
     it = indices.dtype
     return RowSlab(
         rank=rank, world=world, r0=r0, r1=r1,
@@ -109,6 +115,7 @@ def build_slab(data, indices, indptr, n: int, rank: int, world: int, ranges=None
         send_counts=np.asarray(send_counts, dtype=np.int64),
         recv_counts=np.asarray(recv_counts, dtype=np.int64),
         send_idx=np.concatenate(send_idx) if send_idx else np.zeros(0, np.int32),
+        dst_offset=np.asarray(dst_offset, dtype=np.int64),
     )
 
 
@@ -169,6 +176,76 @@ class DeviceSlab:
         self.indices = torch.from_numpy(np.ascontiguousarray(slab.indices)).to(device)
         self.indptr = torch.from_numpy(np.ascontiguousarray(slab.indptr)).to(device)
         self.send_idx = torch.from_numpy(np.ascontiguousarray(slab.send_idx, dtype=np.int32)).to(device)
+
+
+class DistCG:
+    """A persistent row-sharded CG / Jacobi PCG solver, one per rank.
+
+    ``comm="p2p"`` (default on one node): every rank maps its peers' search
+    direction and mailbox into its own address space (CUDA IPC handles,
+    exchanged once through ``torch.distributed``); each iteration pushes the
+    halo entries straight into the peers' vectors and reduces the CG scalars
+    through the mailboxes, inside one captured CUDA graph with no host round
+    trip. ``comm="nccl"`` does the same exchange with NCCL send/recv and
+    all-reduce. Plan, buffers and the graph are built once; ``solve`` only
+    runs iterations. Created collectively by all ranks.
+    """
+
+    def __init__(self, A: "DeviceSlab", *, preconditioned: bool, comm: str = "p2p", communicator=None):
+        import torch.distributed as dist
+
+        from mlx_sparse import _native
+
+        s = A.slab
+        if comm not in ("p2p", "nccl"):
+            raise ValueError("comm must be 'p2p' or 'nccl'")
+        if comm == "p2p" and s.world > 8:
+            raise ValueError("peer-memory mode supports at most 8 ranks")
+        if comm == "p2p":
+            # ranks spin on each other's flags: each must own a distinct GPU
+            import torch
+
+            uuids = [None] * s.world
+            dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(A.device).uuid))
+            if len(set(uuids)) != s.world:
+                raise ValueError("peer-memory mode needs one GPU per rank; use comm='nccl'")
+        self.A = A
+        self.n_global = None
+        mode = _native.CgContext.COMM_P2P if comm == "p2p" else _native.CgContext.COMM_NCCL
+        if comm == "nccl" and communicator is None:
+            communicator = Communicator(s.rank, s.world, A.device)
+        self.communicator = communicator
+        self.ctx = _native.CgContext(
+            A.data, A.indices, A.indptr, s.n_owned, s.n_halo, preconditioned, comm=mode, rank=s.rank,
+            world=s.world, nccl_comm=communicator.handle if communicator is not None else None, peers=s.peers,
+            send_counts=s.send_counts, recv_counts=s.recv_counts, send_idx=A.send_idx, dst_offset=s.dst_offset)
+        if comm == "p2p":
+            handles = [None] * s.world
+            dist.all_gather_object(handles, self.ctx.ipc_handles())
+            self.ctx.connect(handles)
+            dist.barrier()
+
+    def solve(self, b_local, *, x0_local=None, inv_diag_local=None, rtol=1e-5, atol=0.0, maxiter=None):
+        import torch
+
+        n = self.A.slab.n_owned
+        dev = self.A.device
+        if maxiter is None:
+            if self.n_global is None:
+                import torch.distributed as dist
+
+                t = torch.tensor([n], dtype=torch.int64)
+                dist.all_reduce(t)
+                self.n_global = int(t.item())
+            maxiter = 10 * self.n_global
+        x0 = torch.zeros(n, dtype=torch.float32, device=dev) if x0_local is None else x0_local
+        return self.ctx.solve(b_local, x0, inv_diag_local, rtol=rtol, atol=atol, maxiter=maxiter)
+
+    def close(self):
+        self.ctx = None
+        if self.communicator is not None:
+            self.communicator.close()
+            self.communicator = None
 
 
 def dist_cg(comm: Communicator, A: DeviceSlab, b_local, *, x0_local=None, inv_diag_local=None, rtol=1e-5,

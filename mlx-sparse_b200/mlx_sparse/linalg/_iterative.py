@@ -68,6 +68,22 @@ def _maxiter(csr: CSRArray, maxiter) -> int:
     return value
 
 
+def _solve(csr: CSRArray, rhs, guess, inv_diag, rtol, atol, maxiter):
+    """Native solve. Square matrices reuse the matrix's cached solver context
+    (same recurrence as ``_native.csr_cg`` / ``csr_pcg_jacobi``, setup paid
+    once per matrix); otherwise the stateless entry points validate and raise
+    exactly as the reference's primitives do."""
+    n_rows, n_cols = csr.shape
+    if n_rows > 0 and n_rows == n_cols and rhs.shape[0] == n_rows:
+        ctx = csr.cg_context(inv_diag is not None)
+        return ctx.solve(rhs, guess, inv_diag, rtol=float(rtol), atol=float(atol), maxiter=maxiter)
+    if inv_diag is not None:
+        return _native.csr_pcg_jacobi(csr.data, csr.indices, csr.indptr, rhs, guess, inv_diag, csr.shape,
+                                      rtol=float(rtol), atol=float(atol), maxiter=maxiter)
+    return _native.csr_cg(csr.data, csr.indices, csr.indptr, rhs, guess, csr.shape, rtol=float(rtol),
+                          atol=float(atol), maxiter=maxiter)
+
+
 def cg(A, b, *, x0=None, rtol: float = 1e-5, atol: float = 0.0, maxiter: int | None = None, M=None,
        callback=None, return_info: bool = False):
     """Solves the SPD system ``A x = b`` with (Jacobi-preconditioned) CG.
@@ -86,15 +102,12 @@ def cg(A, b, *, x0=None, rtol: float = 1e-5, atol: float = 0.0, maxiter: int | N
         pc = preconditioners.aspreconditioner(M, csr)
         kind = pc.kind
         if isinstance(pc, preconditioners.DiagonalPreconditioner):
-            x, info, residual, iterations = _native.csr_pcg_jacobi(
-                csr.data, csr.indices, csr.indptr, rhs, guess, pc.inverse_diagonal.to(csr.device), csr.shape,
-                rtol=float(rtol), atol=float(atol), maxiter=maxiter_value)
+            x, info, residual, iterations = _solve(csr, rhs, guess, pc.inverse_diagonal.to(csr.device),
+                                                   rtol, atol, maxiter_value)
             return finish_solver_result(x, info, residual, iterations, solver="cg", return_info=bool(return_info),
                                         callback=callback, rtol=float(rtol), atol=float(atol),
                                         maxiter=maxiter_value, preconditioner=kind)
-    x, info, residual, iterations = _native.csr_cg(
-        csr.data, csr.indices, csr.indptr, rhs, guess, csr.shape, rtol=float(rtol), atol=float(atol),
-        maxiter=maxiter_value)
+    x, info, residual, iterations = _solve(csr, rhs, guess, None, rtol, atol, maxiter_value)
     return finish_solver_result(x, info, residual, iterations, solver="cg", return_info=bool(return_info),
                                 callback=callback, rtol=float(rtol), atol=float(atol), maxiter=maxiter_value,
                                 preconditioner=kind)

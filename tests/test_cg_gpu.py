@@ -139,3 +139,25 @@ def test_diagonal_sums_duplicates(ms):
     p = np.array([0, 2, 4, 5], np.int32)
     A = ms.csr_array((_dev(d), _dev(i), _dev(p)), shape=(3, 2))
     assert A.diagonal().cpu().tolist() == [3.0, 4.0]
+
+
+def test_cached_context_matches_stateless_solve(ms, orc):
+    """linalg.cg reuses the matrix's persistent solver; repeated solves (with
+    different right-hand sides and a warm start) must give the stateless
+    entry point's results bit for bit."""
+    from mlx_sparse import _native
+
+    (d, i, p), shape = wl.poisson3d(24)
+    n = shape[0]
+    A = _csr(ms, d, i, p, shape)
+    M = ms.linalg.preconditioners.jacobi(A)
+    inv = M.inverse_diagonal.cuda()
+    for seed in (1, 2):
+        b = _dev(wl.uniform_vector(n, seed))
+        x0 = torch.zeros(n, device="cuda") if seed == 1 else b * 0.1
+        x, info = ms.linalg.cg(A, b, x0=x0, M=M, rtol=1e-6, maxiter=500, return_info=True)
+        xs, info_s, res_s, its_s = _native.csr_pcg_jacobi(A.data, A.indices, A.indptr, b, x0, inv, shape,
+                                                          rtol=1e-6, atol=0.0, maxiter=500)
+        assert torch.equal(x, xs)
+        assert info.status == info_s and info.iterations == its_s
+    assert len(A._solvers) == 1

@@ -101,3 +101,24 @@ def test_partition_balances_nnz():
         assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
         loads = [int(p[b] - p[a]) for a, b in ranges]
         assert max(loads) <= int(p[-1]) / world + int(np.diff(p).max()) + 1
+
+
+@pytest.mark.parametrize("world", [2, 3, 5])
+@pytest.mark.parametrize("kind", ["poisson", "ragged", "random"])
+def test_landing_offsets_match_peer_halo_order(world, kind):
+    """Peer-memory halo push: rank r's entries, written at dst_offset in peer
+    q's local vector, must land exactly on q's halo slots for those columns."""
+    from mlx_sparse.distributed import build_slab, partition_rows
+
+    (d, i, p), (n, _) = _make(kind)
+    ranges = partition_rows(p, world)
+    slabs = [build_slab(d, i, p, n, r, world, ranges) for r in range(world)]
+    for s in slabs:
+        so = 0
+        for q, sc, off in zip(s.peers, s.send_counts, s.dst_offset):
+            t = slabs[int(q)]
+            cols = s.r0 + s.send_idx[so:so + sc].astype(np.int64)
+            h0 = int(off) - t.n_owned
+            assert h0 >= 0
+            assert np.array_equal(t.halo_cols[h0:h0 + sc], cols)
+            so += int(sc)

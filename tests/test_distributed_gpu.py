@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, case, q):
+def _worker(rank, world, port, case, q, mode="stateless"):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -47,8 +47,18 @@ def _worker(rank, world, port, case, q):
         inv = None
         if precond:
             inv = torch.full((slab.n_owned,), 1.0 / float(d.max()), dtype=torch.float32, device=dev)
-        x, info, res, its = dd.dist_cg(comm, A, torch.from_numpy(b[slab.r0:slab.r1].copy()), inv_diag_local=inv,
-                                       rtol=1e-6, maxiter=2000)
+        bl = torch.from_numpy(b[slab.r0:slab.r1].copy())
+        if mode == "stateless":
+            x, info, res, its = dd.dist_cg(comm, A, bl, inv_diag_local=inv, rtol=1e-6, maxiter=2000)
+        else:
+            solver = dd.DistCG(A, preconditioned=precond, comm=mode,
+                               communicator=comm if mode == "nccl" else None)
+            # two solves through one context: the second must repeat the first
+            first = solver.solve(bl.to(dev), inv_diag_local=inv, rtol=1e-6, maxiter=2000)
+            x, info, res, its = solver.solve(bl.to(dev), inv_diag_local=inv, rtol=1e-6, maxiter=2000)
+            assert torch.equal(first[0], x) and first[1:] == (info, res, its)
+            solver.ctx = None
+            torch.cuda.synchronize()
         parts = [None] * world
         dist.all_gather_object(parts, (slab.r0, x.cpu().numpy(), info, res, its))
         comm.close()
@@ -69,11 +79,12 @@ def _worker(rank, world, port, case, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["stateless", "nccl", "p2p"])
 @pytest.mark.parametrize("case", [("p3d", True), ("p3d", False), ("lap2d", True)])
-def test_dist_cg_matches_oracle(case):
+def test_dist_cg_matches_oracle(case, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    mp.spawn(_worker, args=(2, _free_port(), case, q), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), case, q, mode), nprocs=2, join=True)
     same, info, its, info_r, its_r, err = q.get(timeout=120)
     assert same, "ranks disagree on the scalars"
     assert info == info_r
