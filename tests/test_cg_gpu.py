@@ -138,7 +138,7 @@ def test_diagonal_sums_duplicates(ms):
     i = np.array([0, 0, 1, 1, 0], np.int32)
     p = np.array([0, 2, 4, 5], np.int32)
     A = ms.csr_array((_dev(d), _dev(i), _dev(p)), shape=(3, 2))
-    assert A.diagonal().cpu().tolist() == [3.0, 4.0]
+    assert A.diagonal().cpu().tolist() == [3.0, 7.0]
 
 
 def test_cached_context_matches_stateless_solve(ms, orc):
