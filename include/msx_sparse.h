@@ -229,14 +229,16 @@ MSX_API int msx_dist_pcg(void *comm, int index_dtype, const float *data,
  * src/linalg/cg/cg.cpp:338-379, src/preconditioners/pcg/pcg.cpp:317-366,
  * rebuild everything per call); the solve itself is the same recurrence.
  * comm_mode: 0 single GPU, 1 NCCL (nccl_comm from msx_dist_comm_create),
- * 2 peer memory over NVLink: every rank exports two IPC handles
- * (msx_cg_context_ipc_handles), the caller gathers them in rank order and
+ * 2 peer memory over NVLink: every rank exports a descriptor of
+ * MSX_CG_IPC_BYTES (IPC handles of its two direction buffers and its mailbox,
+ * msx_cg_context_ipc_handles), the caller gathers them in rank order and
  * passes all of them to msx_cg_context_connect before the first solve;
  * peer_dst_offset[k] is where this rank's entries for peer k start in that
  * peer's p vector (its owned length plus the offset of this rank's block in
  * its halo). All ranks must call solve together; peer waits are bounded and a
  * lost peer ends the solve with an error instead of hanging. */
 typedef struct msx_cg_context msx_cg_context;
+#define MSX_CG_IPC_BYTES 256
 MSX_API int msx_cg_context_create(int index_dtype, const float *data,
                                   const void *indices, const void *indptr,
                                   int64_t nnz, int64_t n_owned, int64_t n_halo,

@@ -451,9 +451,12 @@ int msx_cg_context_create(int index_dtype, const float *data, const void *indice
   });
 }
 
+static_assert(MSX_CG_IPC_BYTES == msx::kCgIpcBytes, "IPC descriptor size");
+
 int msx_cg_context_ipc_handles(msx_cg_context *ctx, void *out, int64_t size) {
   return guarded([&] {
-    require(ctx && out && size >= 128, MSX_ERR_INVALID, "msx_cg_context_ipc_handles needs a 128-byte buffer.");
+    require(ctx && out && size >= MSX_CG_IPC_BYTES, MSX_ERR_INVALID,
+            "msx_cg_context_ipc_handles needs a buffer of MSX_CG_IPC_BYTES.");
     cg_engine_ipc_handles(ctx->engine, out);
   });
 }
@@ -461,7 +464,8 @@ int msx_cg_context_ipc_handles(msx_cg_context *ctx, void *out, int64_t size) {
 int msx_cg_context_connect(msx_cg_context *ctx, const void *all_handles, int64_t size) {
   return guarded([&] {
     require(ctx && all_handles, MSX_ERR_INVALID, "msx_cg_context_connect: null argument.");
-    require(size >= 128 * (int64_t)ctx->world, MSX_ERR_INVALID, "msx_cg_context_connect: need world x 128 bytes.");
+    require(size >= MSX_CG_IPC_BYTES * (int64_t)ctx->world, MSX_ERR_INVALID,
+            "msx_cg_context_connect: need world x MSX_CG_IPC_BYTES bytes.");
     cg_engine_connect(ctx->engine, all_handles);
   });
 }

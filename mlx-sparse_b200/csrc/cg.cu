@@ -71,8 +71,8 @@ __device__ __forceinline__ void block_sum4(double (&v)[4], double *smem /*[32*4]
 }
 
 // Writes this CTA's partial and, in the last CTA to finish, the ordered sum of
-// all partials into state->red. Returns true in thread 0 of the last CTA.
-__device__ bool reduce_to_state(double (&v)[4], double *partials, CgState *st) {
+// all partials into state->red. Returns true in every thread of the last CTA.
+__device__ bool reduce_last(double (&v)[4], double *partials, CgState *st) {
   __shared__ double smem[32 * 4];
   __shared__ bool is_last;
   block_sum4(v, smem);
@@ -95,9 +95,157 @@ __device__ bool reduce_to_state(double (&v)[4], double *partials, CgState *st) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) st->red[c] = s[c];
     st->counter = 0;
-    return true;
   }
-  return false;
+  __syncthreads();
+  return true;
+}
+
+// ---- peer memory (one node, NVLink) ------------------------------------------------
+constexpr long long kPeerPollLimit = 1ll << 24;
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Sums st->red (4 doubles) over the ranks through their mailboxes. Run by one
+// full warp. Every rank stores its 8 flagged words into every mailbox (its own
+// included), then waits, bounded, for the words of all ranks and adds them in
+// rank order, so every rank computes identical scalars. Returns false on a
+// timeout.
+__device__ bool ll_allreduce(CgState *st, const P2pLink &L) {
+  __shared__ unsigned halves[kMaxRanks][8];
+  const int lane = threadIdx.x & 31;
+  unsigned epoch = 0;
+  if (lane == 0) {
+    epoch = (unsigned)(L.cs->ar_epoch + 1);
+    L.cs->ar_epoch = epoch;
+  }
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
+  const int slot = (int)(epoch & 1u);
+  const int word = lane & 7;
+  const unsigned long long bits = (unsigned long long)__double_as_longlong(st->red[word >> 1]);
+  const unsigned half = (word & 1) ? (unsigned)(bits >> 32) : (unsigned)bits;
+  const unsigned long long w = ((unsigned long long)epoch << 32) | half;
+  const int total = 8 * L.world;
+  for (int i = lane; i < total; i += 32) st_relaxed_sys(&L.peer[i >> 3]->ll[slot][L.rank][word], w);
+  bool ok = true;
+  for (int i = lane; i < total; i += 32) {
+    const unsigned long long *src = &L.mine->ll[slot][i >> 3][word];
+    unsigned long long v = ld_relaxed_sys(src);
+    long long polls = 0;
+    while ((unsigned)(v >> 32) != epoch) {
+      if (++polls > kPeerPollLimit) {
+        ok = false;
+        break;
+      }
+      v = ld_relaxed_sys(src);
+    }
+    halves[i >> 3][word] = (unsigned)v;
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  __syncwarp();
+  if (ok && lane < 4) {
+    double sum = 0.0;
+    for (int q = 0; q < L.world; ++q) {
+      const unsigned long long b = ((unsigned long long)halves[q][2 * lane + 1] << 32) | halves[q][2 * lane];
+      sum += __longlong_as_double((long long)b);
+    }
+    st->red[lane] = sum;
+  }
+  __syncwarp();
+  return ok;
+}
+
+// The last CTA of a reduction: combine over the ranks (peer memory) and run
+// the decision `f` in one thread. Single GPU: decide directly when `decide`.
+template <typename F>
+__device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partials, CgState *st, const P2pLink &L,
+                                                  bool decide, F f) {
+  if (!reduce_last(v, partials, st)) return;
+  if (L.world > 1) {
+    if (threadIdx.x < 32) {
+      const bool ok = ll_allreduce(st, L);
+      if (threadIdx.x == 0) {
+        if (ok) {
+          f();
+        } else {
+          L.cs->error = 1;
+          st->status = -4;  // communication timeout (not a reference status)
+        }
+      }
+    }
+  } else if (threadIdx.x == 0 && decide) {
+    f();
+  }
+}
+
+// Waits (thread 0, bounded) until every rank this one receives halo entries
+// from has completed as many pushes as this rank has; then the CTA may read
+// the halo part of the vector. Call from all threads.
+__device__ __forceinline__ void halo_wait_cta(CgState *st, const P2pLink &L) {
+  if (threadIdx.x == 0) {
+    const unsigned long long epoch = L.cs->halo_epoch;
+    for (int k = 0; k < L.n_recv; ++k) {
+      long long polls = 0;
+      while (ld_acquire_sys(&L.mine->halo_epoch[L.recv[k]]) < epoch) {
+        if (++polls > kPeerPollLimit) {
+          L.cs->error = 1;
+          st->status = -4;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Where one rank's halo entries go: for each receiving peer, the address in
+// that peer's direction buffer where its entries start, and the prefix of the
+// send counts over the concatenated send list `idx`.
+struct PushPlan {
+  float *dst[kMaxRanks];
+  long long off[kMaxRanks + 1];
+  int peer[kMaxRanks];
+  int n_peers;
+  const int *idx;
+};
+
+__device__ __forceinline__ int push_peer(const PushPlan &pp, long long j) {
+  int k = 0;
+  while (k + 1 < pp.n_peers && j >= pp.off[k + 1]) ++k;
+  return k;
+}
+
+// After a CTA's pushes: the last CTA to finish raises this rank's halo epoch
+// in the receiving peers' mailboxes. Call from all threads.
+__device__ __forceinline__ void halo_publish(const PushPlan &pp, const P2pLink &L) {
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(&L.cs->halo_counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence_system();
+    L.cs->halo_counter = 0;
+    const unsigned long long epoch = L.cs->halo_epoch + 1;
+    L.cs->halo_epoch = epoch;
+    for (int k = 0; k < pp.n_peers; ++k) st_release_sys(&L.peer[pp.peer[k]]->halo_epoch[L.rank], epoch);
+  }
 }
 
 // ---- scalar decisions (one thread) -------------------------------------------
@@ -252,7 +400,7 @@ __device__ void decide_pupdate(CgState *st) {
 __global__ void __launch_bounds__(kThreads)
 init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, const float *__restrict__ ap,
             const float *__restrict__ inv_diag, float *__restrict__ r, float *__restrict__ z, float *__restrict__ p,
-            int64_t n, double *partials, CgState *st, float rtol, float atol, bool decide) {
+            int64_t n, double *partials, CgState *st, float rtol, float atol, bool decide, P2pLink L) {
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float bi = b[i];
@@ -272,7 +420,7 @@ init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, 
       if (!(finite_f(ri) && finite_f(zi) && finite_f(inv))) v[3] += 1.0;
     }
   }
-  if (reduce_to_state(v, partials, st) && decide) decide_init(st, kind, rtol, atol);
+  reduce_and_decide(v, partials, st, L, decide, [&] { decide_init(st, kind, rtol, atol); });
 }
 
 // Fuses p.Ap, p.p, Ap.Ap (and the non-finite count) into the SpMV row
@@ -284,8 +432,13 @@ struct DotsEpilogue {
   CgState *st;
   int kind;
   bool decide;
+  bool halo_wait;  // peer memory: wait for the peers' halo pushes first
+  P2pLink L;
   double pap, pp, apap, bad;
   __device__ __forceinline__ bool skip() const { return st->status != kStatusRunning; }
+  __device__ __forceinline__ void begin() {
+    if (halo_wait) halo_wait_cta(st, L);
+  }
   __device__ __forceinline__ void row(int64_t r, float apv) {
     const float pv = __ldg(p + r);
     pap += (double)pv * (double)apv;
@@ -295,13 +448,13 @@ struct DotsEpilogue {
   }
   __device__ __forceinline__ void finish() {
     double v[4] = {pap, pp, apap, bad};
-    if (reduce_to_state(v, partials, st) && decide) decide_spmv(st, kind);
+    reduce_and_decide(v, partials, st, L, decide, [&] { decide_spmv(st, kind); });
   }
 };
 
 __global__ void __launch_bounds__(kThreads)
 dots_kernel(int kind, const float *__restrict__ p, const float *__restrict__ ap, int64_t n, double *partials,
-            CgState *st, bool decide) {
+            CgState *st, bool decide, P2pLink L) {
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -311,13 +464,13 @@ dots_kernel(int kind, const float *__restrict__ p, const float *__restrict__ ap,
     v[2] += (double)av * (double)av;
     if (!(finite_f(pv) && finite_f(av))) v[3] += 1.0;
   }
-  if (reduce_to_state(v, partials, st) && decide) decide_spmv(st, kind);
+  reduce_and_decide(v, partials, st, L, decide, [&] { decide_spmv(st, kind); });
 }
 
 __global__ void __launch_bounds__(kThreads)
 update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__restrict__ z,
               const float *__restrict__ p, const float *__restrict__ ap, const float *__restrict__ inv_diag,
-              int64_t n, double *partials, CgState *st, bool decide) {
+              int64_t n, double *partials, CgState *st, bool decide, P2pLink L) {
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   if (kind == kCG) {
@@ -374,46 +527,73 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
       z[i] = zo;
     }
   }
-  if (reduce_to_state(v, partials, st) && decide) decide_update(st, kind);
+  reduce_and_decide(v, partials, st, L, decide, [&] { decide_update(st, kind); });
 }
 
+// p_next = r + beta p (CG, double) or z + beta p (PCG, float), from p_cur
+// (p_next == p_cur updates in place). Peer memory: the entries the peers read
+// are computed once more from the unchanged inputs and stored straight into
+// the peers' next direction buffers, then published.
 __global__ void __launch_bounds__(kThreads)
-pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ z, float *__restrict__ p, int64_t n,
-               double *partials, CgState *st, bool decide) {
+pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ z, const float *p_cur, float *p_next,
+               int64_t n, double *partials, CgState *st, bool decide, P2pLink L, PushPlan pp) {
   if (st->status != kStatusRunning) return;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const bool push = L.world > 1;
   if (kind == kCG) {
     const double beta = st->beta_d;
     double v[4] = {0.0, 0.0, 0.0, 0.0};
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)p[i]));
+    for (int64_t i = first; i < n; i += stride) {
+      const float old = p_cur[i];
+      const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)old));
       const float pf = __double2float_rn(pc);
       if (!finite_d(pc) || !finite_f(pf)) {
-        v[0] += 1.0;
+        v[0] += 1.0;  // p keeps its value (cg.cpp:238-246)
+        if (p_next != p_cur) p_next[i] = old;
         continue;
       }
-      p[i] = pf;
+      p_next[i] = pf;
     }
-    if (reduce_to_state(v, partials, st) && decide) decide_pupdate(st);
+    if (push) {
+      const long long ns = pp.off[pp.n_peers];
+      for (long long j = first; j < ns; j += stride) {
+        const int k = push_peer(pp, j);
+        const int i = pp.idx[j];
+        const float old = p_cur[i];
+        const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)old));
+        const float pf = __double2float_rn(pc);
+        pp.dst[k][j - pp.off[k]] = (!finite_d(pc) || !finite_f(pf)) ? old : pf;
+      }
+      halo_publish(pp, L);
+    }
+    reduce_and_decide(v, partials, st, L, decide, [&] { decide_pupdate(st); });
   } else {
     const float beta = st->beta_f;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    const int64_t first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t done = 0;
-    if (aligned16(z) && aligned16(p)) {
+    if (aligned16(z) && aligned16(p_cur) && aligned16(p_next)) {
       const int64_t n4 = n / 4;
       for (int64_t i = first; i < n4; i += stride) {
         const float4 zv = __ldcs(reinterpret_cast<const float4 *>(z) + i);
-        float4 pv = reinterpret_cast<const float4 *>(p)[i];
+        float4 pv = reinterpret_cast<const float4 *>(p_cur)[i];
         pv.x = __fadd_rn(zv.x, __fmul_rn(beta, pv.x));
         pv.y = __fadd_rn(zv.y, __fmul_rn(beta, pv.y));
         pv.z = __fadd_rn(zv.z, __fmul_rn(beta, pv.z));
         pv.w = __fadd_rn(zv.w, __fmul_rn(beta, pv.w));
-        reinterpret_cast<float4 *>(p)[i] = pv;
+        reinterpret_cast<float4 *>(p_next)[i] = pv;
       }
       done = n4 * 4;
     }
-    for (int64_t i = done + first; i < n; i += stride) p[i] = __fadd_rn(z[i], __fmul_rn(beta, p[i]));
+    for (int64_t i = done + first; i < n; i += stride) p_next[i] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
+    if (push) {
+      const long long ns = pp.off[pp.n_peers];
+      for (long long j = first; j < ns; j += stride) {
+        const int k = push_peer(pp, j);
+        const int i = pp.idx[j];
+        pp.dst[k][j - pp.off[k]] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
+      }
+      halo_publish(pp, L);
+    }
   }
 }
 
@@ -435,121 +615,22 @@ __global__ void halo_pack_kernel(const float *__restrict__ v, const int *__restr
   if (i < n) out[i] = v[idx[i]];
 }
 
-// ---- peer-memory communication (one node, NVLink) -------------------------------
-constexpr long long kPeerPollLimit = 1ll << 24;
-
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// All-reduce of st->red (4 doubles) over `world` ranks through their mailboxes,
-// then the decision `which`. One warp; thread q talks to rank q. The sum runs
-// in rank order, so every rank computes identical scalars.
-__global__ void p2p_allreduce_decide_kernel(CgState *st, CommState *cs, Mailbox *mine, Mailbox *const *peers,
-                                            int rank, int world, int which, int kind, float rtol, float atol) {
-  if (which != 0 && st->status != kStatusRunning) return;  // identical on every rank
-  __shared__ unsigned long long epoch;
-  __shared__ int timed_out;
-  const int q = threadIdx.x;
-  if (q == 0) {
-    epoch = cs->ar_epoch + 1;
-    cs->ar_epoch = epoch;
-    timed_out = 0;
-  }
-  __syncwarp();
-  const int slot = (int)(epoch & 1);
-  if (q < world) {
-    Mailbox *pm = q == rank ? mine : peers[q];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) pm->red[slot][rank][c] = st->red[c];
-    __threadfence_system();
-    st_release_sys(&pm->red_epoch[rank], epoch);
-  }
-  __syncwarp();
-  if (q < world) {
-    long long polls = 0;
-    while (ld_acquire_sys(&mine->red_epoch[q]) < epoch) {
-      if (++polls > kPeerPollLimit) {
-        timed_out = 1;
-        break;
-      }
-    }
-  }
-  __syncwarp();
-  if (q == 0) {
-    if (timed_out) {
-      cs->error = 1;
-      st->status = -4;  // communication timeout (not a reference status)
-      return;
-    }
-    double sum[4] = {0.0, 0.0, 0.0, 0.0};
-    for (int r = 0; r < world; ++r)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) sum[c] += *((volatile double *)&mine->red[slot][r][c]);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) st->red[c] = sum[c];
-    switch (which) {
-    case 0: decide_init(st, kind, rtol, atol); break;
-    case 1: decide_spmv(st, kind); break;
-    case 2: decide_update(st, kind); break;
-    default: decide_pupdate(st); break;
-    }
-  }
-}
-
-struct PeerSend {
-  float *dst[kMaxRanks];      // peer p buffer + landing offset
-  long long off[kMaxRanks + 1];  // prefix of send counts
-  int peer[kMaxRanks];
-  int n_peers;
-};
-
-// Writes this rank's halo entries straight into the peers' p buffers, then
-// (last CTA) raises this rank's halo flag in every peer's mailbox.
-__global__ void p2p_halo_push_kernel(const CgState *st, CommState *cs, const float *__restrict__ v,
-                                     const int *__restrict__ idx, PeerSend ps, Mailbox *const *peers, int rank) {
+// Standalone halo push of v's send entries into the peers' buffers (the
+// initial residual; the iterations fuse the push into the direction update).
+__global__ void p2p_halo_push_kernel(CgState *st, const float *__restrict__ v, PushPlan pp, P2pLink L) {
   if (st->status != kStatusRunning) return;
-  const long long n = ps.off[ps.n_peers];
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    int k = 0;
-    while (k + 1 < ps.n_peers && i >= ps.off[k + 1]) ++k;
-    ps.dst[k][i - ps.off[k]] = v[idx[i]];
+  const long long ns = pp.off[pp.n_peers];
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < ns; j += (long long)gridDim.x * blockDim.x) {
+    const int k = push_peer(pp, j);
+    pp.dst[k][j - pp.off[k]] = v[pp.idx[j]];
   }
-  __threadfence_system();
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(&cs->halo_counter, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    cs->halo_counter = 0;
-    const unsigned long long epoch = cs->halo_epoch + 1;
-    cs->halo_epoch = epoch;
-    __threadfence_system();
-    for (int k = 0; k < ps.n_peers; ++k) st_release_sys(&peers[ps.peer[k]]->halo_epoch[rank], epoch);
-  }
+  halo_publish(pp, L);
 }
 
-// Waits until every peer this rank receives halo entries from has pushed
-// this iteration's entries (epoch flags), bounded.
-__global__ void p2p_halo_wait_kernel(CgState *st, CommState *cs, const Mailbox *mine, const int *recv_peers,
-                                     int n_recv) {
+// Standalone halo wait (before SpMV kernels that do not wait themselves).
+__global__ void p2p_halo_wait_kernel(CgState *st, P2pLink L) {
   if (st->status != kStatusRunning) return;
-  const unsigned long long epoch = cs->halo_epoch;  // pushed by this rank just before
-  for (int k = 0; k < n_recv; ++k) {
-    long long polls = 0;
-    while (ld_acquire_sys(&mine->halo_epoch[recv_peers[k]]) < epoch) {
-      if (++polls > kPeerPollLimit) {
-        cs->error = 1;
-        st->status = -4;
-        return;
-      }
-    }
-  }
+  halo_wait_cta(st, L);
 }
 
 int elementwise_grid(int64_t n) {
@@ -577,7 +658,9 @@ struct CgEngine {
   int red_grid = 1;
   void *plan_mem = nullptr;
   void *mem = nullptr;       // state, partials, vectors (one allocation)
-  float *p = nullptr;        // own allocation (IPC-exported in P2P mode)
+  float *pbuf = nullptr;     // direction buffer(s), own allocation (IPC-exported in P2P mode)
+  float *p[2] = {};          // P2P: two buffers, alternating by iteration parity; else p[0] == p[1]
+  int64_t p_stride = 0;      // elements between p[0] and p[1]
   Mailbox *mbox = nullptr;   // own allocation (IPC-exported in P2P mode)
   CgState *st = nullptr;
   CommState *cs = nullptr;
@@ -586,11 +669,10 @@ struct CgEngine {
   float *sendbuf = nullptr;
   int64_t n_send = 0;
   // P2P
-  Mailbox **peer_mbox_dev = nullptr;  // device array [world]
-  int *recv_peers_dev = nullptr;
-  int n_recv_peers = 0;
+  P2pLink link{};            // world == 1 unless P2P
+  PushPlan push[2] = {};     // by parity of the destination buffer
+  int push_grid = 1;
   void *opened[2 * kMaxRanks] = {};
-  PeerSend ps{};
   bool connected = false;
   cudaStream_t s = nullptr;
   cudaEvent_t ev = nullptr;
@@ -602,17 +684,11 @@ struct CgEngine {
 
 namespace {
 
-void engine_exchange(CgEngine *e, float *v, cudaStream_t q) {
+bool p2p(const CgEngine *e) { return e->cfg.comm == kCommP2p; }
+
+// NCCL halo exchange of v (owned part -> peers' halo part).
+void engine_exchange_nccl(CgEngine *e, float *v, cudaStream_t q) {
   const CgEngineConfig &c = e->cfg;
-  if (c.comm == kCommP2p) {
-    if (!e->connected) fail(MSX_ERR_RUNTIME, "CG context: peers are not connected.");
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(std::max<int64_t>(e->n_send, 1), 256), 256));
-    p2p_halo_push_kernel<<<grid, 256, 0, q>>>(e->st, e->cs, v, c.send_idx, e->ps, e->peer_mbox_dev, c.rank);
-    MSX_CHECK_LAUNCH();
-    p2p_halo_wait_kernel<<<1, 1, 0, q>>>(e->st, e->cs, e->mbox, e->recv_peers_dev, e->n_recv_peers);
-    MSX_CHECK_LAUNCH();
-    return;
-  }
 #if defined(MSX_HAVE_NCCL)
   if (c.comm != kCommNccl) return;
   if (e->n_send > 0) {
@@ -641,23 +717,29 @@ void engine_exchange(CgEngine *e, float *v, cudaStream_t q) {
 #endif
 }
 
-// After a reduction kernel left local sums in st->red: combine over ranks and
-// decide. Single GPU: the kernel's last CTA already decided.
-void engine_reduce_decide(CgEngine *e, int which, float rtol, float atol, cudaStream_t q) {
-  const CgEngineConfig &c = e->cfg;
-  if (c.comm == kCommP2p) {
-    p2p_allreduce_decide_kernel<<<1, 32, 0, q>>>(e->st, e->cs, e->mbox, e->peer_mbox_dev, c.rank, c.world, which,
-                                                 e->kind, rtol, atol);
-    MSX_CHECK_LAUNCH();
-    return;
-  }
+// Peer memory: push v's send entries into the peers' buffers of parity `par`.
+void engine_push(CgEngine *e, const float *v, int par, cudaStream_t q) {
+  p2p_halo_push_kernel<<<e->push_grid, kThreads, 0, q>>>(e->st, v, e->push[par], e->link);
+  MSX_CHECK_LAUNCH();
+}
+
+void engine_wait(CgEngine *e, cudaStream_t q) {
+  p2p_halo_wait_kernel<<<1, 32, 0, q>>>(e->st, e->link);
+  MSX_CHECK_LAUNCH();
+}
+
+// NCCL: after a reduction kernel left local sums in st->red, all-reduce them
+// and decide. Peer memory and single GPU: the kernel's last CTA already did.
+void engine_reduce_decide_nccl(CgEngine *e, int which, float rtol, float atol, cudaStream_t q) {
 #if defined(MSX_HAVE_NCCL)
+  const CgEngineConfig &c = e->cfg;
   if (c.comm != kCommNccl) return;
   ncclResult_t r = ncclAllReduce(e->st->red, e->st->red, 4, ncclDouble, ncclSum, static_cast<ncclComm_t>(c.nccl_comm), q);
   if (r != ncclSuccess) fail(MSX_ERR_RUNTIME, std::string("NCCL: ") + ncclGetErrorString(r));
   decide_kernel<<<1, 1, 0, q>>>(e->st, which, e->kind, rtol, atol);
   MSX_CHECK_LAUNCH();
 #else
+  (void)e;
   (void)which;
   (void)rtol;
   (void)atol;
@@ -665,31 +747,37 @@ void engine_reduce_decide(CgEngine *e, int which, float rtol, float atol, cudaSt
 #endif
 }
 
-void engine_iteration(CgEngine *e, cudaStream_t q) {
+// One iteration reading direction buffer `par` and writing `par ^ 1` (the
+// same buffer unless P2P). Single GPU and P2P: three kernels, the scalar
+// all-reduce and the halo exchange fused into them.
+void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   const CgEngineConfig &c = e->cfg;
   const bool decide = c.comm == kCommNone;
   const int kind = e->kind;
-  engine_exchange(e, e->p, q);
+  float *pc = e->p[par], *pn = e->p[par ^ 1];
+  engine_exchange_nccl(e, pc, q);
   if (e->fused) {
     dispatch_index(c.index_dtype, [&](auto ityp) {
       using I = decltype(ityp);
-      DotsEpilogue epi{e->p, e->partials, e->st, kind, decide, 0.0, 0.0, 0.0, 0.0};
+      DotsEpilogue epi{pc, e->partials, e->st, kind, decide, p2p(e), e->link, 0.0, 0.0, 0.0, 0.0};
       launch_spmv_binned<float, I, DotsEpilogue>(e->plan, c.data, static_cast<const I *>(c.indices),
-                                                 static_cast<const I *>(c.indptr), e->p, e->ap, e->carry, epi, q);
+                                                 static_cast<const I *>(c.indptr), pc, e->ap, e->carry, epi, q);
     });
   } else {
-    spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p, e->ap, e->carry, q);
-    dots_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->p, e->ap, e->n, e->partials, e->st, decide);
+    if (p2p(e)) engine_wait(e, q);
+    spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, pc, e->ap, e->carry, q);
+    dots_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, pc, e->ap, e->n, e->partials, e->st, decide, e->link);
     MSX_CHECK_LAUNCH();
   }
-  engine_reduce_decide(e, 1, 0.f, 0.f, q);
-  update_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->x, e->r, e->z, e->p, e->ap, e->inv, e->n, e->partials, e->st,
-                                                 decide);
+  engine_reduce_decide_nccl(e, 1, 0.f, 0.f, q);
+  update_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->x, e->r, e->z, pc, e->ap, e->inv, e->n, e->partials, e->st,
+                                                 decide, e->link);
   MSX_CHECK_LAUNCH();
-  engine_reduce_decide(e, 2, 0.f, 0.f, q);
-  pupdate_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->r, e->z, e->p, e->n, e->partials, e->st, decide);
+  engine_reduce_decide_nccl(e, 2, 0.f, 0.f, q);
+  pupdate_kernel<<<std::max(e->red_grid, p2p(e) ? e->push_grid : 1), kThreads, 0, q>>>(
+      kind, e->r, e->z, pc, pn, e->n, e->partials, e->st, decide, e->link, e->push[par ^ 1]);
   MSX_CHECK_LAUNCH();
-  if (kind == kCG) engine_reduce_decide(e, 3, 0.f, 0.f, q);
+  if (kind == kCG) engine_reduce_decide_nccl(e, 3, 0.f, 0.f, q);
 }
 
 template <typename T> T *bump(char *&cur, size_t count) {
@@ -697,6 +785,14 @@ template <typename T> T *bump(char *&cur, size_t count) {
   cur += (sizeof(T) * count + 255) & ~size_t(255);
   return p;
 }
+
+// Layout of one rank's peer-memory descriptor.
+struct IpcBlob {
+  cudaIpcMemHandle_t p;
+  cudaIpcMemHandle_t mbox;
+  int64_t p_stride;
+};
+static_assert(sizeof(IpcBlob) <= kCgIpcBytes, "descriptor too large");
 
 }  // namespace
 
@@ -731,15 +827,15 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
     using I = decltype(ityp);
     spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(E->plan), binned_grid<float, I, NoEpilogue>(E->plan));
   });
-  const int64_t max_grid = std::max<int64_t>(E->red_grid, spmv_grid_n);
   for (int k = 0; k < cfg.n_peers; ++k) E->n_send += cfg.send_counts[k];
+  E->push_grid = elementwise_grid(std::max<int64_t>(E->n_send, 1));
+  const int64_t max_grid = std::max<int64_t>(std::max<int64_t>(E->red_grid, E->push_grid), spmv_grid_n);
   const size_t vec = (size_t)std::max<int64_t>(E->n, 1);
   size_t bytes = 0;
   auto sz = [](size_t b) { return (b + 255) & ~size_t(255); };
   bytes += sz(sizeof(CgState)) + sz(sizeof(CommState)) + sz(sizeof(double) * 4 * max_grid) +
            sz(sizeof(float) * std::max<int64_t>(E->plan.n_chunks, 1)) + 6 * sz(sizeof(float) * vec) +
-           sz(sizeof(float) * std::max<int64_t>(E->n_send, 1)) + sz(sizeof(Mailbox *) * kMaxRanks) +
-           sz(sizeof(int) * kMaxRanks);
+           sz(sizeof(float) * std::max<int64_t>(E->n_send, 1));
   MSX_CUDA(cudaMalloc(&E->mem, bytes));
   MSX_CUDA(cudaMemsetAsync(E->mem, 0, bytes, s));
   char *cur = static_cast<char *>(E->mem);
@@ -754,25 +850,33 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   E->b = bump<float>(cur, vec);
   E->inv = bump<float>(cur, vec);
   E->sendbuf = bump<float>(cur, std::max<int64_t>(E->n_send, 1));
-  E->peer_mbox_dev = bump<Mailbox *>(cur, kMaxRanks);
-  E->recv_peers_dev = bump<int>(cur, kMaxRanks);
-  MSX_CUDA(cudaMalloc(&E->p, sizeof(float) * (size_t)std::max<int64_t>(E->n_cols, 1)));
-  MSX_CUDA(cudaMemsetAsync(E->p, 0, sizeof(float) * (size_t)std::max<int64_t>(E->n_cols, 1), s));
+  // direction buffers: two (16-byte aligned apart) in P2P mode
+  const int64_t cols = std::max<int64_t>(E->n_cols, 1);
+  E->p_stride = cfg.comm == kCommP2p ? (cols + 63) / 64 * 64 : 0;
+  const int64_t p_elems = cfg.comm == kCommP2p ? 2 * E->p_stride : cols;
+  MSX_CUDA(cudaMalloc(&E->pbuf, sizeof(float) * (size_t)p_elems));
+  MSX_CUDA(cudaMemsetAsync(E->pbuf, 0, sizeof(float) * (size_t)p_elems, s));
+  E->p[0] = E->pbuf;
+  E->p[1] = E->pbuf + E->p_stride;
   MSX_CUDA(cudaMalloc(&E->mbox, sizeof(Mailbox)));
   MSX_CUDA(cudaMemsetAsync(E->mbox, 0, sizeof(Mailbox), s));
   if (!cfg.preconditioned) E->z = nullptr, E->inv = nullptr;
   MSX_CUDA(cudaMallocHost(&E->status_host, sizeof(int)));
-  // receive peers (P2P halo waits)
+  E->link.world = 1;
+  E->link.rank = 0;
+  E->link.cs = E->cs;
+  E->link.mine = E->mbox;
   if (cfg.comm == kCommP2p) {
-    int recv[kMaxRanks];
+    E->link.world = cfg.world;
+    E->link.rank = cfg.rank;
     for (int k = 0; k < cfg.n_peers; ++k)
-      if (cfg.recv_counts[k] > 0) recv[E->n_recv_peers++] = cfg.peers[k];
-    MSX_CUDA(cudaMemcpyAsync(E->recv_peers_dev, recv, sizeof(int) * E->n_recv_peers, cudaMemcpyHostToDevice, s));
+      if (cfg.recv_counts[k] > 0) E->link.recv[E->link.n_recv++] = cfg.peers[k];
   }
-  // Iterations per graph launch: about a millisecond of work per batch (even).
+  // Iterations per graph launch: about a millisecond of work per batch, even
+  // (P2P alternates the direction buffers).
   const double bytes_per_iter = 8.0 * cfg.nnz + 56.0 * E->n;
   int batch = (int)std::max(1.0, std::min(64.0, 5.0e9 * 1e-3 / std::max(bytes_per_iter, 1.0)));
-  E->batch = std::max(4, batch);
+  E->batch = std::max(4, (batch + 1) & ~1);
   MSX_CUDA(cudaStreamSynchronize(s));
   return e.release();
 }
@@ -788,7 +892,7 @@ void cg_engine_destroy(CgEngine *e) {
   for (void *p : e->opened)
     if (p) cudaIpcCloseMemHandle(p);
   if (e->status_host) cudaFreeHost(e->status_host);
-  if (e->p) cudaFree(e->p);
+  if (e->pbuf) cudaFree(e->pbuf);
   if (e->mbox) cudaFree(e->mbox);
   if (e->mem) cudaFree(e->mem);
   if (e->plan_mem) cudaFree(e->plan_mem);
@@ -798,63 +902,72 @@ void cg_engine_destroy(CgEngine *e) {
   delete e;
 }
 
-void cg_engine_ipc_handles(CgEngine *e, void *out128) {
-  cudaIpcMemHandle_t h[2];
-  MSX_CUDA(cudaIpcGetMemHandle(&h[0], e->p));
-  MSX_CUDA(cudaIpcGetMemHandle(&h[1], e->mbox));
-  std::memcpy(out128, h, sizeof(h));
+void cg_engine_ipc_handles(CgEngine *e, void *out) {
+  IpcBlob blob{};
+  MSX_CUDA(cudaIpcGetMemHandle(&blob.p, e->pbuf));
+  MSX_CUDA(cudaIpcGetMemHandle(&blob.mbox, e->mbox));
+  blob.p_stride = e->p_stride;
+  std::memset(out, 0, kCgIpcBytes);
+  std::memcpy(out, &blob, sizeof(blob));
 }
 
 void cg_engine_connect(CgEngine *e, const void *all_handles) {
   const CgEngineConfig &c = e->cfg;
-  const auto *hs = static_cast<const cudaIpcMemHandle_t *>(all_handles);
-  Mailbox *mboxes[kMaxRanks] = {};
-  float *ps[kMaxRanks] = {};
+  if (c.comm != kCommP2p) fail(MSX_ERR_INVALID, "CG context: connect is for the peer-memory mode.");
+  if (e->connected) fail(MSX_ERR_INVALID, "CG context: already connected.");
+  const char *raw = static_cast<const char *>(all_handles);
+  float *pb[kMaxRanks] = {};
+  int64_t stride[kMaxRanks] = {};
   for (int q = 0; q < c.world; ++q) {
+    IpcBlob blob;
+    std::memcpy(&blob, raw + (size_t)q * kCgIpcBytes, sizeof(blob));
+    stride[q] = blob.p_stride;
     if (q == c.rank) {
-      mboxes[q] = e->mbox;
-      ps[q] = e->p;
+      e->link.peer[q] = e->mbox;
+      pb[q] = e->pbuf;
       continue;
     }
     void *pp = nullptr, *mb = nullptr;
-    MSX_CUDA(cudaIpcOpenMemHandle(&pp, hs[2 * q], cudaIpcMemLazyEnablePeerAccess));
+    MSX_CUDA(cudaIpcOpenMemHandle(&pp, blob.p, cudaIpcMemLazyEnablePeerAccess));
     e->opened[2 * q] = pp;
-    MSX_CUDA(cudaIpcOpenMemHandle(&mb, hs[2 * q + 1], cudaIpcMemLazyEnablePeerAccess));
+    MSX_CUDA(cudaIpcOpenMemHandle(&mb, blob.mbox, cudaIpcMemLazyEnablePeerAccess));
     e->opened[2 * q + 1] = mb;
-    mboxes[q] = static_cast<Mailbox *>(mb);
-    ps[q] = static_cast<float *>(pp);
+    e->link.peer[q] = static_cast<Mailbox *>(mb);
+    pb[q] = static_cast<float *>(pp);
   }
-  MSX_CUDA(cudaMemcpyAsync(e->peer_mbox_dev, mboxes, sizeof(mboxes), cudaMemcpyHostToDevice, e->s));
-  PeerSend ps_{};
-  long long off = 0;
-  int np = 0;
-  for (int k = 0; k < c.n_peers; ++k) {
-    if (c.send_counts[k] == 0) continue;
-    ps_.dst[np] = ps[c.peers[k]] + c.peer_dst_offset[k];
-    ps_.peer[np] = c.peers[k];
-    ps_.off[np] = off;
-    off += c.send_counts[k];
-    ++np;
+  for (int par = 0; par < 2; ++par) {
+    PushPlan pp{};
+    long long off = 0;
+    int np = 0;
+    for (int k = 0; k < c.n_peers; ++k) {
+      if (c.send_counts[k] == 0) continue;  // that peer waits for no flag of this rank
+      const int q = c.peers[k];
+      pp.dst[np] = pb[q] + par * stride[q] + c.peer_dst_offset[k];
+      pp.peer[np] = q;
+      pp.off[np] = off;
+      off += c.send_counts[k];
+      ++np;
+    }
+    pp.off[np] = off;
+    pp.n_peers = np;
+    pp.idx = c.send_idx;
+    e->push[par] = pp;
   }
-  ps_.off[np] = off;
-  ps_.n_peers = np;
-  // every halo peer is flagged, also those that get nothing from this rank
-  // (their wait lists only contain ranks that send to them, so this is enough)
-  e->ps = ps_;
-  MSX_CUDA(cudaStreamSynchronize(e->s));
   e->connected = true;
 }
 
 CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, const float *inv_in, float *x_out,
                          float rtol, float atol, int maxiter, cudaStream_t user_stream) {
   const CgEngineConfig &c = e->cfg;
+  if (p2p(e) && !e->connected) fail(MSX_ERR_RUNTIME, "CG context: peers are not connected.");
   cudaStream_t s = e->s;
   const int64_t n = e->n;
+  const bool decide = c.comm == kCommNone;
   MSX_CUDA(cudaEventRecord(e->ev, user_stream));
   MSX_CUDA(cudaStreamWaitEvent(s, e->ev, 0));
   MSX_CUDA(cudaMemcpyAsync(e->b, b_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   MSX_CUDA(cudaMemcpyAsync(e->x, x0_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
-  MSX_CUDA(cudaMemcpyAsync(e->p, x0_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+  MSX_CUDA(cudaMemcpyAsync(e->p[0], x0_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   if (e->kind == kPCG) MSX_CUDA(cudaMemcpyAsync(e->inv, inv_in, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   CgState init{};
   init.status = kStatusRunning;
@@ -862,14 +975,19 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
   init.maxiter = maxiter;
   MSX_CUDA(cudaMemcpyAsync(e->st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
 
-  // r0 = b - A x0 (x0 staged in p, whose halo the exchange fills)
-  engine_exchange(e, e->p, s);
-  spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p, e->ap, e->carry, s);
-  const bool decide = c.comm == kCommNone;
-  init_kernel<<<e->red_grid, kThreads, 0, s>>>(e->kind, e->b, e->x, e->ap, e->inv, e->r, e->z, e->p, n, e->partials,
-                                               e->st, rtol, atol, decide);
+  // r0 = b - A x0 (x0 staged in p[0], whose halo the exchange fills); p[0]
+  // then holds the first direction, whose halo is pushed before iteration 1.
+  if (p2p(e)) {
+    engine_push(e, e->p[0], 0, s);
+    engine_wait(e, s);
+  }
+  engine_exchange_nccl(e, e->p[0], s);
+  spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p[0], e->ap, e->carry, s);
+  init_kernel<<<e->red_grid, kThreads, 0, s>>>(e->kind, e->b, e->x, e->ap, e->inv, e->r, e->z, e->p[0], n,
+                                               e->partials, e->st, rtol, atol, decide, e->link);
   MSX_CHECK_LAUNCH();
-  engine_reduce_decide(e, 0, rtol, atol, s);
+  engine_reduce_decide_nccl(e, 0, rtol, atol, s);
+  if (p2p(e)) engine_push(e, e->p[0], 0, s);
   CgState host{};
   MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
@@ -878,7 +996,7 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
     if (!e->exec) {
       MSX_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
       try {
-        for (int k = 0; k < e->batch; ++k) engine_iteration(e, s);
+        for (int k = 0; k < e->batch; ++k) engine_iteration(e, k & 1, s);
       } catch (...) {
         cudaGraph_t g = nullptr;
         cudaStreamEndCapture(s, &g);
@@ -902,8 +1020,8 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
   MSX_CUDA(cudaMemcpyAsync(x_out, e->x, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   MSX_CUDA(cudaEventRecord(e->ev, s));
   MSX_CUDA(cudaStreamWaitEvent(user_stream, e->ev, 0));
-  if (host.status == kStatusRunning) fail(MSX_ERR_RUNTIME, "CG solve ended without a status (internal error).");
   if (host.status == -4) fail(MSX_ERR_RUNTIME, "CG: a peer did not answer (communication timeout).");
+  if (host.status == kStatusRunning) fail(MSX_ERR_RUNTIME, "CG solve ended without a status (internal error).");
   CgResult res{};
   res.info = host.status;
   res.iterations = host.completed;

@@ -30,12 +30,14 @@ struct CgState {
 
 constexpr int kMaxRanks = 8;  // one node
 
-// Peer-memory mailbox of one rank (IPC-exported): the fp64 partial sums every
-// rank sends it (two slots, alternating by epoch) and the epoch flags of the
-// all-reduce and halo exchanges, written by the senders.
+// Peer-memory mailbox of one rank (IPC-exported), written by the other ranks.
+// `ll` carries the fp64 partial sums of the scalar all-reduce in "flagged
+// words": each 64-bit word is (epoch << 32) | one 32-bit half of a double, so
+// a word is valid exactly when its flag matches and no fence is needed
+// between data and flag. Two slots alternate by epoch parity. `halo_epoch[q]`
+// counts the halo pushes rank q has completed into this rank's vector.
 struct Mailbox {
-  double red[2][kMaxRanks][4];
-  unsigned long long red_epoch[kMaxRanks];
+  unsigned long long ll[2][kMaxRanks][8];
   unsigned long long halo_epoch[kMaxRanks];
 };
 
@@ -47,6 +49,20 @@ struct CommState {
   unsigned int halo_counter;
   int error;  // 1: a peer wait timed out
 };
+
+// What a kernel needs to talk to its peers (passed by value). world == 1
+// means no peer-memory exchange (single GPU, or NCCL between kernels).
+struct P2pLink {
+  Mailbox *mine;
+  Mailbox *peer[kMaxRanks];  // every rank's mailbox, mine at [rank]
+  CommState *cs;
+  int rank, world;
+  int n_recv;                // ranks whose halo pushes this rank waits for
+  int recv[kMaxRanks];
+};
+
+// Bytes of one rank's peer-memory descriptor (msx_cg_context_ipc_handles).
+constexpr int kCgIpcBytes = 256;
 
 // Multi-GPU layout of one rank (row slab with halo columns; see
 // mlx_sparse/distributed.py). Host arrays except send_idx (device).
@@ -109,9 +125,10 @@ struct CgEngineConfig {
 };
 CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t stream);
 void cg_engine_destroy(CgEngine *e);
-// P2P: 2 IPC handles (p buffer, mailbox), 64 bytes each.
-void cg_engine_ipc_handles(CgEngine *e, void *out128);
-void cg_engine_connect(CgEngine *e, const void *all_handles /* world x 128 bytes */);
+// P2P: kCgIpcBytes per rank: IPC handles of the search-direction buffers and
+// the mailbox, and the distance between the two direction buffers.
+void cg_engine_ipc_handles(CgEngine *e, void *out);
+void cg_engine_connect(CgEngine *e, const void *all_handles /* world x kCgIpcBytes */);
 CgResult cg_engine_solve(CgEngine *e, const float *b, const float *x0, const float *inv_diag, float *x_out,
                          float rtol, float atol, int maxiter, cudaStream_t stream);
 

@@ -128,6 +128,7 @@ template <> __device__ __forceinline__ __nv_bfloat16 ld_stream<__nv_bfloat16>(co
 struct NoEpilogue {
   static constexpr int kMinBlocks = 8;  // resident CTAs/SM the kernels aim for
   __device__ __forceinline__ bool skip() const { return false; }
+  __device__ __forceinline__ void begin() {}  // called by every thread after skip()
   __device__ __forceinline__ void row(int64_t, float) {}
   __device__ __forceinline__ void finish() {}
 };

@@ -81,6 +81,7 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
                    const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
   __shared__ float red[kBinThreads / 32];
   if (epi.skip()) return;
+  epi.begin();
   for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
   int bin = 0;
 #pragma unroll
@@ -241,6 +242,7 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
   __shared__ I idx_s[kShortRowsPerBlock * 8];
   __shared__ T val_s[kShortRowsPerBlock * 8];
   if (epi.skip()) return;
+  epi.begin();
   const int tid = threadIdx.x;
   const int64_t nblk = (n_rows + kShortRowsPerBlock - 1) / kShortRowsPerBlock;
   for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {

@@ -204,6 +204,7 @@ class CgContext:
     the context."""
 
     COMM_NONE, COMM_NCCL, COMM_P2P = 0, 1, 2
+    IPC_BYTES = 256  # MSX_CG_IPC_BYTES
 
     def __init__(self, data, indices, indptr, n_owned, n_halo, preconditioned, *, comm=0, rank=0, world=1,
                  nccl_comm=None, peers=None, send_counts=None, recv_counts=None, send_idx=None,
@@ -230,8 +231,8 @@ class CgContext:
         self.handle = h
 
     def ipc_handles(self) -> bytes:
-        buf = ctypes.create_string_buffer(128)
-        check(extension().msx_cg_context_ipc_handles(self.handle, buf, 128))
+        buf = ctypes.create_string_buffer(self.IPC_BYTES)
+        check(extension().msx_cg_context_ipc_handles(self.handle, buf, self.IPC_BYTES))
         return bytes(buf.raw)
 
     def connect(self, all_handles: list) -> None:
