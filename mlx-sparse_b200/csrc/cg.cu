@@ -23,6 +23,7 @@
 // and launched back to back; the host reads the status once per batch.
 // Matrices with rows longer than the CTA bin (split into chunks) run the plain
 // SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 #if defined(MSX_HAVE_NCCL)
@@ -125,13 +126,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long
 // included), then waits, bounded, for the words of all ranks and adds them in
 // rank order, so every rank computes identical scalars. Returns false on a
 // timeout.
-__device__ bool ll_allreduce(CgState *st, const P2pLink &L) {
+__device__ bool ll_allreduce(CgState *st, const P2pLink *L) {
   __shared__ unsigned halves[kMaxRanks][8];
   const int lane = threadIdx.x & 31;
   unsigned epoch = 0;
   if (lane == 0) {
-    epoch = (unsigned)(L.cs->ar_epoch + 1);
-    L.cs->ar_epoch = epoch;
+    epoch = (unsigned)(L->cs->ar_epoch + 1);
+    L->cs->ar_epoch = epoch;
   }
   epoch = __shfl_sync(0xffffffffu, epoch, 0);
   const int slot = (int)(epoch & 1u);
@@ -139,11 +140,11 @@ __device__ bool ll_allreduce(CgState *st, const P2pLink &L) {
   const unsigned long long bits = (unsigned long long)__double_as_longlong(st->red[word >> 1]);
   const unsigned half = (word & 1) ? (unsigned)(bits >> 32) : (unsigned)bits;
   const unsigned long long w = ((unsigned long long)epoch << 32) | half;
-  const int total = 8 * L.world;
-  for (int i = lane; i < total; i += 32) st_relaxed_sys(&L.peer[i >> 3]->ll[slot][L.rank][word], w);
+  const int total = 8 * L->world;
+  for (int i = lane; i < total; i += 32) st_relaxed_sys(&L->peer[i >> 3]->ll[slot][L->rank][word], w);
   bool ok = true;
   for (int i = lane; i < total; i += 32) {
-    const unsigned long long *src = &L.mine->ll[slot][i >> 3][word];
+    const unsigned long long *src = &L->mine->ll[slot][i >> 3][word];
     unsigned long long v = ld_relaxed_sys(src);
     long long polls = 0;
     while ((unsigned)(v >> 32) != epoch) {
@@ -159,7 +160,7 @@ __device__ bool ll_allreduce(CgState *st, const P2pLink &L) {
   __syncwarp();
   if (ok && lane < 4) {
     double sum = 0.0;
-    for (int q = 0; q < L.world; ++q) {
+    for (int q = 0; q < L->world; ++q) {
       const unsigned long long b = ((unsigned long long)halves[q][2 * lane + 1] << 32) | halves[q][2 * lane];
       sum += __longlong_as_double((long long)b);
     }
@@ -172,17 +173,17 @@ __device__ bool ll_allreduce(CgState *st, const P2pLink &L) {
 // The last CTA of a reduction: combine over the ranks (peer memory) and run
 // the decision `f` in one thread. Single GPU: decide directly when `decide`.
 template <typename F>
-__device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partials, CgState *st, const P2pLink &L,
+__device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partials, CgState *st, const P2pLink *L,
                                                   bool decide, F f) {
   if (!reduce_last(v, partials, st)) return;
-  if (L.world > 1) {
+  if (L) {
     if (threadIdx.x < 32) {
       const bool ok = ll_allreduce(st, L);
       if (threadIdx.x == 0) {
         if (ok) {
           f();
         } else {
-          L.cs->error = 1;
+          L->cs->error = 1;
           st->status = -4;  // communication timeout (not a reference status)
         }
       }
@@ -192,59 +193,62 @@ __device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partia
   }
 }
 
-// Waits (thread 0, bounded) until every rank this one receives halo entries
-// from has completed as many pushes as this rank has; then the CTA may read
-// the halo part of the vector. Call from all threads.
-__device__ __forceinline__ void halo_wait_cta(CgState *st, const P2pLink &L) {
-  if (threadIdx.x == 0) {
-    const unsigned long long epoch = L.cs->halo_epoch;
-    for (int k = 0; k < L.n_recv; ++k) {
-      long long polls = 0;
-      while (ld_acquire_sys(&L.mine->halo_epoch[L.recv[k]]) < epoch) {
-        if (++polls > kPeerPollLimit) {
-          L.cs->error = 1;
-          st->status = -4;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
+// ---- halo words ----------------------------------------------------------------
+// Halo column j of the current search direction is the word halo[j] of round r
+// when its flag equals r. Rounds are numbered per solve from
+// st->round_base: 0 for x0, then st->it for the direction iteration `it`
+// reads. A producer only writes round r + 1 after every rank has finished
+// reading round r (the scalar all-reduces in between order them), so one
+// array per rank suffices.
+__device__ __forceinline__ unsigned long long halo_word(unsigned round, float v) {
+  return ((unsigned long long)round << 32) | __float_as_uint(v);
 }
 
-// Where one rank's halo entries go: for each receiving peer, the address in
-// that peer's direction buffer where its entries start, and the prefix of the
-// send counts over the concatenated send list `idx`.
+// Reads halo column j of `round`, waiting (bounded) for the owner's store.
+// On a timeout it marks the solve failed and returns 0.
+__device__ __noinline__ float halo_wait_read(CgState *st, const P2pLink *L, int64_t j, unsigned round) {
+  const unsigned long long *w = L->halo + j;
+  long long polls = 0;
+  while (true) {
+    const unsigned long long v = ld_relaxed_sys(w);
+    if ((unsigned)(v >> 32) == round) return __uint_as_float((unsigned)v);
+    if (++polls > kPeerPollLimit || ((polls & 255) == 0 && *(volatile int *)&L->cs->error)) {
+      L->cs->error = 1;
+      st->status = -4;
+      return 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ float halo_read(CgState *st, const P2pLink *L, int64_t j, unsigned round) {
+  const unsigned long long v = ld_relaxed_sys(L->halo + j);
+  if ((unsigned)(v >> 32) == round) return __uint_as_float((unsigned)v);
+  return halo_wait_read(st, L, j, round);
+}
+
+// Where one rank's halo entries go: for each receiving peer, its halo words
+// where this rank's block starts, and the prefix of the send counts over the
+// concatenated send list `idx`. The first `ctas` CTAs of a kernel push.
 struct PushPlan {
-  float *dst[kMaxRanks];
+  unsigned long long *dst[kMaxRanks];
   long long off[kMaxRanks + 1];
-  int peer[kMaxRanks];
   int n_peers;
+  int ctas;
   const int *idx;
 };
 
-__device__ __forceinline__ int push_peer(const PushPlan &pp, long long j) {
-  int k = 0;
-  while (k + 1 < pp.n_peers && j >= pp.off[k + 1]) ++k;
-  return k;
-}
+__device__ __forceinline__ int push_ctas(const PushPlan *pp) { return min((int)gridDim.x, pp->ctas); }
 
-// After a CTA's pushes: the last CTA to finish raises this rank's halo epoch
-// in the receiving peers' mailboxes. Call from all threads.
-__device__ __forceinline__ void halo_publish(const PushPlan &pp, const P2pLink &L) {
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    last = atomicAdd(&L.cs->halo_counter, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    __threadfence_system();
-    L.cs->halo_counter = 0;
-    const unsigned long long epoch = L.cs->halo_epoch + 1;
-    L.cs->halo_epoch = epoch;
-    for (int k = 0; k < pp.n_peers; ++k) st_release_sys(&L.peer[pp.peer[k]]->halo_epoch[L.rank], epoch);
+// Stores value(i) of round `round` for every send entry i into the peers'
+// halo words (pushing CTAs only). No fence: each word carries its own flag.
+template <typename F> __device__ __forceinline__ void halo_push(const PushPlan *pp, unsigned round, F value) {
+  const int P = push_ctas(pp);
+  if ((int)blockIdx.x >= P) return;
+  const long long ns = pp->off[pp->n_peers];
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < ns; j += (long long)P * blockDim.x) {
+    int k = 0;
+    while (k + 1 < pp->n_peers && j >= pp->off[k + 1]) ++k;
+    st_relaxed_sys(pp->dst[k] + (j - pp->off[k]), halo_word(round, value(pp->idx[j])));
   }
 }
 
@@ -400,7 +404,7 @@ __device__ void decide_pupdate(CgState *st) {
 __global__ void __launch_bounds__(kThreads)
 init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, const float *__restrict__ ap,
             const float *__restrict__ inv_diag, float *__restrict__ r, float *__restrict__ z, float *__restrict__ p,
-            int64_t n, double *partials, CgState *st, float rtol, float atol, bool decide, P2pLink L) {
+            int64_t n, double *partials, CgState *st, float rtol, float atol, bool decide, const P2pLink *L) {
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float bi = b[i];
@@ -432,12 +436,15 @@ struct DotsEpilogue {
   CgState *st;
   int kind;
   bool decide;
-  bool halo_wait;  // peer memory: wait for the peers' halo pushes first
-  P2pLink L;
+  bool halo;       // peer memory: read halo columns from the halo words
+  int64_t n_owned;  // halo columns start here
+  const P2pLink *L;  // null: no peer exchange
   double pap, pp, apap, bad;
+  static constexpr bool kHalo = true;
   __device__ __forceinline__ bool skip() const { return st->status != kStatusRunning; }
-  __device__ __forceinline__ void begin() {
-    if (halo_wait) halo_wait_cta(st, L);
+  __device__ __forceinline__ int64_t halo_from() const { return halo ? n_owned : INT64_MAX; }
+  __device__ __forceinline__ float halo_x(int64_t col) {
+    return halo_read(st, L, col - n_owned, st->round_base + (unsigned)st->it);
   }
   __device__ __forceinline__ void row(int64_t r, float apv) {
     const float pv = __ldg(p + r);
@@ -454,7 +461,7 @@ struct DotsEpilogue {
 
 __global__ void __launch_bounds__(kThreads)
 dots_kernel(int kind, const float *__restrict__ p, const float *__restrict__ ap, int64_t n, double *partials,
-            CgState *st, bool decide, P2pLink L) {
+            CgState *st, bool decide, const P2pLink *L) {
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -470,7 +477,7 @@ dots_kernel(int kind, const float *__restrict__ p, const float *__restrict__ ap,
 __global__ void __launch_bounds__(kThreads)
 update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__restrict__ z,
               const float *__restrict__ p, const float *__restrict__ ap, const float *__restrict__ inv_diag,
-              int64_t n, double *partials, CgState *st, bool decide, P2pLink L) {
+              int64_t n, double *partials, CgState *st, bool decide, const P2pLink *L) {
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   if (kind == kCG) {
@@ -531,70 +538,66 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
 }
 
 // p_next = r + beta p (CG, double) or z + beta p (PCG, float), from p_cur
-// (p_next == p_cur updates in place). Peer memory: the entries the peers read
-// are computed once more from the unchanged inputs and stored straight into
-// the peers' next direction buffers, then published.
+// (p_next == p_cur updates in place). Peer memory: the first pp->ctas CTAs
+// only compute the entries the peers read (from the unchanged inputs) and
+// store them straight into the peers' halo words; the remaining CTAs update
+// this rank's rows, so the pushes overlap the update.
 __global__ void __launch_bounds__(kThreads)
 pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ z, const float *p_cur, float *p_next,
-               int64_t n, double *partials, CgState *st, bool decide, P2pLink L, PushPlan pp) {
+               int64_t n, double *partials, CgState *st, bool decide, const P2pLink *L, const PushPlan *pp) {
   if (st->status != kStatusRunning) return;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const bool push = L.world > 1;
+  const int P = L ? push_ctas(pp) : 0;
+  const bool pusher = (int)blockIdx.x < P;
+  const int64_t stride = (int64_t)(gridDim.x - P) * blockDim.x;
+  const int64_t first = (int64_t)(blockIdx.x - P) * blockDim.x + threadIdx.x;
   if (kind == kCG) {
     const double beta = st->beta_d;
     double v[4] = {0.0, 0.0, 0.0, 0.0};
-    for (int64_t i = first; i < n; i += stride) {
-      const float old = p_cur[i];
-      const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)old));
-      const float pf = __double2float_rn(pc);
-      if (!finite_d(pc) || !finite_f(pf)) {
-        v[0] += 1.0;  // p keeps its value (cg.cpp:238-246)
-        if (p_next != p_cur) p_next[i] = old;
-        continue;
-      }
-      p_next[i] = pf;
-    }
-    if (push) {
-      const long long ns = pp.off[pp.n_peers];
-      for (long long j = first; j < ns; j += stride) {
-        const int k = push_peer(pp, j);
-        const int i = pp.idx[j];
+    if (pusher) {
+      // read by iteration it + 1 (decide_pupdate advances it at the end)
+      halo_push(pp, st->round_base + (unsigned)st->it + 1u, [&](int i) {
         const float old = p_cur[i];
         const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)old));
         const float pf = __double2float_rn(pc);
-        pp.dst[k][j - pp.off[k]] = (!finite_d(pc) || !finite_f(pf)) ? old : pf;
+        return (!finite_d(pc) || !finite_f(pf)) ? old : pf;
+      });
+    } else {
+      for (int64_t i = first; i < n; i += stride) {
+        const float old = p_cur[i];
+        const double pc = __dadd_rn((double)r[i], __dmul_rn(beta, (double)old));
+        const float pf = __double2float_rn(pc);
+        if (!finite_d(pc) || !finite_f(pf)) {
+          v[0] += 1.0;  // p keeps its value (cg.cpp:238-246)
+          if (p_next != p_cur) p_next[i] = old;
+          continue;
+        }
+        p_next[i] = pf;
       }
-      halo_publish(pp, L);
     }
     reduce_and_decide(v, partials, st, L, decide, [&] { decide_pupdate(st); });
-  } else {
-    const float beta = st->beta_f;
-    int64_t done = 0;
-    if (aligned16(z) && aligned16(p_cur) && aligned16(p_next)) {
-      const int64_t n4 = n / 4;
-      for (int64_t i = first; i < n4; i += stride) {
-        const float4 zv = __ldcs(reinterpret_cast<const float4 *>(z) + i);
-        float4 pv = reinterpret_cast<const float4 *>(p_cur)[i];
-        pv.x = __fadd_rn(zv.x, __fmul_rn(beta, pv.x));
-        pv.y = __fadd_rn(zv.y, __fmul_rn(beta, pv.y));
-        pv.z = __fadd_rn(zv.z, __fmul_rn(beta, pv.z));
-        pv.w = __fadd_rn(zv.w, __fmul_rn(beta, pv.w));
-        reinterpret_cast<float4 *>(p_next)[i] = pv;
-      }
-      done = n4 * 4;
-    }
-    for (int64_t i = done + first; i < n; i += stride) p_next[i] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
-    if (push) {
-      const long long ns = pp.off[pp.n_peers];
-      for (long long j = first; j < ns; j += stride) {
-        const int k = push_peer(pp, j);
-        const int i = pp.idx[j];
-        pp.dst[k][j - pp.off[k]] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
-      }
-      halo_publish(pp, L);
-    }
+    return;
   }
+  const float beta = st->beta_f;
+  if (pusher) {
+    // decide_update already advanced it to the iteration that reads p_next
+    halo_push(pp, st->round_base + (unsigned)st->it, [&](int i) { return __fadd_rn(z[i], __fmul_rn(beta, p_cur[i])); });
+    return;
+  }
+  int64_t done = 0;
+  if (aligned16(z) && aligned16(p_cur) && aligned16(p_next)) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = first; i < n4; i += stride) {
+      const float4 zv = __ldcs(reinterpret_cast<const float4 *>(z) + i);
+      float4 pv = reinterpret_cast<const float4 *>(p_cur)[i];
+      pv.x = __fadd_rn(zv.x, __fmul_rn(beta, pv.x));
+      pv.y = __fadd_rn(zv.y, __fmul_rn(beta, pv.y));
+      pv.z = __fadd_rn(zv.z, __fmul_rn(beta, pv.z));
+      pv.w = __fadd_rn(zv.w, __fmul_rn(beta, pv.w));
+      reinterpret_cast<float4 *>(p_next)[i] = pv;
+    }
+    done = n4 * 4;
+  }
+  for (int64_t i = done + first; i < n; i += stride) p_next[i] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
 }
 
 // Multi-GPU: the reductions leave local sums in st->red; after the NCCL
@@ -615,22 +618,22 @@ __global__ void halo_pack_kernel(const float *__restrict__ v, const int *__restr
   if (i < n) out[i] = v[idx[i]];
 }
 
-// Standalone halo push of v's send entries into the peers' buffers (the
-// initial residual; the iterations fuse the push into the direction update).
-__global__ void p2p_halo_push_kernel(CgState *st, const float *__restrict__ v, PushPlan pp, P2pLink L) {
+// Standalone halo push of v's send entries as round `round` (x0 and the first
+// direction; the iterations push from the direction update).
+__global__ void p2p_halo_push_kernel(CgState *st, const float *__restrict__ v, const PushPlan *pp, int round) {
   if (st->status != kStatusRunning) return;
-  const long long ns = pp.off[pp.n_peers];
-  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < ns; j += (long long)gridDim.x * blockDim.x) {
-    const int k = push_peer(pp, j);
-    pp.dst[k][j - pp.off[k]] = v[pp.idx[j]];
-  }
-  halo_publish(pp, L);
+  halo_push(pp, st->round_base + (unsigned)round, [&](int i) { return v[i]; });
 }
 
-// Standalone halo wait (before SpMV kernels that do not wait themselves).
-__global__ void p2p_halo_wait_kernel(CgState *st, P2pLink L) {
+// Copies the halo words of a round (round < 0: the current iteration's) into
+// the halo part of a vector, for SpMV kernels that do not read the words
+// themselves.
+__global__ void p2p_halo_unpack_kernel(CgState *st, const P2pLink *L, float *__restrict__ v_halo, int64_t n_halo,
+                                       int round) {
   if (st->status != kStatusRunning) return;
-  halo_wait_cta(st, L);
+  const unsigned r = st->round_base + (unsigned)(round >= 0 ? round : st->it);
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n_halo; j += (int64_t)gridDim.x * blockDim.x)
+    v_halo[j] = halo_read(st, L, j, r);
 }
 
 int elementwise_grid(int64_t n) {
@@ -658,8 +661,10 @@ struct CgEngine {
   int red_grid = 1;
   void *plan_mem = nullptr;
   void *mem = nullptr;       // state, partials, vectors (one allocation)
-  float *pbuf = nullptr;     // direction buffer(s), own allocation (IPC-exported in P2P mode)
+  float *pbuf = nullptr;     // direction buffer(s)
   float *p[2] = {};          // P2P: two buffers, alternating by iteration parity; else p[0] == p[1]
+  unsigned long long *halo_words = nullptr;  // P2P: own allocation, IPC-exported
+  unsigned round_base = 1;   // P2P: halo round 0 of the next solve (identical on every rank)
   int64_t p_stride = 0;      // elements between p[0] and p[1]
   Mailbox *mbox = nullptr;   // own allocation (IPC-exported in P2P mode)
   CgState *st = nullptr;
@@ -669,8 +674,10 @@ struct CgEngine {
   float *sendbuf = nullptr;
   int64_t n_send = 0;
   // P2P
-  P2pLink link{};            // world == 1 unless P2P
-  PushPlan push[2] = {};     // by parity of the destination buffer
+  P2pLink link{};            // host copy
+  PushPlan push{};           // host copy
+  P2pLink *link_dev = nullptr;   // device copies (P2P only)
+  PushPlan *push_dev = nullptr;
   int push_grid = 1;
   void *opened[2 * kMaxRanks] = {};
   bool connected = false;
@@ -685,6 +692,8 @@ struct CgEngine {
 namespace {
 
 bool p2p(const CgEngine *e) { return e->cfg.comm == kCommP2p; }
+const P2pLink *link_of(const CgEngine *e) { return p2p(e) ? e->link_dev : nullptr; }
+const PushPlan *push_of(const CgEngine *e) { return p2p(e) ? e->push_dev : nullptr; }
 
 // NCCL halo exchange of v (owned part -> peers' halo part).
 void engine_exchange_nccl(CgEngine *e, float *v, cudaStream_t q) {
@@ -717,14 +726,19 @@ void engine_exchange_nccl(CgEngine *e, float *v, cudaStream_t q) {
 #endif
 }
 
-// Peer memory: push v's send entries into the peers' buffers of parity `par`.
-void engine_push(CgEngine *e, const float *v, int par, cudaStream_t q) {
-  p2p_halo_push_kernel<<<e->push_grid, kThreads, 0, q>>>(e->st, v, e->push[par], e->link);
+// Peer memory: push v's send entries into the peers' halo words as `round`.
+void engine_push(CgEngine *e, const float *v, int round, cudaStream_t q) {
+  p2p_halo_push_kernel<<<e->push_grid, kThreads, 0, q>>>(e->st, v, push_of(e), round);
   MSX_CHECK_LAUNCH();
 }
 
-void engine_wait(CgEngine *e, cudaStream_t q) {
-  p2p_halo_wait_kernel<<<1, 32, 0, q>>>(e->st, e->link);
+// Peer memory: copy the halo words of `round` (< 0: the current iteration's)
+// into v's halo part.
+void engine_unpack(CgEngine *e, float *v, int round, cudaStream_t q) {
+  const int64_t nh = e->cfg.n_halo;
+  if (nh == 0) return;
+  p2p_halo_unpack_kernel<<<(unsigned)std::min<int64_t>(ceil_div(nh, kThreads), 1024), kThreads, 0, q>>>(
+      e->st, link_of(e), v + e->n, nh, round);
   MSX_CHECK_LAUNCH();
 }
 
@@ -756,26 +770,28 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   const int kind = e->kind;
   float *pc = e->p[par], *pn = e->p[par ^ 1];
   engine_exchange_nccl(e, pc, q);
+  // the short-row SpMV reads the halo words itself; other kernels get them unpacked
+  const bool words_in_spmv = p2p(e) && e->fused && short_rows_plan(e->plan);
+  if (p2p(e) && !words_in_spmv) engine_unpack(e, pc, -1, q);
   if (e->fused) {
     dispatch_index(c.index_dtype, [&](auto ityp) {
       using I = decltype(ityp);
-      DotsEpilogue epi{pc, e->partials, e->st, kind, decide, p2p(e), e->link, 0.0, 0.0, 0.0, 0.0};
+      DotsEpilogue epi{pc, e->partials, e->st, kind, decide, words_in_spmv, e->n, link_of(e), 0.0, 0.0, 0.0, 0.0};
       launch_spmv_binned<float, I, DotsEpilogue>(e->plan, c.data, static_cast<const I *>(c.indices),
                                                  static_cast<const I *>(c.indptr), pc, e->ap, e->carry, epi, q);
     });
   } else {
-    if (p2p(e)) engine_wait(e, q);
     spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, pc, e->ap, e->carry, q);
-    dots_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, pc, e->ap, e->n, e->partials, e->st, decide, e->link);
+    dots_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, pc, e->ap, e->n, e->partials, e->st, decide, link_of(e));
     MSX_CHECK_LAUNCH();
   }
   engine_reduce_decide_nccl(e, 1, 0.f, 0.f, q);
   update_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->x, e->r, e->z, pc, e->ap, e->inv, e->n, e->partials, e->st,
-                                                 decide, e->link);
+                                                 decide, link_of(e));
   MSX_CHECK_LAUNCH();
   engine_reduce_decide_nccl(e, 2, 0.f, 0.f, q);
-  pupdate_kernel<<<std::max(e->red_grid, p2p(e) ? e->push_grid : 1), kThreads, 0, q>>>(
-      kind, e->r, e->z, pc, pn, e->n, e->partials, e->st, decide, e->link, e->push[par ^ 1]);
+  pupdate_kernel<<<e->red_grid + (p2p(e) ? e->push_grid : 0), kThreads, 0, q>>>(kind, e->r, e->z, pc, pn, e->n, e->partials, e->st, decide,
+                                                  link_of(e), push_of(e));
   MSX_CHECK_LAUNCH();
   if (kind == kCG) engine_reduce_decide_nccl(e, 3, 0.f, 0.f, q);
 }
@@ -788,9 +804,9 @@ template <typename T> T *bump(char *&cur, size_t count) {
 
 // Layout of one rank's peer-memory descriptor.
 struct IpcBlob {
-  cudaIpcMemHandle_t p;
+  cudaIpcMemHandle_t halo;
   cudaIpcMemHandle_t mbox;
-  int64_t p_stride;
+  int64_t n_owned;
 };
 static_assert(sizeof(IpcBlob) <= kCgIpcBytes, "descriptor too large");
 
@@ -828,14 +844,17 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
     spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(E->plan), binned_grid<float, I, NoEpilogue>(E->plan));
   });
   for (int k = 0; k < cfg.n_peers; ++k) E->n_send += cfg.send_counts[k];
-  E->push_grid = elementwise_grid(std::max<int64_t>(E->n_send, 1));
-  const int64_t max_grid = std::max<int64_t>(std::max<int64_t>(E->red_grid, E->push_grid), spmv_grid_n);
+  // pushing CTAs: about 512 entries each (MSX_P2P_PUSH_PER_CTA overrides)
+  int64_t per_cta = 2 * kThreads;
+  if (const char *v = std::getenv("MSX_P2P_PUSH_PER_CTA")) per_cta = std::max<int64_t>(kThreads, std::atoll(v));
+  E->push_grid = (int)std::min<int64_t>(std::max<int64_t>(ceil_div(E->n_send, per_cta), 1), E->red_grid);
+  const int64_t max_grid = std::max<int64_t>(E->red_grid + E->push_grid, spmv_grid_n);
   const size_t vec = (size_t)std::max<int64_t>(E->n, 1);
   size_t bytes = 0;
   auto sz = [](size_t b) { return (b + 255) & ~size_t(255); };
   bytes += sz(sizeof(CgState)) + sz(sizeof(CommState)) + sz(sizeof(double) * 4 * max_grid) +
            sz(sizeof(float) * std::max<int64_t>(E->plan.n_chunks, 1)) + 6 * sz(sizeof(float) * vec) +
-           sz(sizeof(float) * std::max<int64_t>(E->n_send, 1));
+           sz(sizeof(float) * std::max<int64_t>(E->n_send, 1)) + sz(sizeof(P2pLink)) + sz(sizeof(PushPlan));
   MSX_CUDA(cudaMalloc(&E->mem, bytes));
   MSX_CUDA(cudaMemsetAsync(E->mem, 0, bytes, s));
   char *cur = static_cast<char *>(E->mem);
@@ -850,16 +869,24 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   E->b = bump<float>(cur, vec);
   E->inv = bump<float>(cur, vec);
   E->sendbuf = bump<float>(cur, std::max<int64_t>(E->n_send, 1));
+  E->link_dev = bump<P2pLink>(cur, 1);
+  E->push_dev = bump<PushPlan>(cur, 1);
   // direction buffers: two (16-byte aligned apart) in P2P mode
   const int64_t cols = std::max<int64_t>(E->n_cols, 1);
-  E->p_stride = cfg.comm == kCommP2p ? (cols + 63) / 64 * 64 : 0;
-  const int64_t p_elems = cfg.comm == kCommP2p ? 2 * E->p_stride : cols;
+  const bool dbl = cfg.comm == kCommP2p;
+  E->p_stride = dbl ? (cols + 63) / 64 * 64 : 0;
+  const int64_t p_elems = dbl ? 2 * E->p_stride : cols;
   MSX_CUDA(cudaMalloc(&E->pbuf, sizeof(float) * (size_t)p_elems));
   MSX_CUDA(cudaMemsetAsync(E->pbuf, 0, sizeof(float) * (size_t)p_elems, s));
   E->p[0] = E->pbuf;
   E->p[1] = E->pbuf + E->p_stride;
   MSX_CUDA(cudaMalloc(&E->mbox, sizeof(Mailbox)));
   MSX_CUDA(cudaMemsetAsync(E->mbox, 0, sizeof(Mailbox), s));
+  if (cfg.comm == kCommP2p) {
+    const size_t hb = sizeof(unsigned long long) * (size_t)std::max<int64_t>(cfg.n_halo, 1);
+    MSX_CUDA(cudaMalloc(&E->halo_words, hb));
+    MSX_CUDA(cudaMemsetAsync(E->halo_words, 0, hb, s));  // flag 0: no round (rounds start at 1)
+  }
   if (!cfg.preconditioned) E->z = nullptr, E->inv = nullptr;
   MSX_CUDA(cudaMallocHost(&E->status_host, sizeof(int)));
   E->link.world = 1;
@@ -869,8 +896,8 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   if (cfg.comm == kCommP2p) {
     E->link.world = cfg.world;
     E->link.rank = cfg.rank;
-    for (int k = 0; k < cfg.n_peers; ++k)
-      if (cfg.recv_counts[k] > 0) E->link.recv[E->link.n_recv++] = cfg.peers[k];
+    E->link.halo = E->halo_words;
+    E->link.n_owned = E->n;
   }
   // Iterations per graph launch: about a millisecond of work per batch, even
   // (P2P alternates the direction buffers).
@@ -893,6 +920,7 @@ void cg_engine_destroy(CgEngine *e) {
     if (p) cudaIpcCloseMemHandle(p);
   if (e->status_host) cudaFreeHost(e->status_host);
   if (e->pbuf) cudaFree(e->pbuf);
+  if (e->halo_words) cudaFree(e->halo_words);
   if (e->mbox) cudaFree(e->mbox);
   if (e->mem) cudaFree(e->mem);
   if (e->plan_mem) cudaFree(e->plan_mem);
@@ -903,10 +931,11 @@ void cg_engine_destroy(CgEngine *e) {
 }
 
 void cg_engine_ipc_handles(CgEngine *e, void *out) {
+  if (!p2p(e)) fail(MSX_ERR_INVALID, "CG context: IPC handles are for the peer-memory mode.");
   IpcBlob blob{};
-  MSX_CUDA(cudaIpcGetMemHandle(&blob.p, e->pbuf));
+  MSX_CUDA(cudaIpcGetMemHandle(&blob.halo, e->halo_words));
   MSX_CUDA(cudaIpcGetMemHandle(&blob.mbox, e->mbox));
-  blob.p_stride = e->p_stride;
+  blob.n_owned = e->n;
   std::memset(out, 0, kCgIpcBytes);
   std::memcpy(out, &blob, sizeof(blob));
 }
@@ -916,43 +945,46 @@ void cg_engine_connect(CgEngine *e, const void *all_handles) {
   if (c.comm != kCommP2p) fail(MSX_ERR_INVALID, "CG context: connect is for the peer-memory mode.");
   if (e->connected) fail(MSX_ERR_INVALID, "CG context: already connected.");
   const char *raw = static_cast<const char *>(all_handles);
-  float *pb[kMaxRanks] = {};
-  int64_t stride[kMaxRanks] = {};
+  unsigned long long *hw[kMaxRanks] = {};
+  int64_t owned[kMaxRanks] = {};
   for (int q = 0; q < c.world; ++q) {
     IpcBlob blob;
     std::memcpy(&blob, raw + (size_t)q * kCgIpcBytes, sizeof(blob));
-    stride[q] = blob.p_stride;
+    owned[q] = blob.n_owned;
     if (q == c.rank) {
       e->link.peer[q] = e->mbox;
-      pb[q] = e->pbuf;
+      hw[q] = e->halo_words;
       continue;
     }
-    void *pp = nullptr, *mb = nullptr;
-    MSX_CUDA(cudaIpcOpenMemHandle(&pp, blob.p, cudaIpcMemLazyEnablePeerAccess));
-    e->opened[2 * q] = pp;
+    void *hp = nullptr, *mb = nullptr;
+    MSX_CUDA(cudaIpcOpenMemHandle(&hp, blob.halo, cudaIpcMemLazyEnablePeerAccess));
+    e->opened[2 * q] = hp;
     MSX_CUDA(cudaIpcOpenMemHandle(&mb, blob.mbox, cudaIpcMemLazyEnablePeerAccess));
     e->opened[2 * q + 1] = mb;
     e->link.peer[q] = static_cast<Mailbox *>(mb);
-    pb[q] = static_cast<float *>(pp);
+    hw[q] = static_cast<unsigned long long *>(hp);
   }
-  for (int par = 0; par < 2; ++par) {
-    PushPlan pp{};
-    long long off = 0;
-    int np = 0;
-    for (int k = 0; k < c.n_peers; ++k) {
-      if (c.send_counts[k] == 0) continue;  // that peer waits for no flag of this rank
-      const int q = c.peers[k];
-      pp.dst[np] = pb[q] + par * stride[q] + c.peer_dst_offset[k];
-      pp.peer[np] = q;
-      pp.off[np] = off;
-      off += c.send_counts[k];
-      ++np;
-    }
+  PushPlan pp{};
+  long long off = 0;
+  int np = 0;
+  for (int k = 0; k < c.n_peers; ++k) {
+    if (c.send_counts[k] == 0) continue;
+    const int q = c.peers[k];
+    const int64_t h0 = c.peer_dst_offset[k] - owned[q];  // first halo slot of this rank's block at q
+    if (h0 < 0) fail(MSX_ERR_INVALID, "CG context: a landing offset lies inside the peer's owned rows.");
+    pp.dst[np] = hw[q] + h0;
     pp.off[np] = off;
-    pp.n_peers = np;
-    pp.idx = c.send_idx;
-    e->push[par] = pp;
+    off += c.send_counts[k];
+    ++np;
   }
+  pp.off[np] = off;
+  pp.n_peers = np;
+  pp.ctas = e->push_grid;
+  pp.idx = c.send_idx;
+  e->push = pp;
+  MSX_CUDA(cudaMemcpyAsync(e->link_dev, &e->link, sizeof(P2pLink), cudaMemcpyHostToDevice, e->s));
+  MSX_CUDA(cudaMemcpyAsync(e->push_dev, &e->push, sizeof(PushPlan), cudaMemcpyHostToDevice, e->s));
+  MSX_CUDA(cudaStreamSynchronize(e->s));
   e->connected = true;
 }
 
@@ -973,21 +1005,22 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
   init.status = kStatusRunning;
   init.it = 1;
   init.maxiter = maxiter;
+  init.round_base = e->round_base;
   MSX_CUDA(cudaMemcpyAsync(e->st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
 
   // r0 = b - A x0 (x0 staged in p[0], whose halo the exchange fills); p[0]
   // then holds the first direction, whose halo is pushed before iteration 1.
   if (p2p(e)) {
     engine_push(e, e->p[0], 0, s);
-    engine_wait(e, s);
+    engine_unpack(e, e->p[0], 0, s);
   }
   engine_exchange_nccl(e, e->p[0], s);
   spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, e->p[0], e->ap, e->carry, s);
   init_kernel<<<e->red_grid, kThreads, 0, s>>>(e->kind, e->b, e->x, e->ap, e->inv, e->r, e->z, e->p[0], n,
-                                               e->partials, e->st, rtol, atol, decide, e->link);
+                                               e->partials, e->st, rtol, atol, decide, link_of(e));
   MSX_CHECK_LAUNCH();
   engine_reduce_decide_nccl(e, 0, rtol, atol, s);
-  if (p2p(e)) engine_push(e, e->p[0], 0, s);
+  if (p2p(e)) engine_push(e, e->p[0], 1, s);  // read by iteration 1
   CgState host{};
   MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
@@ -1017,6 +1050,8 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
     MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
     MSX_CUDA(cudaStreamSynchronize(s));
   }
+  // rounds 0 .. completed + 1 were used; the next solve starts past them
+  e->round_base += (unsigned)host.completed + 3u;
   MSX_CUDA(cudaMemcpyAsync(x_out, e->x, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
   MSX_CUDA(cudaEventRecord(e->ev, s));
   MSX_CUDA(cudaStreamWaitEvent(user_stream, e->ev, 0));

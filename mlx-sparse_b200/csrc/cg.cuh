@@ -25,28 +25,29 @@ struct CgState {
   int it;             // index of the iteration being run (1-based)
   int maxiter;
   unsigned int counter;  // last-block-done counter of the reductions
-  int pad[3];
+  unsigned int round_base;  // peer memory: flag of this solve's halo round 0
+  int pad[2];
 };
 
 constexpr int kMaxRanks = 8;  // one node
 
-// Peer-memory mailbox of one rank (IPC-exported), written by the other ranks.
-// `ll` carries the fp64 partial sums of the scalar all-reduce in "flagged
-// words": each 64-bit word is (epoch << 32) | one 32-bit half of a double, so
-// a word is valid exactly when its flag matches and no fence is needed
-// between data and flag. Two slots alternate by epoch parity. `halo_epoch[q]`
-// counts the halo pushes rank q has completed into this rank's vector.
+// Peer-memory mailbox of one rank (IPC-exported), written by the other ranks:
+// the fp64 partial sums of the scalar all-reduce in "flagged words" - each
+// 64-bit word is (epoch << 32) | one 32-bit half of a double, so a word is
+// valid exactly when its flag matches and no fence is needed between data and
+// flag. Two slots alternate by epoch parity.
+//
+// The halo of the search direction travels the same way: each rank owns an
+// IPC-exported array of n_halo flagged words (round << 32) | float bits, which
+// its peers store into directly and which the SpMV reads (and checks) in place.
 struct Mailbox {
   unsigned long long ll[2][kMaxRanks][8];
-  unsigned long long halo_epoch[kMaxRanks];
 };
 
 // Counters that persist across solves of one context (never reset, so flags
 // in peers' mailboxes stay monotonic).
 struct CommState {
   unsigned long long ar_epoch;
-  unsigned long long halo_epoch;
-  unsigned int halo_counter;
   int error;  // 1: a peer wait timed out
 };
 
@@ -56,9 +57,9 @@ struct P2pLink {
   Mailbox *mine;
   Mailbox *peer[kMaxRanks];  // every rank's mailbox, mine at [rank]
   CommState *cs;
+  const unsigned long long *halo;  // this rank's halo words
+  int64_t n_owned;           // halo column j is local column n_owned + j
   int rank, world;
-  int n_recv;                // ranks whose halo pushes this rank waits for
-  int recv[kMaxRanks];
 };
 
 // Bytes of one rank's peer-memory descriptor (msx_cg_context_ipc_handles).
@@ -125,8 +126,8 @@ struct CgEngineConfig {
 };
 CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t stream);
 void cg_engine_destroy(CgEngine *e);
-// P2P: kCgIpcBytes per rank: IPC handles of the search-direction buffers and
-// the mailbox, and the distance between the two direction buffers.
+// P2P: kCgIpcBytes per rank: IPC handles of the halo words and the mailbox,
+// and the rank's owned length.
 void cg_engine_ipc_handles(CgEngine *e, void *out);
 void cg_engine_connect(CgEngine *e, const void *all_handles /* world x kCgIpcBytes */);
 CgResult cg_engine_solve(CgEngine *e, const float *b, const float *x0, const float *inv_diag, float *x_out,

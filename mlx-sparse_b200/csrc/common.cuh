@@ -128,7 +128,11 @@ template <> __device__ __forceinline__ __nv_bfloat16 ld_stream<__nv_bfloat16>(co
 struct NoEpilogue {
   static constexpr int kMinBlocks = 8;  // resident CTAs/SM the kernels aim for
   __device__ __forceinline__ bool skip() const { return false; }
-  __device__ __forceinline__ void begin() {}  // called by every thread after skip()
+  // kHalo: columns >= halo_from() are read through halo_x() (multi-GPU
+  // halo words) instead of from x (short-row kernel only).
+  static constexpr bool kHalo = false;
+  __device__ __forceinline__ int64_t halo_from() const { return INT64_MAX; }
+  __device__ __forceinline__ float halo_x(int64_t) { return 0.f; }
   __device__ __forceinline__ void row(int64_t, float) {}
   __device__ __forceinline__ void finish() {}
 };

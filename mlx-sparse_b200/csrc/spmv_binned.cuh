@@ -81,7 +81,6 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
                    const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
   __shared__ float red[kBinThreads / 32];
   if (epi.skip()) return;
-  epi.begin();
   for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
   int bin = 0;
 #pragma unroll
@@ -242,7 +241,7 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
   __shared__ I idx_s[kShortRowsPerBlock * 8];
   __shared__ T val_s[kShortRowsPerBlock * 8];
   if (epi.skip()) return;
-  epi.begin();
+  const int64_t halo_from = epi.halo_from();  // multi-GPU: halo columns come from the epilogue
   const int tid = threadIdx.x;
   const int64_t nblk = (n_rows + kShortRowsPerBlock - 1) / kShortRowsPerBlock;
   for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
@@ -270,7 +269,13 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
       float xv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) xv[u] = VT<T>::load(__ldg(x + idx_s[q0 + u]));
+        if (q0 + u < q1) {
+          const I c = idx_s[q0 + u];
+          if constexpr (Epi::kHalo)
+            xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
+          else
+            xv[u] = VT<T>::load(__ldg(x + c));
+        }
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
