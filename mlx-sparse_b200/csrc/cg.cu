@@ -23,6 +23,7 @@
 // and launched back to back; the host reads the status once per batch.
 // Matrices with rows longer than the CTA bin (split into chunks) run the plain
 // SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -104,14 +105,6 @@ __device__ bool reduce_last(double (&v)[4], double *partials, CgState *st) {
 // ---- peer memory (one node, NVLink) ------------------------------------------------
 constexpr long long kPeerPollLimit = 1ll << 24;
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -405,6 +398,8 @@ __global__ void __launch_bounds__(kThreads)
 init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, const float *__restrict__ ap,
             const float *__restrict__ inv_diag, float *__restrict__ r, float *__restrict__ z, float *__restrict__ p,
             int64_t n, double *partials, CgState *st, float rtol, float atol, bool decide, const P2pLink *L) {
+  pdl_wait();
+  pdl_trigger();
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float bi = b[i];
@@ -429,7 +424,7 @@ init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, 
 
 // Fuses p.Ap, p.p, Ap.Ap (and the non-finite count) into the SpMV row
 // epilogue; the last CTA makes the step decision.
-struct DotsEpilogue {
+template <bool kHaloWords> struct DotsEpilogueT {
   static constexpr int kMinBlocks = 6;  // room for the fp64 accumulators
   const float *p;
   double *partials;
@@ -440,7 +435,7 @@ struct DotsEpilogue {
   int64_t n_owned;  // halo columns start here
   const P2pLink *L;  // null: no peer exchange
   double pap, pp, apap, bad;
-  static constexpr bool kHalo = true;
+  static constexpr bool kHalo = kHaloWords;
   __device__ __forceinline__ bool skip() const { return st->status != kStatusRunning; }
   __device__ __forceinline__ int64_t halo_from() const { return halo ? n_owned : INT64_MAX; }
   __device__ __forceinline__ float halo_x(int64_t col) {
@@ -462,6 +457,8 @@ struct DotsEpilogue {
 __global__ void __launch_bounds__(kThreads)
 dots_kernel(int kind, const float *__restrict__ p, const float *__restrict__ ap, int64_t n, double *partials,
             CgState *st, bool decide, const P2pLink *L) {
+  pdl_wait();
+  pdl_trigger();
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -478,6 +475,8 @@ __global__ void __launch_bounds__(kThreads)
 update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__restrict__ z,
               const float *__restrict__ p, const float *__restrict__ ap, const float *__restrict__ inv_diag,
               int64_t n, double *partials, CgState *st, bool decide, const P2pLink *L) {
+  pdl_wait();
+  pdl_trigger();
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   if (kind == kCG) {
@@ -545,6 +544,8 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
 __global__ void __launch_bounds__(kThreads)
 pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ z, const float *p_cur, float *p_next,
                int64_t n, double *partials, CgState *st, bool decide, const P2pLink *L, const PushPlan *pp) {
+  pdl_wait();
+  pdl_trigger();
   if (st->status != kStatusRunning) return;
   const int P = L ? push_ctas(pp) : 0;
   const bool pusher = (int)blockIdx.x < P;
@@ -686,6 +687,7 @@ struct CgEngine {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int batch = 4;
+  bool pdl = false;          // programmatic dependent launch inside the iteration graph (MSX_CG_PDL=1)
   int *status_host = nullptr;
 };
 
@@ -768,6 +770,8 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   const CgEngineConfig &c = e->cfg;
   const bool decide = c.comm == kCommNone;
   const int kind = e->kind;
+  // kernels follow kernels directly (no NCCL call in between): overlap launches
+  const bool pdl = c.comm != kCommNccl && e->pdl;
   float *pc = e->p[par], *pn = e->p[par ^ 1];
   engine_exchange_nccl(e, pc, q);
   // the short-row SpMV reads the halo words itself; other kernels get them unpacked
@@ -776,9 +780,14 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   if (e->fused) {
     dispatch_index(c.index_dtype, [&](auto ityp) {
       using I = decltype(ityp);
-      DotsEpilogue epi{pc, e->partials, e->st, kind, decide, words_in_spmv, e->n, link_of(e), 0.0, 0.0, 0.0, 0.0};
-      launch_spmv_binned<float, I, DotsEpilogue>(e->plan, c.data, static_cast<const I *>(c.indices),
-                                                 static_cast<const I *>(c.indptr), pc, e->ap, e->carry, epi, q);
+      auto run = [&](auto epi) {
+        launch_spmv_binned<float, I, decltype(epi)>(e->plan, c.data, static_cast<const I *>(c.indices),
+                                                    static_cast<const I *>(c.indptr), pc, e->ap, e->carry, epi, q, pdl);
+      };
+      if (words_in_spmv)
+        run(DotsEpilogueT<true>{pc, e->partials, e->st, kind, decide, true, e->n, link_of(e), 0.0, 0.0, 0.0, 0.0});
+      else
+        run(DotsEpilogueT<false>{pc, e->partials, e->st, kind, decide, false, e->n, link_of(e), 0.0, 0.0, 0.0, 0.0});
     });
   } else {
     spmv_binned_run(MSX_F32, c.index_dtype, e->plan, c.data, c.indices, c.indptr, pc, e->ap, e->carry, q);
@@ -786,13 +795,11 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
     MSX_CHECK_LAUNCH();
   }
   engine_reduce_decide_nccl(e, 1, 0.f, 0.f, q);
-  update_kernel<<<e->red_grid, kThreads, 0, q>>>(kind, e->x, e->r, e->z, pc, e->ap, e->inv, e->n, e->partials, e->st,
-                                                 decide, link_of(e));
-  MSX_CHECK_LAUNCH();
+  launch(update_kernel, dim3(e->red_grid), dim3(kThreads), 0, q, pdl, kind, e->x, e->r, e->z, pc, e->ap, e->inv, e->n,
+         e->partials, e->st, decide, link_of(e));
   engine_reduce_decide_nccl(e, 2, 0.f, 0.f, q);
-  pupdate_kernel<<<e->red_grid + (p2p(e) ? e->push_grid : 0), kThreads, 0, q>>>(kind, e->r, e->z, pc, pn, e->n, e->partials, e->st, decide,
-                                                  link_of(e), push_of(e));
-  MSX_CHECK_LAUNCH();
+  launch(pupdate_kernel, dim3(e->red_grid + (p2p(e) ? e->push_grid : 0)), dim3(kThreads), 0, q, pdl, kind, e->r, e->z,
+         pc, pn, e->n, e->partials, e->st, decide, link_of(e), push_of(e));
   if (kind == kCG) engine_reduce_decide_nccl(e, 3, 0.f, 0.f, q);
 }
 
@@ -841,7 +848,9 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   int64_t spmv_grid_n = 0;
   dispatch_index(cfg.index_dtype, [&](auto ityp) {
     using I = decltype(ityp);
-    spmv_grid_n = std::max(binned_grid<float, I, DotsEpilogue>(E->plan), binned_grid<float, I, NoEpilogue>(E->plan));
+    spmv_grid_n = std::max({binned_grid<float, I, DotsEpilogueT<true>>(E->plan),
+                            binned_grid<float, I, DotsEpilogueT<false>>(E->plan),
+                            binned_grid<float, I, NoEpilogue>(E->plan)});
   });
   for (int k = 0; k < cfg.n_peers; ++k) E->n_send += cfg.send_counts[k];
   // pushing CTAs: about 512 entries each (MSX_P2P_PUSH_PER_CTA overrides)
@@ -904,6 +913,7 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   const double bytes_per_iter = 8.0 * cfg.nnz + 56.0 * E->n;
   int batch = (int)std::max(1.0, std::min(64.0, 5.0e9 * 1e-3 / std::max(bytes_per_iter, 1.0)));
   E->batch = std::max(4, (batch + 1) & ~1);
+  if (const char *v = std::getenv("MSX_CG_PDL")) E->pdl = std::atoi(v) != 0;
   MSX_CUDA(cudaStreamSynchronize(s));
   return e.release();
 }

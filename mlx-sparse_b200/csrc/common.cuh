@@ -39,6 +39,30 @@ struct Error : public std::runtime_error {
 
 #define MSX_CHECK_LAUNCH() MSX_CUDA(cudaGetLastError())
 
+// Programmatic dependent launch. A kernel launched with launch(..., pdl=true)
+// may be scheduled while the previous kernel in the stream drains; it must call
+// pdl_wait() before touching anything that kernel wrote. Kernels call
+// pdl_trigger() as soon as they start, so their successor's CTAs fill the SMs
+// their own CTAs free. Both are no-ops for ordinary launches.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+            Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  MSX_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 void set_last_error(const std::string &msg);
 
 template <typename Fn> int guarded(Fn &&fn) {

@@ -80,6 +80,8 @@ spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, co
                    const int64_t *__restrict__ chunk_row, const int64_t *__restrict__ chunk_lo,
                    const int64_t *__restrict__ chunk_hi, float *__restrict__ carry, Epi epi) {
   __shared__ float red[kBinThreads / 32];
+  pdl_wait();
+  pdl_trigger();
   if (epi.skip()) return;
   for (long long b = blockIdx.x; b < info.block_start[kBins]; b += gridDim.x) {
   int bin = 0;
@@ -240,6 +242,8 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
   __shared__ I ptr_s[kShortRowsPerBlock + 1];
   __shared__ I idx_s[kShortRowsPerBlock * 8];
   __shared__ T val_s[kShortRowsPerBlock * 8];
+  pdl_wait();
+  pdl_trigger();
   if (epi.skip()) return;
   const int64_t halo_from = epi.halo_from();  // multi-GPU: halo columns come from the epilogue
   const int tid = threadIdx.x;
@@ -332,18 +336,16 @@ int64_t binned_grid(const BinnedPlan &plan) {
 
 template <typename T, typename I, typename Epi>
 void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices, const I *indptr, const T *x, T *y,
-                        float *carry, Epi epi, cudaStream_t stream) {
+                        float *carry, Epi epi, cudaStream_t stream, bool pdl = false) {
   const int64_t grid = binned_grid<T, I, Epi>(plan);
   if (grid == 0) return;
   if (short_rows_plan(plan)) {
-    spmv_short_kernel<T, I, Epi><<<(unsigned)grid, kShortRowsPerBlock, 0, stream>>>(data, indices, indptr, x, y,
-                                                                                  plan.n_rows, epi);
-    MSX_CHECK_LAUNCH();
+    launch(spmv_short_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock), 0, stream, pdl, data, indices,
+           indptr, x, y, plan.n_rows, epi);
     return;
   }
-  spmv_binned_kernel<T, I, Epi><<<(unsigned)grid, kBinThreads, 0, stream>>>(
-      data, indices, indptr, x, y, plan.rows, plan.info, plan.chunk_row, plan.chunk_lo, plan.chunk_hi, carry, epi);
-  MSX_CHECK_LAUNCH();
+  launch(spmv_binned_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kBinThreads), 0, stream, pdl, data, indices, indptr,
+         x, y, plan.rows, plan.info, plan.chunk_row, plan.chunk_lo, plan.chunk_hi, carry, epi);
 }
 
 template <typename T>
