@@ -436,6 +436,7 @@ template <bool kHaloWords> struct DotsEpilogueT {
   const P2pLink *L;  // null: no peer exchange
   double pap, pp, apap, bad;
   static constexpr bool kHalo = kHaloWords;
+  static constexpr bool kShortPipe = true;  // measured faster inside the CG iteration (256^3: 61.3 vs 64.0 ms)
   __device__ __forceinline__ bool skip() const { return st->status != kStatusRunning; }
   __device__ __forceinline__ int64_t halo_from() const { return halo ? n_owned : INT64_MAX; }
   __device__ __forceinline__ float halo_x(int64_t col) {

@@ -155,6 +155,7 @@ struct NoEpilogue {
   // kHalo: columns >= halo_from() are read through halo_x() (multi-GPU
   // halo words) instead of from x (short-row kernel only).
   static constexpr bool kHalo = false;
+  static constexpr bool kShortPipe = false;  // always use the pipelined short-row kernel
   __device__ __forceinline__ int64_t halo_from() const { return INT64_MAX; }
   __device__ __forceinline__ float halo_x(int64_t) { return 0.f; }
   __device__ __forceinline__ void row(int64_t, float) {}

@@ -80,7 +80,7 @@ __device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
 // shuffles and issues kUnroll independent RHS gathers per lane before
 // accumulating, so each lane keeps several 16-byte gathers in flight. The
 // nonzeros are still consumed strictly in order (the reference's order).
-template <typename T, typename I, int V, int L, int kUnroll, int kMinBlocks>
+template <typename T, typename I, int V, int L, int kUnroll, int kMinBlocks, int kPairs = 1>
 __global__ void __launch_bounds__(256, kMinBlocks)
 spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
             const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols,
@@ -102,29 +102,40 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    for (int64_t base = p0; base < p1; base += L) {
-      const int64_t j = base + lane_in_row;
-      I my_col = 0;
-      float my_val = 0.f;
-      if (j < p1) {
-        my_col = ld_stream(indices + j);
-        my_val = VT<T>::load(ld_stream(data + j));
-      }
-      const int cnt = (int)min((int64_t)L, p1 - base);
-      for (int q = 0; q < cnt; q += kUnroll) {
-        float a[kUnroll];
-        float b[kUnroll][V];
+    for (int64_t base = p0; base < p1; base += (int64_t)L * kPairs) {
+      // kPairs chunks of L (index, value) pairs loaded at once (one round trip)
+      I my_col[kPairs];
+      float my_val[kPairs];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const I col = __shfl_sync(gmask, my_col, (q + u) & (L - 1), L);
-          a[u] = __shfl_sync(gmask, my_val, (q + u) & (L - 1), L);
-          if (q + u < cnt && col_ok) load_vec<T, V>(rhs + (int64_t)col * k + c, b[u], pol_rhs);
+      for (int pp = 0; pp < kPairs; ++pp) {
+        const int64_t j = base + pp * L + lane_in_row;
+        my_col[pp] = 0;
+        my_val[pp] = 0.f;
+        if (j < p1) {
+          my_col[pp] = ld_stream(indices + j);
+          my_val[pp] = VT<T>::load(ld_stream(data + j));
         }
+      }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (q + u < cnt)
+      for (int pp = 0; pp < kPairs; ++pp) {
+        const int64_t cb = base + pp * L;
+        if (cb >= p1) break;  // uniform within the group
+        const int cnt = (int)min((int64_t)L, p1 - cb);
+        for (int q = 0; q < cnt; q += kUnroll) {
+          float a[kUnroll];
+          float b[kUnroll][V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a[u], b[u][i]));
+          for (int u = 0; u < kUnroll; ++u) {
+            const I col = __shfl_sync(gmask, my_col[pp], (q + u) & (L - 1), L);
+            a[u] = __shfl_sync(gmask, my_val[pp], (q + u) & (L - 1), L);
+            if (q + u < cnt && col_ok) load_vec<T, V>(rhs + (int64_t)col * k + c, b[u], pol_rhs);
+          }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u)
+            if (q + u < cnt)
+#pragma unroll
+              for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a[u], b[u][i]));
+        }
       }
     }
     if (row_ok && col_ok) store_vec<T, V>(out + row * k + c, acc);
@@ -138,7 +149,7 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
   // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
-  // MSX_SPMM_VARIANT=0..4; 0 is the default.
+  // MSX_SPMM_VARIANT=0..8; 0 is the default.
   static const int variant = [] {
     const char *e = getenv("MSX_SPMM_VARIANT");
     return e && *e ? atoi(e) : 0;
@@ -148,9 +159,30 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   case 2: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  default: spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
+  case 5: spmm_kernel<T, I, V, L, 8, 4, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 6: spmm_kernel<T, I, V, L, 8, 3, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 7: spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 8: spmm_kernel<T, I, V, L, 8, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  default:
+    // measured defaults: 8 gathers in flight at 4 CTAs/SM for 4-byte values;
+    // 4 in flight, 6 CTAs/SM, two chunks of pairs per load for 2-byte values
+    if constexpr (sizeof(T) == 2)
+      spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
+    else
+      spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
   }
   MSX_CHECK_LAUNCH();
+}
+
+// Bytes per RHS row of one column slab: one 128-byte line. Narrower slabs
+// (MSX_SPMM_SLAB_BYTES = 64 or 32) fit L2 better but measured slower on B200:
+// the kernel is bound by gather issue and latency, not by DRAM misses.
+int64_t spmm_slab_bytes(int64_t, int64_t) {
+  if (const char *env = getenv("MSX_SPMM_SLAB_BYTES")) {
+    const int64_t v = atoll(env);
+    if (v == 32 || v == 64 || v == 128) return v;
+  }
+  return 128;
 }
 
 // Bytes of the RHS slab that should stay L2 resident while rows stream by.
@@ -187,9 +219,9 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
       const T *b = static_cast<const T *>(rhs);
       T *o = static_cast<T *>(out);
       // One pass over the rows when the whole RHS fits the L2 budget (or the
-      // env override forces it); otherwise column slabs of one 128-byte cache
-      // line per RHS row, so every line the gathers bring into L2 is used in
-      // full.
+      // env override forces it); otherwise column slabs whose RHS part fits
+      // the budget (128, 64 or 32 bytes per RHS row), so the random row
+      // gathers of a slab hit L2 while the matrix is re-streamed per slab.
       // TMA row gathers when the RHS rows are whole 128/256-byte boxes; the
       // register kernel then only takes the rows too long for a TMA stage.
       int64_t skip_le = -1;
@@ -197,10 +229,11 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
                        stream))
         skip_le = spmm_tma_max_row();
       const int64_t budget = spmm_l2_budget();
-      const bool one_pass = n_cols * k * elem <= budget || k * elem <= 128;
+      const int64_t slab_bytes = spmm_slab_bytes(n_cols, budget);
+      const bool one_pass = n_cols * k * elem <= budget || k * elem <= slab_bytes;
       if (vec_ok) {
         const int64_t kv = k / kVec;  // 16-byte vectors per row
-        const int64_t slab_vecs = one_pass ? kv : 128 / 16;
+        const int64_t slab_vecs = one_pass ? kv : slab_bytes / 16;
         if (slab_vecs >= 16) {
           launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream, skip_le);
         } else if (slab_vecs >= 8) {

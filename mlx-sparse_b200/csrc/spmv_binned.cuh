@@ -293,23 +293,145 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
   epi.finish();
 }
 
-inline bool short_rows_plan(const BinnedPlan &plan) { return plan.info.identity && plan.info.single_bin == 0; }
+// Pipelined variant for small matrices (few row blocks per CTA, where the
+// three dependent round trips of each block - offsets, nonzeros, x - dominate):
+// while block j is summed from shared memory, block j+1's nonzeros and block
+// j+2's row offsets are already in flight (cp.async groups). Three offset
+// buffers and two nonzero buffers in dynamic shared memory.
+template <typename I>
+constexpr size_t short_ptr_bytes() {
+  return ((3 * (kShortRowsPerBlock + 1) * sizeof(I)) + 15) & ~size_t(15);
+}
+template <typename T, typename I>
+constexpr size_t short_pipe_smem_bytes() {
+  return short_ptr_bytes<I>() + 2 * kShortRowsPerBlock * 8 * (sizeof(I) + sizeof(T));
+}
 
 template <typename T, typename I, typename Epi>
-int64_t short_grid(int64_t n_rows) {
-  static thread_local int cached_dev = -1, per_sm = 0, sms = 0;
+__global__ void __launch_bounds__(kShortRowsPerBlock)
+spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                       const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
+  extern __shared__ __align__(16) unsigned char short_smem[];
+  using PtrBuf = I[kShortRowsPerBlock + 1];
+  using IdxBuf = I[kShortRowsPerBlock * 8];
+  using ValBuf = T[kShortRowsPerBlock * 8];
+  PtrBuf *ptr_s = reinterpret_cast<PtrBuf *>(short_smem);
+  IdxBuf *idx_s = reinterpret_cast<IdxBuf *>(short_smem + short_ptr_bytes<I>());
+  ValBuf *val_s = reinterpret_cast<ValBuf *>(short_smem + short_ptr_bytes<I>() + 2 * sizeof(IdxBuf));
+  pdl_wait();
+  pdl_trigger();
+  if (epi.skip()) return;
+  const int64_t halo_from = epi.halo_from();
+  const int tid = threadIdx.x;
+  const int64_t nblk = (n_rows + kShortRowsPerBlock - 1) / kShortRowsPerBlock;
+  auto rows_of = [&](int64_t blk) { return (int)min((int64_t)kShortRowsPerBlock, n_rows - blk * kShortRowsPerBlock); };
+  auto load_ptr = [&](int64_t blk, int buf) {
+    if (blk >= nblk) return;
+    const int64_t r0 = blk * kShortRowsPerBlock;
+    const int nr = rows_of(blk);
+    if (tid < nr) stage_elem(&ptr_s[buf][tid], indptr + r0 + tid);
+    if (tid == 0) stage_elem(&ptr_s[buf][nr], indptr + r0 + nr);
+  };
+  auto load_data = [&](int64_t blk, int pbuf, int dbuf) {
+    if (blk >= nblk) return;
+    const int nr = rows_of(blk);
+    const int64_t k0 = (int64_t)ptr_s[pbuf][0];
+    const int K = (int)((int64_t)ptr_s[pbuf][nr] - k0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = tid + q * kShortRowsPerBlock;
+      if (e < K) {
+        stage_elem(&idx_s[dbuf][e], indices + k0 + e);
+        stage_elem(&val_s[dbuf][e], data + k0 + e);
+      }
+    }
+  };
+  const int64_t G = gridDim.x;
+  int64_t blk = blockIdx.x;
+  load_ptr(blk, 0);
+  cp_async_wait_all();
+  __syncthreads();
+  load_data(blk, 0, 0);
+  load_ptr(blk + G, 1);
+  for (int j = 0; blk < nblk; ++j, blk += G) {
+    const int pc = j % 3, pn = (j + 1) % 3, pnn = (j + 2) % 3, dc = j & 1, dn = dc ^ 1;
+    cp_async_wait_all();
+    __syncthreads();  // block j's nonzeros and block j+1's offsets have landed
+    load_data(blk + G, pn, dn);
+    load_ptr(blk + 2 * G, pnn);
+    const int64_t r0 = blk * kShortRowsPerBlock;
+    const int nr = rows_of(blk);
+    if (tid < nr) {
+      const int64_t k0 = (int64_t)ptr_s[pc][0];
+      const int q0 = (int)((int64_t)ptr_s[pc][tid] - k0);
+      const int q1 = (int)((int64_t)ptr_s[pc][tid + 1] - k0);
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) {
+          const I c = idx_s[dc][q0 + u];
+          if constexpr (Epi::kHalo)
+            xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
+          else
+            xv[u] = VT<T>::load(__ldg(x + c));
+        }
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[dc][q0 + u]), xv[u]));
+      const T out = VT<T>::store(acc);
+      y[r0 + tid] = out;
+      epi.row(r0 + tid, VT<T>::load(out));
+    }
+    __syncthreads();  // buffers of block j are refilled two steps later
+  }
+  cp_async_wait_all();
+  epi.finish();
+}
+
+inline bool short_rows_plan(const BinnedPlan &plan) { return plan.info.identity && plan.info.single_bin == 0; }
+
+// Grid and kernel choice of the short-row path: the single-stage kernel on a
+// persistent grid, or the pipelined kernel when that grid would give each CTA
+// at most kShortPipeMaxBlocks row blocks or the epilogue asks for it
+// (Epi::kShortPipe; MSX_SPMV_SHORT_PIPE=0/1 forces either).
+constexpr int64_t kShortPipeMaxBlocks = 8;
+struct ShortLaunch {
+  bool pipe;
+  int64_t grid;
+};
+
+template <typename T, typename I, typename Epi>
+ShortLaunch short_launch(int64_t n_rows) {
+  static thread_local int cached_dev = -1, per_sm = 0, per_sm_pipe = 0, sms = 0, force = -1;
   int dev = 0;
   MSX_CUDA(cudaGetDevice(&dev));
   if (dev != cached_dev) {
     int occ = 0;
     MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_short_kernel<T, I, Epi>, kShortRowsPerBlock, 0));
     per_sm = occ > 0 ? occ : 1;
+    constexpr size_t smem = short_pipe_smem_bytes<T, I>();
+    MSX_CUDA(cudaFuncSetAttribute(spmv_short_pipe_kernel<T, I, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    occ = 0;
+    MSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmv_short_pipe_kernel<T, I, Epi>,
+                                                           kShortRowsPerBlock, smem));
+    per_sm_pipe = occ > 0 ? occ : 1;
     sms = num_sms();
+    const char *env = getenv("MSX_SPMV_SHORT_PIPE");
+    force = env && *env ? atoi(env) : -1;
     cached_dev = dev;
   }
   const int64_t nb = ceil_div(n_rows, kShortRowsPerBlock);
   const int64_t cap = (int64_t)per_sm * sms;
-  return nb < cap ? nb : cap;
+  const bool pipe = force >= 0 ? force != 0 : (Epi::kShortPipe || nb <= kShortPipeMaxBlocks * cap);
+  const int64_t cap_used = pipe ? (int64_t)per_sm_pipe * sms : cap;
+  return {pipe, nb < cap_used ? nb : cap_used};
+}
+
+template <typename T, typename I, typename Epi>
+int64_t short_grid(int64_t n_rows) {
+  return short_launch<T, I, Epi>(n_rows).grid;
 }
 
 inline int64_t binned_blocks(const BinnedPlan &plan) { return plan.info.block_start[kBins]; }
@@ -340,8 +462,12 @@ void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices,
   const int64_t grid = binned_grid<T, I, Epi>(plan);
   if (grid == 0) return;
   if (short_rows_plan(plan)) {
-    launch(spmv_short_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock), 0, stream, pdl, data, indices,
-           indptr, x, y, plan.n_rows, epi);
+    if (short_launch<T, I, Epi>(plan.n_rows).pipe)
+      launch(spmv_short_pipe_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock),
+             short_pipe_smem_bytes<T, I>(), stream, pdl, data, indices, indptr, x, y, plan.n_rows, epi);
+    else
+      launch(spmv_short_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock), 0, stream, pdl, data,
+             indices, indptr, x, y, plan.n_rows, epi);
     return;
   }
   launch(spmv_binned_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kBinThreads), 0, stream, pdl, data, indices, indptr,
