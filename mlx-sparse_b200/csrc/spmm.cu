@@ -149,7 +149,7 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
   // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
-  // MSX_SPMM_VARIANT=0..8; 0 is the default.
+  // MSX_SPMM_VARIANT=0..10; 0 is the default.
   static const int variant = [] {
     const char *e = getenv("MSX_SPMM_VARIANT");
     return e && *e ? atoi(e) : 0;
@@ -163,6 +163,8 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   case 6: spmm_kernel<T, I, V, L, 8, 3, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 7: spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 8: spmm_kernel<T, I, V, L, 8, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 9: spmm_kernel<T, I, V, L, 8, 3, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 10: spmm_kernel<T, I, V, L, 6, 4, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   default:
     // measured defaults: 8 gathers in flight at 4 CTAs/SM for 4-byte values;
     // 4 in flight, 6 CTAs/SM, two chunks of pairs per load for 2-byte values

@@ -74,7 +74,7 @@ __device__ __forceinline__ float group_sum(float v, int G) {
 }
 
 template <typename T, typename I, typename Epi>
-__global__ void __launch_bounds__(kBinThreads)
+__global__ void __launch_bounds__(kBinThreads, 4)  // 64 registers, no spills: 4 CTAs/SM instead of 3
 spmv_binned_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
                    const T *__restrict__ x, T *__restrict__ y, const int *__restrict__ rows, BinInfo info,
                    const int64_t *__restrict__ chunk_row, const int64_t *__restrict__ chunk_lo,
