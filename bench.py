@@ -364,10 +364,11 @@ class PcgWorkload(Workload):
         self.step()  # warm up and learn the (deterministic) iteration count
         self.units_per_step = float(self.iterations)
         self.local_bytes = self.bytes_per_iter * self.iterations / world
-        # per iteration: SpMV(+dots), update, direction update, plus at N>1
-        # the halo exchange and the scalar reductions (peer memory: push +
-        # wait + 2 all-reduce kernels; NCCL: pack + 2 decide kernels)
-        per_it = 3 if world == 1 else (7 if self.mode == "p2p" else 6)
+        # per iteration: SpMV(+dots), update, direction update; peer memory
+        # fuses the halo exchange and the scalar all-reduces into those three;
+        # NCCL adds the halo pack and two decision kernels (NCCL's own
+        # kernels are not counted)
+        per_it = 3 if world == 1 or self.mode == "p2p" else 6
         self.launches_per_step = per_it * self.iterations + 6
 
     def step(self):
