@@ -114,6 +114,25 @@ MSX_API int msx_csr_matmul(int value_dtype, int index_dtype, const void *data,
 /* ------------------------------------------------------------------------ */
 /* SpGEMM C = A @ B, canonical (sorted, duplicate-free, exact zeros pruned). */
 /* ------------------------------------------------------------------------ */
+/* Batched products with one matrix, replacing csr_batched_matvec
+ * (src/bindings.cpp:907-915; src/sparse/csr_batched_matvec/
+ * csr_batched_matvec.cpp:82-130) and csr_batched_matmul (src/bindings.cpp:
+ * 1000-1008). rhs is [batch, n_cols] (matvec) or [batch, n_cols, rhs_cols]
+ * (matmul), row-major and contiguous; out is [batch, n_rows] or
+ * [batch, n_rows, rhs_cols]. Every output element sums its row's nonzeros in
+ * order, as the reference does. */
+MSX_API int msx_csr_batched_matvec(int value_dtype, int index_dtype,
+                                   const void *data, const void *indices,
+                                   const void *indptr, int64_t nnz,
+                                   const void *rhs, int64_t batch, void *out,
+                                   int64_t n_rows, int64_t n_cols, void *stream);
+MSX_API int msx_csr_batched_matmul(int value_dtype, int index_dtype,
+                                   const void *data, const void *indices,
+                                   const void *indptr, int64_t nnz,
+                                   const void *rhs, int64_t batch,
+                                   int64_t rhs_cols, void *out, int64_t n_rows,
+                                   int64_t n_cols, void *stream);
+
 /* Replaces `csr_matmat(lhs_data, lhs_indices, lhs_indptr, rhs_data,
  * rhs_indices, rhs_indptr, lhs_n_rows, lhs_n_cols, rhs_n_rows, rhs_n_cols)`
  * (src/bindings.cpp:1116-1131 -> src/sparse/csr_matmat/csr_matmat.cpp:1319-1424,

@@ -197,6 +197,43 @@ int msx_csr_matmul(int value_dtype, int index_dtype, const void *data, const voi
   });
 }
 
+int msx_csr_batched_matvec(int value_dtype, int index_dtype, const void *data, const void *indices,
+                           const void *indptr, int64_t nnz, const void *rhs, int64_t batch, void *out, int64_t n_rows,
+                           int64_t n_cols, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0, MSX_ERR_INVALID, "csr_batched_matvec shape dimensions must be non-negative.");
+    require(nnz >= 0 && batch >= 0, MSX_ERR_INVALID, "csr_batched_matvec sizes must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(data, nnz, "csr_batched_matvec data");
+    check_ptr(indices, nnz, "csr_batched_matvec indices");
+    check_ptr(indptr, n_rows + 1, "csr_batched_matvec indptr");
+    check_ptr(rhs, batch * n_cols, "csr_batched_matvec rhs");
+    check_ptr(out, batch * n_rows, "csr_batched_matvec out");
+    csr_batched_matvec_run(value_dtype, index_dtype, data, indices, indptr, nnz, n_rows, n_cols, batch, rhs, out,
+                           as_stream(stream));
+  });
+}
+
+int msx_csr_batched_matmul(int value_dtype, int index_dtype, const void *data, const void *indices,
+                           const void *indptr, int64_t nnz, const void *rhs, int64_t batch, int64_t rhs_cols,
+                           void *out, int64_t n_rows, int64_t n_cols, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0, MSX_ERR_INVALID, "csr_batched_matmul shape dimensions must be non-negative.");
+    require(nnz >= 0 && batch >= 0 && rhs_cols >= 0, MSX_ERR_INVALID,
+            "csr_batched_matmul sizes must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(data, nnz, "csr_batched_matmul data");
+    check_ptr(indices, nnz, "csr_batched_matmul indices");
+    check_ptr(indptr, n_rows + 1, "csr_batched_matmul indptr");
+    check_ptr(rhs, batch * n_cols * rhs_cols, "csr_batched_matmul rhs");
+    check_ptr(out, batch * n_rows * rhs_cols, "csr_batched_matmul out");
+    csr_batched_matmul_run(value_dtype, index_dtype, data, indices, indptr, nnz, n_rows, n_cols, batch, rhs_cols,
+                           rhs, out, as_stream(stream));
+  });
+}
+
 static void check_matmat_args(int value_dtype, int lit, const void *ld, const void *li, const void *lp,
                               int64_t lnnz, int rit, const void *rd, const void *ri, const void *rp, int64_t rnnz,
                               int64_t m, int64_t k, int64_t rk, int64_t n, int out_it) {

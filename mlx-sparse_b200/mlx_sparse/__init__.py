@@ -11,7 +11,7 @@ from mlx_sparse import linalg
 from mlx_sparse._coo import COOArray, coo_array
 from mlx_sparse._csr import CSRArray, csr_array
 from mlx_sparse._native import extension, library_path
-from mlx_sparse._ops import csr_matmat, csr_matmul, csr_matvec
+from mlx_sparse._ops import csr_batched_matmul, csr_batched_matvec, csr_matmat, csr_matmul, csr_matvec
 
 __version__ = "0.1.0"
 
@@ -21,6 +21,8 @@ __all__ = [
     "coo_array",
     "csr_array",
     "csr_matmat",
+    "csr_batched_matmul",
+    "csr_batched_matvec",
     "csr_matmul",
     "csr_matvec",
     "extension",

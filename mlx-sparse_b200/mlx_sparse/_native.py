@@ -55,6 +55,8 @@ def extension():
         L.msx_spmv_plan_info.argtypes = [p, ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.msx_csr_matvec.argtypes = [c_int, c_int, p, p, p, i64, p, p, i64, i64, p, p]
         L.msx_csr_matmul.argtypes = [c_int, c_int, p, p, p, i64, p, i64, p, i64, i64, p]
+        L.msx_csr_batched_matvec.argtypes = [c_int, c_int, p, p, p, i64, p, i64, p, i64, i64, p]
+        L.msx_csr_batched_matmul.argtypes = [c_int, c_int, p, p, p, i64, p, i64, i64, p, i64, i64, p]
         mm = [c_int, c_int, p, p, p, i64, c_int, p, p, p, i64, i64, i64, i64, i64, c_int]
         if hasattr(L, "msx_csr_matmat_symbolic"):
             L.msx_csr_matmat_symbolic.argtypes = mm + [p, ctypes.POINTER(i64), c_int, p]
@@ -160,6 +162,34 @@ def csr_matmul(data, indices, indptr, rhs, shape, *, out=None):
         check(L.msx_csr_matmul(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
                                _p(indptr), data.numel(), _p(rhs), k, _p(y), shape[0], shape[1],
                                stream_ptr(dev)))
+    return y
+
+
+def csr_batched_matvec(data, indices, indptr, rhs, shape):
+    """``Y[b] = A @ X[b]`` for ``rhs`` of shape ``(batch, n_cols)``."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr, rhs)
+    data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
+    batch = rhs.shape[0]
+    y = torch.empty((batch, shape[0]), dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_batched_matvec(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                                       _p(indptr), data.numel(), _p(rhs), batch, _p(y), shape[0], shape[1],
+                                       stream_ptr(dev)))
+    return y
+
+
+def csr_batched_matmul(data, indices, indptr, rhs, shape):
+    """``Y[b] = A @ B[b]`` for ``rhs`` of shape ``(batch, n_cols, k)``."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr, rhs)
+    data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
+    batch, k = rhs.shape[0], rhs.shape[2]
+    y = torch.empty((batch, shape[0], k), dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_batched_matmul(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                                       _p(indptr), data.numel(), _p(rhs), batch, k, _p(y), shape[0], shape[1],
+                                       stream_ptr(dev)))
     return y
 
 

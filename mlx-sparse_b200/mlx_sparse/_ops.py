@@ -29,7 +29,8 @@ def csr_matvec(a: CSRArray, x):
 
 
 def csr_matmul(a: CSRArray, rhs):
-    """``Y = A @ B`` for a rank-2 dense ``B``; rank >= 3 multiplies each batch."""
+    """``Y = A @ B`` for a rank-2 dense ``B``; rank >= 3 is a batch of matrices
+    (``rhs.shape[-2]`` is the sparse dimension), one native batched call."""
     if not isinstance(a, CSRArray):
         raise TypeError(f"csr_matmul expects CSRArray, got {type(a).__name__}.")
     rhs = ensure_array(rhs, device=a.device)
@@ -42,12 +43,63 @@ def csr_matmul(a: CSRArray, rhs):
         raise ValueError(
             f"csr_matmul RHS has sparse dimension {rhs.shape[-2]}, but sparse n_cols={a.shape[1]}."
         )
-    batch = rhs.shape[:-2]
-    flat = rhs.reshape(-1, rhs.shape[-2], rhs.shape[-1])
-    outs = [csr_matmul(a, flat[i]) for i in range(flat.shape[0])]
-    import torch
+    return _csr_matmul_batched(a, rhs)
 
-    return torch.stack(outs).reshape(*batch, a.shape[0], rhs.shape[-1])
+
+def _csr_matmul_batched(a: CSRArray, rhs):
+    """Reference: ``_ops._csr_matmul_batched`` (``mlx_sparse/_ops.py:985-998``)."""
+    if a.data.dtype != rhs.dtype:
+        raise TypeError(
+            "csr_matmul requires sparse data and RHS to have the same dtype, "
+            f"got {a.data.dtype} and {rhs.dtype}."
+        )
+    batch_shape = tuple(int(d) for d in rhs.shape[:-2])
+    k = int(rhs.shape[-1])
+    flat = rhs.reshape(-1, a.shape[1], k)
+    out = _native.csr_batched_matmul(a.data, a.indices, a.indptr, flat, a.shape)
+    return out.reshape(*batch_shape, a.shape[0], k)
+
+
+def csr_batched_matmul(a: CSRArray, rhs):
+    """``Y[..] = A @ B[..]`` for ``rhs`` of shape ``(..., n_cols, k)``, rank >= 3.
+
+    Reference: ``_ops.csr_batched_matmul`` (``mlx_sparse/_ops.py:1097-1115``).
+    """
+    if not isinstance(a, CSRArray):
+        raise TypeError(f"csr_batched_matmul expects CSRArray, got {type(a).__name__}.")
+    rhs = ensure_array(rhs, device=a.device)
+    if rhs.ndim < 3:
+        raise ValueError(f"csr_batched_matmul expects rank-3 or higher RHS, got {tuple(rhs.shape)}.")
+    if rhs.shape[-2] != a.shape[1]:
+        raise ValueError(
+            f"csr_batched_matmul RHS has sparse dimension {rhs.shape[-2]}, but sparse n_cols={a.shape[1]}."
+        )
+    return _csr_matmul_batched(a, rhs)
+
+
+def csr_batched_matvec(a: CSRArray, rhs):
+    """``Y[..] = A @ X[..]`` for ``rhs`` of shape ``(..., n_cols)``, rank >= 2.
+
+    Reference: ``_ops.csr_batched_matvec`` (``mlx_sparse/_ops.py:821-852``).
+    """
+    if not isinstance(a, CSRArray):
+        raise TypeError(f"csr_batched_matvec expects CSRArray, got {type(a).__name__}.")
+    rhs = ensure_array(rhs, device=a.device)
+    if rhs.ndim < 2:
+        raise ValueError(f"csr_batched_matvec expects rank-2 or higher RHS, got {tuple(rhs.shape)}.")
+    if rhs.shape[-1] != a.shape[1]:
+        raise ValueError(
+            f"csr_batched_matvec RHS has vector dimension {rhs.shape[-1]}, but sparse n_cols={a.shape[1]}."
+        )
+    if a.data.dtype != rhs.dtype:
+        raise TypeError(
+            "csr_batched_matvec requires sparse data and RHS to have the same dtype, "
+            f"got {a.data.dtype} and {rhs.dtype}."
+        )
+    batch_shape = tuple(int(d) for d in rhs.shape[:-1])
+    flat = rhs.reshape(-1, a.shape[1])
+    out = _native.csr_batched_matvec(a.data, a.indices, a.indptr, flat, a.shape)
+    return out.reshape(*batch_shape, a.shape[0])
 
 
 def csr_matmat(a: CSRArray, rhs: CSRArray) -> CSRArray:
