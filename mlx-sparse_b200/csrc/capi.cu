@@ -454,6 +454,12 @@ int msx_cg_context_create(int index_dtype, const float *data, const void *indice
     require(n_peers == 0 || (peers && send_counts && recv_counts), MSX_ERR_INVALID, "peer lists must not be null.");
     require(comm_mode != kCommP2p || n_peers == 0 || peer_dst_offset, MSX_ERR_INVALID,
             "P2P mode needs the landing offsets.");
+    int64_t n_send = 0;
+    for (int k = 0; k < n_peers; ++k) {
+      require(send_counts[k] >= 0 && recv_counts[k] >= 0, MSX_ERR_INVALID, "peer counts must be non-negative.");
+      n_send += send_counts[k];
+    }
+    require(n_send == 0 || send_idx, MSX_ERR_INVALID, "send_idx must not be null when entries are sent.");
     dispatch_index(index_dtype, [](auto) {});
     check_ptr(data, nnz, "csr_cg data");
     check_ptr(indices, nnz, "csr_cg indices");

@@ -81,3 +81,34 @@ def test_solver_status_reasons():
     assert status_reason(-2)[1] == "non_positive_preconditioned_inner_product"
     x, info = finish_solver_result(None, -3, 1.0, 2, solver="cg", return_info=True)
     assert info.status == -3 and not info.converged and int(info) == -3
+
+
+def test_batched_and_context_entry_points_validate_without_gpu():
+    """Argument checks of the batched products and the CG context run before
+    any CUDA call, so they answer with status codes on a GPU-less host."""
+    from mlx_sparse import _native
+
+    lib = _native.extension()
+    # negative batch -> invalid
+    rc = lib.msx_csr_batched_matvec(0, 0, None, None, None, 0, None, -1, None, 4, 4, None)
+    assert rc == 1 and b"non-negative" in lib.msx_last_error()
+    rc = lib.msx_csr_batched_matmul(0, 0, None, None, None, 0, None, 2, -3, None, 4, 4, None)
+    assert rc == 1 and b"non-negative" in lib.msx_last_error()
+    # bad value dtype code -> type error
+    rc = lib.msx_csr_batched_matmul(9, 0, None, None, None, 0, None, 1, 1, None, 0, 0, None)
+    assert rc == 2
+    # the context needs an output handle and at most 8 ranks
+    out = ctypes.c_void_p()
+    rc = lib.msx_cg_context_create(0, None, None, None, 0, 4, 0, 1, 0, 0, 1, None, 0, None, None, None, None, None,
+                                   None, None)
+    assert rc == 1
+    rc = lib.msx_cg_context_create(0, None, None, None, 0, 4, 0, 1, 2, 0, 9, None, 0, None, None, None, None, None,
+                                   None, ctypes.byref(out))
+    assert rc == 1 and not out.value
+    # peer-memory mode needs the landing offsets when there are peers
+    peers = (ctypes.c_int * 1)(1)
+    counts = (ctypes.c_int64 * 1)(4)
+    rc = lib.msx_cg_context_create(0, None, None, None, 0, 4, 4, 1, 2, 0, 2, None, 1, peers, counts, counts, None,
+                                   None, None, ctypes.byref(out))
+    assert rc == 1 and b"landing offsets" in lib.msx_last_error()
+    assert lib.msx_cg_context_ipc_handles(None, None, 0) == 1
