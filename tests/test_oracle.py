@@ -150,3 +150,72 @@ def test_workload_generators_are_canonical():
             row = i[p[r]:p[r + 1]]
             assert np.all(np.diff(row) > 0)
             assert row.size == 0 or (row[0] >= 0 and row[-1] < shape[1])
+
+
+_HB = "/root/reference/tests/fixtures/suitesparse/HB"
+
+
+def _hb_matrices():
+    import os
+
+    if not os.path.isdir(_HB):
+        return []
+    return sorted(f for f in os.listdir(_HB) if f.endswith(".mtx") and not f.endswith("_b.mtx"))
+
+
+@pytest.mark.skipif(not _hb_matrices(), reason="reference SuiteSparse fixtures not present")
+@pytest.mark.parametrize("name", _hb_matrices() or ["none"])
+def test_oracle_on_reference_suitesparse_fixtures(orc, name):
+    """The SuiteSparse Harwell-Boeing matrices the reference's tests ship
+    (read in place, not copied): oracle SpMV / SpMM / SpGEMM against SciPy,
+    the secondary oracle the reference's own tests use."""
+    import os
+
+    import scipy.io
+
+    A = sp.csr_matrix(scipy.io.mmread(os.path.join(_HB, name))).astype(np.float32)
+    A.sum_duplicates()
+    A.sort_indices()
+    d, i, p = A.data, A.indices.astype(np.int32), A.indptr.astype(np.int32)
+    m, n = A.shape
+    x = wl.uniform_vector(n, 3)
+    y = orc.csr_matvec(d, i, p, x, m)
+    scale = np.abs(A) @ np.abs(x) + 1e-30
+    assert np.max(np.abs(y - A @ x) / np.maximum(np.abs(A @ x), scale)) <= 1e-5
+    B = wl.uniform_matrix(n, 8, 4)
+    np.testing.assert_allclose(orc.csr_matmul(d, i, p, B, m), A @ B, rtol=1e-4, atol=1e-4 * float(np.abs(A).max()))
+    if m == n:
+        cd, ci, cp = orc.csr_matmat((d, i, p), (d, i, p), (m, n), (m, n))
+        C = (A @ A).tocsr()
+        C.eliminate_zeros()
+        C.sort_indices()
+        np.testing.assert_array_equal(ci, C.indices)
+        np.testing.assert_array_equal(cp, C.indptr)
+
+
+@pytest.mark.skipif(not _hb_matrices(), reason="reference SuiteSparse fixtures not present")
+def test_oracle_pcg_on_bcsstk03():
+    """Jacobi PCG on the SPD structural matrix bcsstk03: converged solutions
+    satisfy the reference's stopping rule against a float64 check."""
+    import os
+
+    import scipy.io
+
+    from oracle import oracle as orc
+
+    path = os.path.join(_HB, "bcsstk03.mtx")
+    if not os.path.exists(path):
+        pytest.skip("bcsstk03 not present")
+    A = sp.csr_matrix(scipy.io.mmread(path)).astype(np.float32)
+    A.sum_duplicates()
+    A.sort_indices()
+    n = A.shape[0]
+    d, i, p = A.data, A.indices.astype(np.int32), A.indptr.astype(np.int32)
+    b = (A @ wl.uniform_vector(n, 1)).astype(np.float32)
+    inv = (1.0 / A.diagonal()).astype(np.float32)
+    x, info, res, its = orc.csr_pcg_jacobi(d, i, p, b, np.zeros(n, np.float32), inv, rtol=1e-5, atol=0.0,
+                                           maxiter=10 * n)
+    assert info in (0, -1, 10 * n)
+    if info == 0:
+        r = b.astype(np.float64) - A.astype(np.float64) @ x.astype(np.float64)
+        assert np.linalg.norm(r) <= 1e-3 * np.linalg.norm(b)
