@@ -142,6 +142,111 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
   }
 }
 
+// Asynchronous-copy variant: the RHS gathers go to shared memory with 16-byte
+// cp.async (L2-only, evict_last hint), so a gather in flight holds no
+// registers and each thread keeps kDepth of them outstanding; every thread
+// consumes only the slots it filled, in nonzero order, so no barrier is
+// needed beyond the group's own pair staging. Same per-element order as the
+// register kernel. Requires 16-byte vectors (V * sizeof(T) == 16).
+constexpr int kAsyncChunk = 16;  // (index, value) pairs staged per row at a time
+
+template <typename I, int L, int kDepth>
+constexpr size_t spmm_async_smem() {
+  return (size_t)kDepth * 256 * 16 + (size_t)(256 / L) * kAsyncChunk * (sizeof(I) + sizeof(float));
+}
+
+__device__ __forceinline__ void cp_async16_hint(void *dst, const void *src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T, typename I, int V, int L, int kDepth>
+__global__ void __launch_bounds__(256)
+spmm_async_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                  const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+  static_assert(V * sizeof(T) == 16, "16-byte vectors only");
+  constexpr int kRows = 256 / L;
+  extern __shared__ __align__(16) unsigned char spmm_sm[];
+  float4 *stage = reinterpret_cast<float4 *>(spmm_sm);  // [kDepth][256]
+  I *col_s = reinterpret_cast<I *>(spmm_sm + (size_t)kDepth * 256 * 16);  // [kRows][kAsyncChunk]
+  float *val_s = reinterpret_cast<float *>(col_s + kRows * kAsyncChunk);     // [kRows][kAsyncChunk]
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int lane_in_row = tid % L;
+  const int rloc = tid / L;
+  const unsigned gmask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
+  const int64_t row = blockIdx.x * (int64_t)kRows + rloc;
+  const bool row_ok = row < n_rows;
+  const int64_t slab0 = blockIdx.y * slab_cols;
+  const int64_t slab1 = min(slab0 + slab_cols, k);
+  const int64_t p0 = row_ok ? (int64_t)indptr[row] : 0;
+  const int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
+  const uint64_t pol_rhs = policy_evict_last();
+  I *my_cols = col_s + rloc * kAsyncChunk;
+  float *my_vals = val_s + rloc * kAsyncChunk;
+  for (int64_t c = slab0 + (int64_t)lane_in_row * V; c - (int64_t)lane_in_row * V < slab1; c += (int64_t)L * V) {
+    const bool col_ok = c < slab1;
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int64_t base = p0; base < p1; base += kAsyncChunk) {
+      const int cnt = (int)min((int64_t)kAsyncChunk, p1 - base);
+      __syncwarp(gmask);  // the previous chunk's pairs are no longer read
+      for (int j = lane_in_row; j < cnt; j += L) {
+        my_cols[j] = ld_stream(indices + base + j);
+        my_vals[j] = VT<T>::load(ld_stream(data + base + j));
+      }
+      __syncwarp(gmask);
+#pragma unroll
+      for (int q = 0; q < kDepth; ++q) {
+        if (q < cnt && col_ok) cp_async16_hint(&stage[q * 256 + tid], rhs + (int64_t)my_cols[q] * k + c, pol_rhs);
+        cp_async_commit();
+      }
+      for (int q = 0; q < cnt; ++q) {
+        cp_async_wait<kDepth - 1>();  // the group of gather q has landed
+        const int slot = (q % kDepth) * 256 + tid;
+        float b[V];
+        if (col_ok) {
+          const float4 raw = stage[slot];
+          const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+          for (int i = 0; i < V; ++i) b[i] = VT<T>::load(e[i]);
+          const float a = my_vals[q];
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, b[i]));
+        }
+        if (q + kDepth < cnt && col_ok)
+          cp_async16_hint(&stage[slot], rhs + (int64_t)my_cols[q + kDepth] * k + c, pol_rhs);
+        cp_async_commit();
+      }
+      cp_async_wait<0>();
+    }
+    if (row_ok && col_ok) store_vec<T, V>(out + row * k + c, acc);
+  }
+}
+
+template <typename T, typename I, int V, int L, int kDepth>
+void launch_spmm_async(dim3 grid, cudaStream_t stream, const T *data, const I *indices, const I *indptr,
+                       const T *rhs, T *out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+  constexpr size_t smem = spmm_async_smem<I, L, kDepth>();
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  MSX_CUDA(cudaGetDevice(&dev));
+  if (dev != configured_dev) {
+    MSX_CUDA(cudaFuncSetAttribute(spmm_async_kernel<T, I, V, L, kDepth>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured_dev = dev;
+  }
+  spmm_async_kernel<T, I, V, L, kDepth><<<grid, 256, smem, stream>>>(data, indices, indptr, rhs, out, n_rows, k,
+                                                                    slab_cols);
+}
+
 template <typename T, typename I, int V, int L>
 void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs, T *out, int64_t n_rows,
                  int64_t k, int64_t slab_cols, cudaStream_t stream, int64_t skip_le = -1) {
@@ -149,7 +254,7 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
   // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
-  // MSX_SPMM_VARIANT=0..10; 0 is the default.
+  // MSX_SPMM_VARIANT=0..12 (11, 12: cp.async gathers, 8 or 12 deep); 0 is the default.
   static const int variant = [] {
     const char *e = getenv("MSX_SPMM_VARIANT");
     return e && *e ? atoi(e) : 0;
@@ -165,6 +270,19 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   case 8: spmm_kernel<T, I, V, L, 8, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 9: spmm_kernel<T, I, V, L, 8, 3, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
   case 10: spmm_kernel<T, I, V, L, 6, 4, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
+  case 11:
+  case 12:
+    if constexpr (V * sizeof(T) == 16) {
+      if (skip_le < 0) {
+        if (variant == 11)
+          launch_spmm_async<T, I, V, L, 8>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+        else
+          launch_spmm_async<T, I, V, L, 12>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+        break;
+      }
+    }
+    spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
+    break;
   default:
     // measured defaults: 8 gathers in flight at 4 CTAs/SM for 4-byte values;
     // 4 in flight, 6 CTAs/SM, two chunks of pairs per load for 2-byte values
