@@ -254,7 +254,7 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
   // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
-  // MSX_SPMM_VARIANT=0..12 (11, 12: cp.async gathers, 8 or 12 deep); 0 is the default.
+  // MSX_SPMM_VARIANT=0..12 (11, 12: cp.async gathers, 8 or 12 deep); 0 is the default (= 11 for 16-byte vectors).
   static const int variant = [] {
     const char *e = getenv("MSX_SPMM_VARIANT");
     return e && *e ? atoi(e) : 0;
@@ -284,8 +284,16 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
     spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
     break;
   default:
-    // measured defaults: 8 gathers in flight at 4 CTAs/SM for 4-byte values;
-    // 4 in flight, 6 CTAs/SM, two chunks of pairs per load for 2-byte values
+    // measured defaults: cp.async gathers 8 deep for 16-byte vectors (fp32
+    // 0.555 ms vs 0.847, bf16 0.307 vs 0.800 ms on the 1M x 1M, 16/row, k = 64
+    // config); else the register kernel with 8 gathers in flight at 4 CTAs/SM
+    // for 4-byte values, 4 in flight at 6 CTAs/SM for 2-byte values
+    if constexpr (V * sizeof(T) == 16) {
+      if (skip_le < 0) {
+        launch_spmm_async<T, I, V, L, 8>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+        break;
+      }
+    }
     if constexpr (sizeof(T) == 2)
       spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
     else
