@@ -1,5 +1,5 @@
-// Plain CG and Jacobi-preconditioned CG on one GPU, with the whole Krylov loop
-// on the device.
+// Plain CG and Jacobi-preconditioned CG with the whole Krylov loop on the
+// device, on one GPU or as one rank of a row-sharded solve.
 //
 // Reference behaviour (restated step by step, same scalar types):
 //   plain CG   src/linalg/cg/cg.cpp:75-256 - double dots, x/r/p updated in
@@ -23,6 +23,16 @@
 // and launched back to back; the host reads the status once per batch.
 // Matrices with rows longer than the CTA bin (split into chunks) run the plain
 // SpMV + chunk fixup and a separate dot kernel instead of the fused K1.
+//
+// Row-sharded (one rank per GPU of a node), peer-memory mode: K3's first CTAs
+// store the direction entries the peers read straight into the peers' halo
+// word arrays; K1 reads halo columns from this rank's word array, checking
+// each word's round flag; the last CTA of each reduction exchanges flagged
+// fp64 partial-sum words through the ranks' mailboxes and adds them in rank
+// order before deciding. Still three kernels per iteration. NCCL mode adds a
+// send/recv of the halo before K1 and an all-reduce + decision kernel after
+// each reduction. The solver state (plan, buffers, captured graph) lives in a
+// CgEngine that is reused across solves.
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>

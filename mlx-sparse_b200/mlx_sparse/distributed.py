@@ -5,15 +5,22 @@ ranges (``src/common/cpu_parallel.cpp:202-253``). Here the same partition is
 applied to GPUs: rank ``r`` owns a contiguous slab of rows with about
 ``nnz / world`` nonzeros. Its local matrix keeps the owned columns first
 (renumbered ``c - r0``) and appends the "halo" columns it reads from other
-ranks, sorted by owner and then by column. Each SpMV inside the solver first
-receives the halo entries of the input vector from their owners over NCCL
-(grouped send/recv), and each scalar reduction of CG is an NCCL all-reduce of
-a few fp64 partial sums, so every rank takes the same scalar decisions and the
-solve keeps the reference's recurrence and status codes.
+ranks, sorted by global column (hence grouped by owner).
 
-Host-side logic (partition, halo lists) is plain numpy and is tested on CPU
-with ``gloo`` ranks; the solve itself runs in the CUDA library
-(``msx_dist_*`` in ``include/msx_sparse.h``).
+The row-sharded CG (``DistCG``) keeps the reference's recurrence and status
+codes; every rank takes identical scalar decisions. Two exchange modes:
+
+- peer memory (default, one node): each rank maps its peers' halo arrays and
+  mailboxes (CUDA IPC handles exchanged once through ``torch.distributed``);
+  the direction update stores the entries peers read straight into their halo
+  arrays as flagged words, the SpMV reads and checks them in place, and the
+  reductions' last CTAs all-reduce the CG scalars through the mailboxes;
+- NCCL: grouped send/recv of the halo and an all-reduce of the fp64 partial
+  sums per reduction (also ``dist_cg``, the stateless form).
+
+Host-side logic (partition, halo lists, landing offsets) is plain numpy and is
+tested on CPU with ``gloo`` ranks; the solve itself runs in the CUDA library
+(``msx_cg_context_*`` and ``msx_dist_*`` in ``include/msx_sparse.h``).
 """
 
 from __future__ import annotations
