@@ -599,8 +599,11 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         workers = len(os.sched_getaffinity(0))
         v, sample = wk.cpu_sample(workers, budget_s=args.cpu_budget)
+        # the reference's auto worker count and, beside it, one worker
+        v1, _ = wk.cpu_sample(1, budget_s=min(3.0, args.cpu_budget))
         line["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
-                                "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop"}
+                                "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop",
+                                "value_1_worker": round(v1, 3), "cpu_model": _cpu_model()}
     if not args.no_extras:
         # every rank takes part in the multi-GPU extras; rank 0 reports
         names = (["spmv_lap2d", "spmv_powerlaw", "spmm_bf16", "spmm_f32", "pcg_poisson3d", "spgemm"]
@@ -698,9 +701,21 @@ def run_reference(args):
             "config": wk.config(), "impl": "reference",
             "cpu_baseline": {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
                              "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop "
-                                                "(the reference itself needs MLX, absent here)"},
+                                                "(the reference itself needs MLX, absent here)",
+                             "cpu_model": _cpu_model()},
             "e2e": {"value": round(v, 3), "unit": wk.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def _setup_host_only(wk):
