@@ -157,37 +157,58 @@ class SpmmWorkload(Workload):
         s = 2 if bf16 else 4
         nnz = n * per_row
         self.problem_bytes = nnz * (s + 4) + 4 * (n + 1) + 2 * n * k * s
+        self.world = 1
 
     def config(self):
         return {"workload": self.name, "matrix": f"{self.n}x{self.n} csr, {self.per_row} nnz/row uniform cols",
                 "rhs": f"{self.n}x{self.k} row-major", "index": "int32",
                 "l2": "flushed before every step (512 MiB write)"}
 
+    def setup_host(self):
+        (d, i, p), shape = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
+        B = np.random.default_rng(self.seed + 100).uniform(-1, 1, (self.n, self.k)).astype(np.float32)
+        self.full = (d, i, p, B)
+
     def setup(self, rank, world, device):
         import torch
         import mlx_sparse as ms
 
-        (d, i, p), shape = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
-        B = np.random.default_rng(self.seed + 100).uniform(-1, 1, (self.n, self.k)).astype(np.float32)
+        self.setup_host()
+        d, i, p, B = self.full
         r0, r1 = _shard_rows(p, rank, world)
+        self.world, self.r0, self.r1 = world, r0, r1
         d, i, p = _slice_rows(d, i, p, r0, r1)
         self.host = (d, i, p, B)
         self.rows = r1 - r0
         tdt = torch.bfloat16 if self.bf16 else torch.float32
+        self.tdt = tdt
         self.A = ms.csr_array((torch.from_numpy(d).to(device).to(tdt), torch.from_numpy(i).to(device),
                                torch.from_numpy(p).to(device)), shape=(self.rows, self.n), canonical=True)
         self.B = torch.from_numpy(B).to(device).to(tdt)
         self.out = torch.empty((self.rows, self.k), dtype=tdt, device=device)
-        # pinned host copies for the end-to-end leg
-        self.h_d = torch.from_numpy(d).to(tdt).pin_memory()
-        self.h_i = torch.from_numpy(i).pin_memory()
-        self.h_p = torch.from_numpy(p).pin_memory()
-        self.h_B = torch.from_numpy(B).to(tdt).pin_memory()
-        self.h_out = torch.empty((self.rows, self.k), dtype=tdt).pin_memory()
+        s = 2 if self.bf16 else 4
         self.dev = device
         self.launches_per_step = 1
-        s = 2 if self.bf16 else 4
-        self.h2d_bytes = d.size * s + i.nbytes + p.nbytes + B.size * s
+        self.h_d = torch.from_numpy(d).to(tdt).pin_memory()
+        self.h_p = torch.from_numpy(p).pin_memory()
+        self.h_out = torch.empty((self.rows, self.k), dtype=tdt).pin_memory()
+        if world == 1:
+            # pinned host copies for the end-to-end leg
+            self.h_i = torch.from_numpy(i).pin_memory()
+            self.h_B = torch.from_numpy(B).to(tdt).pin_memory()
+            self.h2d_bytes = d.size * s + i.nbytes + p.nbytes + B.size * s
+        else:
+            # end to end at N > 1: each rank uploads its slab of A and only its
+            # own rows of B; the rows of B are then all-gathered over NVLink
+            # (NCCL), so no rank copies the whole B over PCIe
+            from mlx_sparse.distributed import OperandExchange
+
+            fd, fi, fp, _ = self.full
+            self.exch = OperandExchange(fd, fi, fp, self.n, rank, world, device, mode="allgather")
+            self.h_i = torch.from_numpy(np.ascontiguousarray(self.exch.local_indices)).pin_memory()
+            self.h_B = torch.from_numpy(B[r0:r1]).to(tdt).pin_memory()
+            self.n_local_cols = self.exch.n_local_cols
+            self.h2d_bytes = d.size * s + i.nbytes + p.nbytes + (r1 - r0) * self.k * s
         self.d2h_bytes = self.rows * self.k * s
 
     def step(self):
@@ -198,39 +219,52 @@ class SpmmWorkload(Workload):
     def e2e_step(self):
         import mlx_sparse as ms
 
-        A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
-                          self.h_p.to(self.dev, non_blocking=True)), shape=self.A.shape, canonical=True)
-        Y = A @ self.h_B.to(self.dev, non_blocking=True)
+        dev = self.dev
+        if self.world == 1:
+            A = ms.csr_array((self.h_d.to(dev, non_blocking=True), self.h_i.to(dev, non_blocking=True),
+                              self.h_p.to(dev, non_blocking=True)), shape=self.A.shape, canonical=True)
+            Y = A @ self.h_B.to(dev, non_blocking=True)
+        else:
+            A = ms.csr_array((self.h_d.to(dev, non_blocking=True), self.h_i.to(dev, non_blocking=True),
+                              self.h_p.to(dev, non_blocking=True)), shape=(self.rows, self.n_local_cols),
+                             canonical=True)
+            Y = A @ self.exch.exchange(self.h_B.to(dev, non_blocking=True))
         self.h_out.copy_(Y, non_blocking=True)
 
     def cpu_sample(self, workers, budget_s=10.0):
         from oracle import oracle
 
-        d, i, p, B = self.host
-        rows = min(self.rows, 1 << 16)
-        dd, ii, pp = _slice_rows(d, i, p, 0, rows)
+        d, i, p, B = self.full
+        rows = self.n
         if self.bf16:
-            dd, Bc = oracle.f32_to_bf16_bits(dd), oracle.f32_to_bf16_bits(B)
+            dd, Bc = oracle.f32_to_bf16_bits(d), oracle.f32_to_bf16_bits(B)
         else:
-            Bc = B
+            dd, Bc = d, B
         s = 2 if self.bf16 else 4
-        sample_bytes = int(pp[-1]) * (s + 4) + 4 * (rows + 1) + 2 * rows * self.k * s
+        sample_bytes = int(p[-1]) * (s + 4) + 4 * (rows + 1) + 2 * rows * self.k * s
         times = []
         t_end = time.perf_counter() + budget_s
-        while time.perf_counter() < t_end or len(times) < 3:
+        while time.perf_counter() < t_end or len(times) < 2:
             t0 = time.perf_counter()
-            oracle.csr_matmul(dd, ii, pp, Bc, rows, bf16=self.bf16, workers=workers)
+            oracle.csr_matmul(dd, i, p, Bc, rows, bf16=self.bf16, workers=workers)
             times.append(time.perf_counter() - t0)
             if len(times) >= 200:
                 break
         med = statistics.median(times)
-        return sample_bytes / med / 1e9, f"{rows} of {self.n} rows, median of {len(times)} runs"
+        return sample_bytes / med / 1e9, f"full matrix ({rows} rows), median of {len(times)} runs"
 
 
 class SpmvWorkload(Workload):
-    def __init__(self, kind="lap2d"):
-        self.kind = kind
-        self.name = f"spmv_{kind}"
+    """BASELINE configs 1 and 3. ``sharded=False``: at N > 1 every rank holds
+    all of x (replicated input placement) and its nnz-balanced row slab;
+    ``sharded=True``: x is sharded like the rows and each step first
+    exchanges the entries a rank reads (NCCL: halo all-to-all for the
+    Laplacian, all-gather for random power-law columns) - the exchange is
+    inside the timed step."""
+
+    def __init__(self, kind="lap2d", sharded=False):
+        self.kind, self.sharded = kind, sharded
+        self.name = f"spmv_{kind}" + ("_xsharded" if sharded else "")
         if kind == "lap2d":
             self.make = lambda: wl.lap2d(1024, np.int32)
             self.x_seed, self.it_bytes, self.dtype = 0, 4, "f32"
@@ -239,67 +273,125 @@ class SpmvWorkload(Workload):
             self.x_seed, self.it_bytes, self.dtype = 5, 8, "f32 values, int64 indices"
 
     def config(self):
+        x = {"x": "row-sharded, exchanged each step" if self.sharded else "replicated on every GPU"}
         if self.kind == "lap2d":
             return {"workload": self.name, "matrix": "2D 5-point Laplacian 1024x1024 grid (n=1,048,576)",
-                    "index": "int32", "l2": "flushed before every step (512 MiB write)"}
+                    "index": "int32", "l2": "flushed before every step (512 MiB write)", **x}
         return {"workload": self.name, "matrix": "power-law rows n=4,194,304 (Lomax alpha 2.1, mean ~20)",
-                "index": "int64", "l2": "flushed before every step (512 MiB write)"}
+                "index": "int64", "l2": "flushed before every step (512 MiB write)", **x}
+
+    def setup_host(self):
+        (d, i, p), shape = self.make()
+        x = wl.uniform_vector(shape[1], self.x_seed)
+        ib = self.it_bytes
+        self.full = (d, i, p, x)
+        self.shape = shape
+        # metric bytes of the whole product: (4+ib) per nnz, indptr, x once, y
+        self.problem_bytes = d.size * (4 + ib) + ib * (shape[0] + 1) + 4 * shape[1] + 4 * shape[0]
 
     def setup(self, rank, world, device):
         import torch
         import mlx_sparse as ms
 
-        (d, i, p), shape = self.make()
-        x = wl.uniform_vector(shape[1], self.x_seed)
+        self.setup_host()
+        d, i, p, x = self.full
+        shape = self.shape
         ib = self.it_bytes
-        # metric bytes of the whole product: (4+ib) per nnz, indptr, x once, y
-        self.problem_bytes = d.size * (4 + ib) + ib * (shape[0] + 1) + 4 * shape[1] + 4 * shape[0]
+        self.world, self.rank, self.dev = world, rank, device
         r0, r1 = _shard_rows(p, rank, world)
-        d, i, p = _slice_rows(d, i, p, r0, r1)
+        self.r0, self.r1 = r0, r1
         self.rows, self.n = r1 - r0, shape[1]
-        self.host = (d, i, p, x)
-        self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
-                               torch.from_numpy(p).to(device)), shape=(self.rows, self.n), canonical=True)
-        self.plan = self.A.spmv_plan()
-        self.x = torch.from_numpy(x).to(device)
+        if self.sharded and world > 1:
+            from mlx_sparse.distributed import DistProduct
+
+            self.P = DistProduct(d, i, p, shape[0], rank, world, device,
+                                 mode="halo" if self.kind == "lap2d" else "allgather")
+            self.x_own = torch.from_numpy(x[r0:r1].copy()).to(device)
+            self.A = self.P.A
+            self.plan = self.A.spmv_plan()
+            sd, si, sp_ = self.P.slab.data, self.P.local_indices, self.P.slab.indptr
+            self.h_x = torch.from_numpy(x[r0:r1].copy()).pin_memory()
+            self.h2d_bytes = sd.nbytes + si.nbytes + sp_.nbytes + 4 * (r1 - r0)
+        else:
+            sd, si, sp_ = _slice_rows(d, i, p, r0, r1)
+            self.A = ms.csr_array((torch.from_numpy(sd).to(device), torch.from_numpy(si).to(device),
+                                   torch.from_numpy(sp_).to(device)), shape=(self.rows, self.n), canonical=True)
+            self.plan = self.A.spmv_plan()
+            self.x = torch.from_numpy(x).to(device)
+            self.h_x = torch.from_numpy(x).pin_memory()
+            self.h2d_bytes = sd.nbytes + si.nbytes + sp_.nbytes + x.nbytes
+        self.host = (sd, si, sp_, x)
         self.y = torch.empty(self.rows, dtype=torch.float32, device=device)
-        self.h_d, self.h_i, self.h_p = (torch.from_numpy(a).pin_memory() for a in (d, i, p))
-        self.h_x = torch.from_numpy(x).pin_memory()
+        self.h_d, self.h_i, self.h_p = (torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in (sd, si, sp_))
         self.h_y = torch.empty(self.rows, dtype=torch.float32).pin_memory()
-        self.dev = device
-        self.launches_per_step = 1 + (1 if self.plan.n_long > 0 else 0)
-        self.h2d_bytes = d.nbytes + i.nbytes + p.nbytes + x.nbytes
+        self.launches_per_step = 1 + (1 if self.plan.n_long > 0 else 0) + (2 if self.sharded and world > 1 else 0)
         self.d2h_bytes = self.rows * 4
-        self.local_bytes = d.size * (4 + ib) + ib * (self.rows + 1) + 4 * self.n + 4 * self.rows
+        self.local_bytes = sd.size * (4 + ib) + ib * (self.rows + 1) + 4 * self.n + 4 * self.rows
 
     def step(self):
         from mlx_sparse import _native
 
-        _native.csr_matvec(self.A.data, self.A.indices, self.A.indptr, self.x, self.A.shape, plan=self.plan,
+        if self.sharded and self.world > 1:
+            xl = self.P.exchange(self.x_own)
+        else:
+            xl = self.x
+        _native.csr_matvec(self.A.data, self.A.indices, self.A.indptr, xl, self.A.shape, plan=self.plan,
                            out=self.y)
 
     def e2e_step(self):
         import mlx_sparse as ms
 
-        A = ms.csr_array((self.h_d.to(self.dev, non_blocking=True), self.h_i.to(self.dev, non_blocking=True),
-                          self.h_p.to(self.dev, non_blocking=True)), shape=self.A.shape, canonical=True)
-        y = A @ self.h_x.to(self.dev, non_blocking=True)
+        dev = self.dev
+        A = ms.csr_array((self.h_d.to(dev, non_blocking=True), self.h_i.to(dev, non_blocking=True),
+                          self.h_p.to(dev, non_blocking=True)), shape=self.A.shape, canonical=True)
+        xd = self.h_x.to(dev, non_blocking=True)
+        if self.sharded and self.world > 1:
+            xd = self.P.exchange(xd)
+        y = A @ xd
         self.h_y.copy_(y, non_blocking=True)
+
+    def parity(self):
+        """N > 1: the row-sharded product gathered on rank 0 against the
+        single-GPU product of the whole matrix (per row 1e-5)."""
+        import torch
+        import torch.distributed as dist
+
+        self.step()
+        ys = [None] * self.world
+        dist.all_gather_object(ys, (self.r0, self.y.cpu().numpy()))
+        if self.rank != 0:
+            return None
+        import mlx_sparse as ms
+
+        d, i, p, x = self.full
+        A = ms.csr_array((torch.from_numpy(d).to(self.dev), torch.from_numpy(i).to(self.dev),
+                          torch.from_numpy(p).to(self.dev)), shape=self.shape, canonical=True)
+        xd = torch.from_numpy(x).to(self.dev)
+        y1 = (A @ xd).cpu().numpy()
+        scale = (ms.csr_array((A.data.abs(), A.indices, A.indptr), shape=self.shape, canonical=True)
+                 @ xd.abs()).cpu().numpy()
+        yg = np.zeros_like(y1)
+        for r0, yl in ys:
+            yg[r0:r0 + yl.size] = yl
+        err = float(np.max(np.abs(yg - y1) / np.maximum(np.maximum(np.abs(y1), scale), 1e-30)))
+        del A
+        return {"status": "ok" if err <= 1e-5 else "FAIL", "check": "gathered y vs 1-GPU product of the whole matrix",
+                "max_rel_row_err": err}
 
     def cpu_sample(self, workers, budget_s=10.0):
         from oracle import oracle
 
-        d, i, p, x = self.host
+        d, i, p, x = self.full
         times = []
         t_end = time.perf_counter() + budget_s
         while time.perf_counter() < t_end or len(times) < 3:
             t0 = time.perf_counter()
-            oracle.csr_matvec(d, i, p, x, self.rows, workers=workers)
+            oracle.csr_matvec(d, i, p, x, self.shape[0], workers=workers)
             times.append(time.perf_counter() - t0)
             if len(times) >= 500:
                 break
         med = statistics.median(times)
-        return self.local_bytes / med / 1e9, f"full matrix, median of {len(times)} runs"
+        return self.problem_bytes / med / 1e9, f"full matrix, median of {len(times)} runs"
 
 
 class PcgWorkload(Workload):
@@ -322,15 +414,21 @@ class PcgWorkload(Workload):
                 "solver": "Jacobi PCG, rtol 1e-6, maxiter 2000, x0 = 0", "index": "int32",
                 "l2": "inputs (1.2 GB) exceed L2"}
 
+    def setup_host(self):
+        (d, i, p), (n, _) = wl.poisson3d(self.m)
+        xs = wl.uniform_vector(n, 1)
+        self.n, self.nnz = n, d.size
+        self.bytes_per_iter = 8 * d.size + 4 * (n + 1) + 52 * n
+        self.host = (d, i, p, xs)
+
     def setup(self, rank, world, device):
         import torch
         import mlx_sparse as ms
 
-        (d, i, p), (n, _) = wl.poisson3d(self.m)
-        xs = wl.uniform_vector(n, 1)
-        self.n, self.nnz, self.world, self.dev = n, d.size, world, device
-        self.bytes_per_iter = 8 * d.size + 4 * (n + 1) + 52 * n
-        self.host = (d, i, p, xs)
+        self.setup_host()
+        d, i, p, xs = self.host
+        n = self.n
+        self.world, self.dev, self.rank = world, device, rank
         if world == 1:
             self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
                                    torch.from_numpy(p).to(device)), shape=(n, n), canonical=True)
@@ -346,6 +444,7 @@ class PcgWorkload(Workload):
             from mlx_sparse import _native
 
             slab = dd.build_slab(d, i, p, n, rank, world)
+            self.r0 = slab.r0
             self.slab = dd.DeviceSlab(slab, device)
             xl = np.concatenate([xs[slab.r0:slab.r1], xs[slab.halo_cols]]).astype(np.float32)
             self.b = _native.csr_matvec(self.slab.data, self.slab.indices, self.slab.indptr,
@@ -380,6 +479,47 @@ class PcgWorkload(Workload):
         else:
             _, info, _, its = self.solver.solve(self.b, inv_diag_local=self.inv, rtol=1e-6, maxiter=2000)
             self.iterations, self.info = its, info
+
+    def parity(self):
+        """N > 1: the sharded solve against the same system solved on rank 0's
+        GPU alone (status, iterations +-2, max |x - x_1|), and against the
+        oracle's committed 256^3 result (tests/golden/pcg_poisson3d.json:
+        status 0, 147 iterations, the first entries of x)."""
+        import torch
+        import torch.distributed as dist
+
+        x, info, _, its = self.solver.solve(self.b, inv_diag_local=self.inv, rtol=1e-6, maxiter=2000)
+        parts = [None] * self.world
+        dist.all_gather_object(parts, (self.r0, x.cpu().numpy(), info, its))
+        if self.rank != 0:
+            return None
+        import mlx_sparse as ms
+
+        d, i, p, xs = self.host
+        n = self.n
+        xg = np.zeros(n, np.float32)
+        for r0, xl, _, _ in parts:
+            xg[r0:r0 + xl.size] = xl
+        A = ms.csr_array((torch.from_numpy(d).to(self.dev), torch.from_numpy(i).to(self.dev),
+                          torch.from_numpy(p).to(self.dev)), shape=(n, n), canonical=True)
+        b = A @ torch.from_numpy(xs).to(self.dev)
+        x1, inf1 = ms.linalg.cg(A, b, M=ms.linalg.preconditioners.jacobi(A), rtol=1e-6, maxiter=2000,
+                                return_info=True)
+        diff = float(np.max(np.abs(xg - x1.cpu().numpy())))
+        out = {"check": "gathered x vs 1-GPU solve on rank 0, and vs the oracle's 256^3 fixture",
+               "iterations": its, "iterations_1gpu": inf1.iterations, "info": info,
+               "ranks_agree": all(pp[2:] == parts[0][2:] for pp in parts), "max_abs_dx_vs_1gpu": diff}
+        ok = out["ranks_agree"] and info == inf1.status == 0 and abs(its - inf1.iterations) <= 2 and diff <= 1e-3
+        gpath = os.path.join(ROOT, "tests", "golden", "pcg_poisson3d.json")
+        if self.m == 256 and os.path.exists(gpath):
+            with open(gpath) as f:
+                g = json.load(f)["256"]
+            head = float(np.max(np.abs(xg[:8] - np.asarray(g["x_head"], np.float32))))
+            out.update(golden_iterations=g["iterations"], max_abs_dx_head_vs_golden=head)
+            ok = ok and abs(its - g["iterations"]) <= 2 and head <= 1e-3
+        del A
+        out["status"] = "ok" if ok else "FAIL"
+        return out
 
     def e2e_step(self):
         import mlx_sparse as ms
@@ -424,17 +564,23 @@ class SpgemmWorkload(Workload):
     def __init__(self, n=1 << 18, per_row=8, seed=4):
         self.n, self.per_row, self.seed = n, per_row, seed
         self.name = "spgemm"
+        self.local_bytes = None
 
     def config(self):
         return {"workload": self.name, "matrix": f"{self.n}x{self.n}, {self.per_row} nnz/row uniform",
                 "output": "canonical CSR, exact zeros pruned", "index": "int32"}
 
+    def setup_host(self):
+        (d, i, p), _ = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
+        self.host = (d, i, p)
+        self.products = int(np.sum(np.diff(p)[i]))
+
     def setup(self, rank, world, device):
         import torch
         import mlx_sparse as ms
 
-        (d, i, p), _ = wl.random_k_per_row(self.n, self.n, self.per_row, self.seed)
-        self.host = (d, i, p)
+        self.setup_host()
+        d, i, p = self.host
         self.A = ms.csr_array((torch.from_numpy(d).to(device), torch.from_numpy(i).to(device),
                                torch.from_numpy(p).to(device)), shape=(self.n, self.n), canonical=True)
         C = self.A @ self.A
@@ -468,8 +614,11 @@ class SpgemmWorkload(Workload):
         t_end = time.perf_counter() + budget_s
         while time.perf_counter() < t_end or len(times) < 2:
             t0 = time.perf_counter()
-            oracle.csr_matmat((d, i, p), (d, i, p), (self.n, self.n), (self.n, self.n))
+            c = oracle.csr_matmat((d, i, p), (d, i, p), (self.n, self.n), (self.n, self.n))
+            self.c_nnz = int(c[0].size)
             times.append(time.perf_counter() - t0)
+        if self.local_bytes is None:  # reference arm: compulsory bytes from the oracle's own output
+            self.local_bytes = 2 * (8 * d.size + 4 * (self.n + 1)) + 8 * self.c_nnz + 4 * (self.n + 1)
         return self.local_bytes / statistics.median(times) / 1e9, f"full product, median of {len(times)} runs, 1 thread"
 
 
@@ -478,6 +627,8 @@ WORKLOADS = {
     "spmm_bf16": lambda: SpmmWorkload(bf16=True),
     "spmv_lap2d": lambda: SpmvWorkload("lap2d"),
     "spmv_powerlaw": lambda: SpmvWorkload("powerlaw"),
+    "spmv_lap2d_xsharded": lambda: SpmvWorkload("lap2d", sharded=True),
+    "spmv_powerlaw_xsharded": lambda: SpmvWorkload("powerlaw", sharded=True),
     "pcg_poisson3d": lambda: PcgWorkload(),
     "spgemm": lambda: SpgemmWorkload(),
 }
@@ -596,6 +747,8 @@ def run_b200(args):
         "gpu_launches": int(wk.launches_per_step * args.steps),
         "clocks": clock,
     }
+    if world > 1 and hasattr(wk, "parity"):
+        line["parity"] = wk.parity()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         workers = len(os.sched_getaffinity(0))
         v, sample = wk.cpu_sample(workers, budget_s=args.cpu_budget)
@@ -607,7 +760,8 @@ def run_b200(args):
     if not args.no_extras:
         # every rank takes part in the multi-GPU extras; rank 0 reports
         names = (["spmv_lap2d", "spmv_powerlaw", "spmm_bf16", "spmm_f32", "pcg_poisson3d", "spgemm"]
-                 if world == 1 else ["pcg_poisson3d"])
+                 if world == 1 else ["pcg_poisson3d", "spmv_powerlaw", "spmv_powerlaw_xsharded",
+                                     "spmv_lap2d_xsharded"])
         extras = {}
         for name in names:
             if name == args.workload:
@@ -672,9 +826,18 @@ def _extra(name, args, device, peak, rank=0, world=1):
         out.update({"iterations": wk.iterations, "info": wk.info, "bytes_per_iteration": int(wk.bytes_per_iter)})
     if isinstance(wk, SpgemmWorkload):
         out["products_per_s"] = round(wk.products / (ms_max * 1e-3), 1)
-    if rank == 0 and world == 1 and getattr(args, "extra_cpu", False):
-        v, sample = wk.cpu_sample(len(os.sched_getaffinity(0)), budget_s=5.0)
-        out["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "sample": sample}
+    if world > 1 and hasattr(wk, "parity"):
+        out["parity"] = wk.parity()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        workers = len(os.sched_getaffinity(0))
+        v, sample = wk.cpu_sample(workers, budget_s=args.cpu_budget / 2)
+        out["cpu_baseline"] = {"value": round(v, 3), "unit": wk.unit, "cores": workers, "kind": "port",
+                               "sample": sample + "; oracle/oracle.cpp restatement of the reference CPU loop"}
+        if not isinstance(wk, (PcgWorkload, SpgemmWorkload)):  # those are serial by construction
+            v1, _ = wk.cpu_sample(1, budget_s=2.0)
+            out["cpu_baseline"]["value_1_worker"] = round(v1, 3)
+        else:
+            out["cpu_baseline"]["cores"] = 1
     del wk
     torch.cuda.empty_cache()
     return out
@@ -695,6 +858,8 @@ def run_reference(args):
         v, sample = wk.cpu_sample(workers, budget_s=0.0)
         vals.append(v)
     v = statistics.median(vals)
+    if isinstance(wk, (PcgWorkload, SpgemmWorkload)):
+        workers = 1  # the reference's solver loop and the oracle's SpGEMM run on one thread
     line = {"metric": METRIC, "value": round(v, 3), "unit": wk.unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": wk.scaling, "vs_baseline": None,
             "dtype": wk.dtype, "data": "synthetic (seeded numpy default_rng, BASELINE config shapes)",
@@ -719,15 +884,9 @@ def _cpu_model():
 
 
 def _setup_host_only(wk):
+    wk.setup_host()
     if isinstance(wk, SpmmWorkload):
-        (d, i, p), shape = wl.random_k_per_row(wk.n, wk.n, wk.per_row, wk.seed)
-        B = np.random.default_rng(wk.seed + 100).uniform(-1, 1, (wk.n, wk.k)).astype(np.float32)
-        wk.host, wk.rows = (d, i, p, B), wk.n
-    else:
-        (d, i, p), shape = wk.make()
-        x = wl.uniform_vector(shape[1], wk.x_seed)
-        wk.host, wk.rows, wk.n = (d, i, p, x), shape[0], shape[1]
-        wk.local_bytes = d.size * (4 + wk.it_bytes) + wk.it_bytes * (wk.rows + 1) + 8 * wk.n
+        wk.rows = wk.n
 
 
 def main():
@@ -738,7 +897,6 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="spmm_f32", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--extra-cpu", action="store_true", help="also time the CPU oracle for every extra workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()

@@ -54,6 +54,19 @@ MSX_API const char *msx_last_error(void);
 MSX_API int msx_version(void);
 MSX_API int msx_compiled_sm(void);
 
+/* Device-side error check. The SpMV kernels that stage tiles with bulk copies
+ * wait on shared-memory barriers with a bounded number of polls; if a wait
+ * gives up, the kernel stops, records the event in a per-device flag and the
+ * rows it had not reached stay unwritten. The flag is sticky: this call
+ * synchronises `stream`, reads and clears the flag of the current device and
+ * returns MSX_ERR_RUNTIME if it was set. No counterpart in the reference,
+ * whose CPU loops cannot time out. */
+MSX_API int msx_check_device_errors(void *stream);
+/* Test hook: the number of polls those waits make before giving up
+ * (default 2^22; 0 makes every wait give up at once; negative restores the
+ * default). Process-wide. */
+MSX_API int msx_debug_set_spmv_poll_limit(int64_t polls);
+
 /* ------------------------------------------------------------------------ */
 /* SpMV plan: row-length bins of a CSR matrix.                              */
 /* ------------------------------------------------------------------------ */
@@ -92,9 +105,10 @@ MSX_API int msx_csr_matvec(int value_dtype, int index_dtype, const void *data,
  * Same algorithm and results as msx_csr_matvec with plan == NULL, but the
  * tile partition and split-row partials live in one fixed 4 MiB device array
  * per GPU (held from library load until exit), which limits n_rows + nnz to
- * about 223 million; larger inputs return MSX_ERR_INVALID. The first call on a
- * device looks up that array's device address (cudaGetSymbolAddress), so make
- * it before any stream capture. All calls share the array: calls whose work
+ * about 223 million; larger inputs return MSX_ERR_INVALID. Every call looks
+ * up that array's device address (cudaGetSymbolAddress); the first call on a
+ * device may also load the module there, so make it before any stream
+ * capture. All calls share the array: calls whose work
  * overlaps on the GPU race and must be ordered on one stream. */
 MSX_API int msx_csr_matvec_noalloc(int value_dtype, int index_dtype,
                                    const void *data, const void *indices,

@@ -77,6 +77,20 @@ int msx_compiled_sm(void) {
 #endif
 }
 
+int msx_check_device_errors(void *stream) {
+  return guarded([&] {
+    MSX_CUDA(cudaStreamSynchronize(as_stream(stream)));
+    if (spmv_take_error())
+      fail(MSX_ERR_RUNTIME,
+           "an SpMV bulk-copy wait on this device gave up (poll limit reached); the results of SpMV calls "
+           "made since the last check are incomplete.");
+  });
+}
+
+int msx_debug_set_spmv_poll_limit(int64_t polls) {
+  return guarded([&] { spmv_set_poll_limit(polls); });
+}
+
 int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows, int64_t nnz, void *stream,
                          msx_spmv_plan **out) {
   return guarded([&] {

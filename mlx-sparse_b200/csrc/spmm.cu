@@ -19,11 +19,6 @@
 
 namespace msx {
 
-bool spmm_tma_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
-                  const void *rhs, int64_t k, void *out, int64_t n_rows, int64_t n_cols, int64_t nnz,
-                  cudaStream_t stream);
-int64_t spmm_tma_max_row();
-
 namespace {
 
 // L2 eviction-priority policies: the RHS slab is gathered repeatedly and should
@@ -83,8 +78,7 @@ __device__ __forceinline__ void store_vec(T *p, const float (&in)[V]) {
 template <typename T, typename I, int V, int L, int kUnroll, int kMinBlocks, int kPairs = 1>
 __global__ void __launch_bounds__(256, kMinBlocks)
 spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
-            const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols,
-            int64_t skip_le) {
+            const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
   constexpr int kRowsPerBlock = 256 / L;
   const int lane = threadIdx.x & 31;
   const int lane_in_row = threadIdx.x % L;
@@ -94,8 +88,7 @@ spmm_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *
   const int64_t slab0 = blockIdx.y * slab_cols;
   const int64_t slab1 = min(slab0 + slab_cols, k);
   const int64_t p0 = row_ok ? (int64_t)indptr[row] : 0;
-  int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
-  if (p1 - p0 <= skip_le) return;  // rows done by the TMA kernel (whole group shares the row)
+  const int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
   const uint64_t pol_rhs = policy_evict_last();
   for (int64_t c = slab0 + (int64_t)lane_in_row * V; c - (int64_t)lane_in_row * V < slab1; c += (int64_t)L * V) {
     const bool col_ok = c < slab1;
@@ -249,55 +242,20 @@ void launch_spmm_async(dim3 grid, cudaStream_t stream, const T *data, const I *i
 
 template <typename T, typename I, int V, int L>
 void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs, T *out, int64_t n_rows,
-                 int64_t k, int64_t slab_cols, cudaStream_t stream, int64_t skip_le = -1) {
+                 int64_t k, int64_t slab_cols, cudaStream_t stream) {
   constexpr int kRowsPerBlock = 256 / L;
   const int64_t n_slabs = ceil_div(k, slab_cols);
   dim3 grid((unsigned)ceil_div(n_rows, kRowsPerBlock), (unsigned)n_slabs);
-  // Variant (gathers in flight per lane, resident CTAs per SM) for tuning:
-  // MSX_SPMM_VARIANT=0..12 (11, 12: cp.async gathers, 8 or 12 deep); 0 is the default (= 11 for 16-byte vectors).
-  static const int variant = [] {
-    const char *e = getenv("MSX_SPMM_VARIANT");
-    return e && *e ? atoi(e) : 0;
-  }();
-  switch (variant) {
-  case 1: spmm_kernel<T, I, V, L, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 2: spmm_kernel<T, I, V, L, 8, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 3: spmm_kernel<T, I, V, L, 16, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 4: spmm_kernel<T, I, V, L, 4, 8><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 5: spmm_kernel<T, I, V, L, 8, 4, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 6: spmm_kernel<T, I, V, L, 8, 3, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 7: spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 8: spmm_kernel<T, I, V, L, 8, 4, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 9: spmm_kernel<T, I, V, L, 8, 3, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 10: spmm_kernel<T, I, V, L, 6, 4, 1><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le); break;
-  case 11:
-  case 12:
-    if constexpr (V * sizeof(T) == 16) {
-      if (skip_le < 0) {
-        if (variant == 11)
-          launch_spmm_async<T, I, V, L, 8>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
-        else
-          launch_spmm_async<T, I, V, L, 12>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
-        break;
-      }
-    }
-    spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
-    break;
-  default:
-    // measured defaults: cp.async gathers 8 deep for 16-byte vectors (fp32
-    // 0.555 ms vs 0.847, bf16 0.307 vs 0.800 ms on the 1M x 1M, 16/row, k = 64
-    // config); else the register kernel with 8 gathers in flight at 4 CTAs/SM
-    // for 4-byte values, 4 in flight at 6 CTAs/SM for 2-byte values
-    if constexpr (V * sizeof(T) == 16) {
-      if (skip_le < 0) {
-        launch_spmm_async<T, I, V, L, 8>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
-        break;
-      }
-    }
-    if constexpr (sizeof(T) == 2)
-      spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
-    else
-      spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, skip_le);
+  // measured defaults: cp.async gathers 8 deep for 16-byte vectors (fp32
+  // 0.555 ms vs 0.847, bf16 0.307 vs 0.800 ms on the 1M x 1M, 16/row, k = 64
+  // config); else the register kernel with 8 gathers in flight at 4 CTAs/SM
+  // for 4-byte values, 4 in flight at 6 CTAs/SM for 2-byte values
+  if constexpr (V * sizeof(T) == 16) {
+    launch_spmm_async<T, I, V, L, 8>(grid, stream, data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  } else if constexpr (sizeof(T) == 2) {
+    spmm_kernel<T, I, V, L, 4, 6, 2><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
+  } else {
+    spmm_kernel<T, I, V, L, 8, 4><<<grid, 256, 0, stream>>>(data, indices, indptr, rhs, out, n_rows, k, slab_cols);
   }
   MSX_CHECK_LAUNCH();
 }
@@ -350,12 +308,6 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
       // env override forces it); otherwise column slabs whose RHS part fits
       // the budget (128, 64 or 32 bytes per RHS row), so the random row
       // gathers of a slab hit L2 while the matrix is re-streamed per slab.
-      // TMA row gathers when the RHS rows are whole 128/256-byte boxes; the
-      // register kernel then only takes the rows too long for a TMA stage.
-      int64_t skip_le = -1;
-      if (spmm_tma_run(value_dtype, index_dtype, data, indices, indptr, rhs, k, out, n_rows, n_cols, nnz,
-                       stream))
-        skip_le = spmm_tma_max_row();
       const int64_t budget = spmm_l2_budget();
       const int64_t slab_bytes = spmm_slab_bytes(n_cols, budget);
       const bool one_pass = n_cols * k * elem <= budget || k * elem <= slab_bytes;
@@ -363,24 +315,24 @@ void spmm_run(int value_dtype, int index_dtype, const void *data, const void *in
         const int64_t kv = k / kVec;  // 16-byte vectors per row
         const int64_t slab_vecs = one_pass ? kv : slab_bytes / 16;
         if (slab_vecs >= 16) {
-          launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream, skip_le);
+          launch_spmm<T, I, kVec, 16>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 16) * 16 * kVec, stream);
         } else if (slab_vecs >= 8) {
-          launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream, skip_le);
+          launch_spmm<T, I, kVec, 8>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 8) * 8 * kVec, stream);
         } else if (slab_vecs >= 4) {
-          launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream, skip_le);
+          launch_spmm<T, I, kVec, 4>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 4) * 4 * kVec, stream);
         } else if (slab_vecs >= 2) {
-          launch_spmm<T, I, kVec, 2>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 2) * 2 * kVec, stream, skip_le);
+          launch_spmm<T, I, kVec, 2>(d, ix, ip, b, o, n_rows, k, ceil_div(slab_vecs, 2) * 2 * kVec, stream);
         } else {
-          launch_spmm<T, I, kVec, 1>(d, ix, ip, b, o, n_rows, k, kVec, stream, skip_le);
+          launch_spmm<T, I, kVec, 1>(d, ix, ip, b, o, n_rows, k, kVec, stream);
         }
       } else {
         // Scalar path for widths that are not a multiple of the 16-byte vector.
         if (k >= 16) {
-          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, one_pass ? ceil_div(k, 16) * 16 : 32, stream, skip_le);
+          launch_spmm<T, I, 1, 16>(d, ix, ip, b, o, n_rows, k, one_pass ? ceil_div(k, 16) * 16 : 32, stream);
         } else if (k >= 4) {
-          launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream, skip_le);
+          launch_spmm<T, I, 1, 4>(d, ix, ip, b, o, n_rows, k, k, stream);
         } else {
-          launch_spmm<T, I, 1, 1>(d, ix, ip, b, o, n_rows, k, k, stream, skip_le);
+          launch_spmm<T, I, 1, 1>(d, ix, ip, b, o, n_rows, k, k, stream);
         }
       }
     });

@@ -16,6 +16,8 @@
 // than kSplitRowLen are split between tiles; their tile partials go to scratch
 // and a small fixup kernel adds them in tile order (deterministic, no
 // atomics on values).
+#include <atomic>
+
 #include "spmv.cuh"
 
 namespace msx {
@@ -114,18 +116,29 @@ void spmv_build_plan(int index_dtype, const void *indptr, int64_t n_rows, int64_
 
 namespace {
 __device__ int g_spmv_error;
+std::atomic<long long> g_poll_limit{kMaxPolls};
+}  // namespace
+
+// Looked up on every call (cheap), so the address is right for whatever
+// context is current, including after a device reset.
+int *spmv_error_flag() {
+  int *ptr = nullptr;
+  MSX_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_spmv_error));
+  return ptr;
 }
 
-int *spmv_error_flag() {
-  static thread_local int cached_dev = -1;
-  static thread_local int *ptr = nullptr;
-  int dev = 0;
-  MSX_CUDA(cudaGetDevice(&dev));
-  if (dev != cached_dev) {
-    MSX_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_spmv_error));
-    cached_dev = dev;
+long long spmv_poll_limit() { return g_poll_limit.load(std::memory_order_relaxed); }
+void spmv_set_poll_limit(long long v) { g_poll_limit.store(v < 0 ? kMaxPolls : v, std::memory_order_relaxed); }
+
+// Reads and clears this device's SpMV timeout flag.
+bool spmv_take_error() {
+  int v = 0;
+  MSX_CUDA(cudaMemcpyFromSymbol(&v, g_spmv_error, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    MSX_CUDA(cudaMemcpyToSymbol(g_spmv_error, &zero, sizeof(int)));
   }
-  return ptr;
+  return v != 0;
 }
 
 bool spmv_tma_ok(const void *data, const void *indices, const void *indptr) {

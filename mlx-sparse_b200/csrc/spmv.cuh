@@ -207,6 +207,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Waits (at most kMaxPolls polls) for phase `parity` of `bar` to complete, so
+// no bulk copy is still writing into shared memory when the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  for (long long polls = 0; polls < kMaxPolls && !mbar_try_wait(bar, parity); ++polls) {
+  }
+}
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -271,14 +278,15 @@ __device__ __forceinline__ void tma_issue(int64_t t, TmaStage<T, I> &st, uint64_
 }
 
 // Persistent CTA over tiles blockIdx.x, +gridDim.x, ... with a two-stage TMA
-// pipeline. `err` receives 1 if an mbarrier wait ever exceeds kMaxPolls.
+// pipeline. `err` receives 1 if an mbarrier wait exceeds `poll_limit` polls;
+// the CTA then stops and the rows of its remaining tiles are not written.
 template <typename T, typename I, typename Epi>
 __global__ void __launch_bounds__(kSpmvThreads)
 spmv_tiles_tma_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
                       const T *__restrict__ x, T *__restrict__ y, const int64_t *__restrict__ tile_row,
                       const int64_t *__restrict__ tile_nz, float *__restrict__ carry_head,
                       float *__restrict__ carry_tail, int64_t n_tiles, int64_t nnz, int64_t n_rows, Epi epi,
-                      int *__restrict__ err) {
+                      int *__restrict__ err, long long poll_limit) {
   extern __shared__ __align__(128) unsigned char dyn_smem[];
   TmaSmem<T, I> &sm = *reinterpret_cast<TmaSmem<T, I> *>(dyn_smem);
   const int tid = threadIdx.x;
@@ -301,12 +309,20 @@ spmv_tiles_tma_kernel(const T *__restrict__ data, const I *__restrict__ indices,
       tma_issue<T, I>(t_next, sm.stage[s ^ 1], &sm.bar[s ^ 1], data, indices, indptr, nnz, n_rows, tile_row,
                       tile_nz);
     }
-    long long polls = 0;
-    while (!mbar_try_wait(&sm.bar[s], phase[s])) {
-      if (++polls > kMaxPolls) {
-        if (tid == 0) atomicOr(err, 1);
-        return;
+    // Bounded wait (poll_limit polls; 0 fails at once, which tests use to
+    // reach this path). The CTA leaves together: one thread records the
+    // timeout and waits, with the fixed bound, for the copies still in flight
+    // into this CTA's shared memory before the CTA exits.
+    bool done = false;
+    for (long long polls = 0; polls < poll_limit && !(done = mbar_try_wait(&sm.bar[s], phase[s])); ++polls) {
+    }
+    if (__syncthreads_or(!done)) {
+      if (tid == 0) {
+        atomicOr(err, 1);
+        mbar_drain(&sm.bar[s], phase[s]);
+        if (t_next < n_tiles) mbar_drain(&sm.bar[s ^ 1], phase[s ^ 1]);
       }
+      return;
     }
     phase[s] ^= 1u;
 
@@ -368,8 +384,16 @@ bool spmv_tma_ok(const void *data, const void *indices, const void *indptr);
 template <typename T, typename I, typename Epi>
 int spmv_grid_for(int64_t n_tiles, bool tma);
 int spmv_grid(int64_t n_tiles);
-// Device int the TMA kernels flag when an mbarrier wait times out (per device).
+// Device int the TMA kernels flag when an mbarrier wait times out (per device;
+// sticky until msx_check_device_errors reads and clears it).
 int *spmv_error_flag();
+// Poll bound of the TMA kernels' mbarrier waits (kMaxPolls unless changed by
+// msx_debug_set_spmv_poll_limit).
+long long spmv_poll_limit();
+// Sets it (a negative value restores kMaxPolls); process-wide.
+void spmv_set_poll_limit(long long polls);
+// Reads and clears the current device's timeout flag.
+bool spmv_take_error();
 // carry_scratch: float[2*n_tiles] when launch_fixup, else may be null.
 void spmv_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
               const void *x, void *y, int64_t n_rows, int64_t nnz, const void *plan_dev, int64_t n_tiles,
@@ -390,7 +414,7 @@ void launch_spmv_tiles(const T *data, const I *indices, const I *indptr, const T
   if (tma) {
     spmv_tiles_tma_kernel<T, I, Epi><<<grid, kSpmvThreads, tma_smem_bytes<T, I>(), stream>>>(
         data, indices, indptr, x, y, tile_row, tile_nz, carry_head, carry_tail, n_tiles, nnz, n_rows, epi,
-        spmv_error_flag());
+        spmv_error_flag(), spmv_poll_limit());
   } else {
     spmv_tiles_kernel<T, I, Epi><<<grid, kSpmvThreads, 0, stream>>>(data, indices, indptr, x, y, tile_row, tile_nz,
                                                                     carry_head, carry_tail, n_tiles, epi);

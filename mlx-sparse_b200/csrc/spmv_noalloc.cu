@@ -11,16 +11,17 @@
 //
 // Limits and sharing: the array holds kNoAllocScratchBytes (4 MiB) on every
 // GPU that loads the library, for the life of the process. A call needs
-// 16 + 24 * n_tiles + 8 bytes, n_tiles = ceil((n_rows + nnz) / 1280), i.e. up
-// to about 223 million rows + nonzeros; larger problems are rejected with
-// MSX_ERR_INVALID. All calls on a device share the one array, so two calls
+// round_up_256(16 + 16 * (n_tiles + 1)) + 8 * n_tiles bytes (tile partition,
+// then two float partials per tile), n_tiles = ceil((n_rows + nnz) / 1280),
+// i.e. up to about 223 million rows + nonzeros; larger problems are rejected
+// with MSX_ERR_INVALID. All calls on a device share the one array, so two calls
 // whose kernels overlap on the GPU (different streams, or different host
 // threads without ordering) race and corrupt each other's results; order them
 // on one stream. The partition is rebuilt on each call, so nothing carried
 // over from the previous call is read; the split-row counter is cleared each
-// call.
-#include <mutex>
-
+// call. Every call looks up the array's device address
+// (cudaGetSymbolAddress); the first call on a device may also load the module
+// there, so make that first call before any stream capture.
 #include "spmv.cuh"
 
 namespace msx {
@@ -31,27 +32,17 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void *g_noalloc_ptr[kMaxDevices] = {};
-
-// Device address of the array on the current device. The array's host-side
-// name is only a stand-in for the symbol, so kernels must be given this
-// address. Resolved once per device, on the first call made on that device.
+// Device address of the array in the current device's context. The array's
+// host-side name is only a stand-in for the symbol, so kernels must be given
+// this address. It is looked up on every call (cheap), so it is always the
+// address in the context that is current now, also after a device reset.
 void *noalloc_scratch_current_device() {
-  int dev = 0;
-  MSX_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) fail(MSX_ERR_RUNTIME, "msx_csr_matvec_noalloc: device index out of range.");
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      fail(MSX_ERR_CUDA, std::string("cudaGetSymbolAddress for the no-allocation scratch failed: ") +
-                             cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
-  }
-  return g_noalloc_ptr[dev];
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    fail(MSX_ERR_CUDA, std::string("cudaGetSymbolAddress for the no-allocation scratch failed: ") +
+                           cudaGetErrorString(e));
+  return p;
 }
 
 }  // namespace

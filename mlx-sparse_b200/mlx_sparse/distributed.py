@@ -294,3 +294,139 @@ def dist_cg(comm: Communicator, A: DeviceSlab, b_local, *, x0_local=None, inv_di
             int(peers.shape[0]), peers.ctypes.data, sc.ctypes.data, rc.ctypes.data, A.send_idx.data_ptr(),
             ctypes.addressof(info), ctypes.addressof(res), ctypes.addressof(its), _native.stream_ptr(dev)))
     return x, info.value, res.value, its.value
+
+
+# ---------------------------------------------------------------------------
+# Row-sharded SpMV / SpMM with the dense operand sharded too (GPU, NCCL)
+# ---------------------------------------------------------------------------
+def allgather_layout(indices, indptr, ranges, r0: int, r1: int):
+    """Column renumbering of rows [r0, r1) for the all-gather exchange.
+
+    Every rank contributes its owned block of x padded to ``max_rows`` =
+    the longest row range, so after ``all_gather_into_tensor`` global column
+    ``c`` owned by rank ``q`` sits at ``q * max_rows + (c - start_q)``.
+    Returns the renumbered indices of the slab (same dtype) and ``max_rows``.
+    """
+    indptr = np.asarray(indptr)
+    starts = np.asarray([a for a, _ in ranges], dtype=np.int64)
+    max_rows = max(b - a for a, b in ranges) if ranges else 0
+    cols = np.asarray(indices[int(indptr[r0]):int(indptr[r1])]).astype(np.int64)
+    owner = np.searchsorted(starts, cols, side="right") - 1
+    local = owner * max_rows + (cols - starts[owner])
+    return local.astype(np.asarray(indices).dtype), int(max_rows)
+
+
+class OperandExchange:
+    """Gathers, for one rank's row slab, the entries of a row-sharded dense
+    operand (x, or the rows of B) that the slab's columns read.
+
+    Each rank owns rows ``r0:r1`` of A and the same entries of x. Two
+    exchanges over ``torch.distributed`` (NCCL on GPUs; gloo works for CPU
+    tensors):
+
+    - ``"halo"``: one ``all_to_all_single`` carrying exactly the entries each
+      peer reads (the slab's send lists, landing in halo order); suits banded
+      matrices (stencils), where a rank reads a few planes of its neighbours;
+    - ``"allgather"``: ``all_gather_into_tensor`` of the owned blocks padded
+      to the longest row range; suits random columns, which read almost all
+      of x anyway;
+    - ``"auto"``: halo when the halo is under a quarter of the global vector.
+
+    ``local_indices`` is the slab's column numbering into the buffer that
+    ``exchange`` fills. Created collectively by all ranks.
+    """
+
+    def __init__(self, data, indices, indptr, n: int, rank: int, world: int, device, *, mode: str = "auto",
+                 ranges=None):
+        import torch
+        import torch.distributed as dist
+
+        if mode not in ("auto", "halo", "allgather"):
+            raise ValueError("mode must be 'auto', 'halo' or 'allgather'")
+        indptr = np.asarray(indptr)
+        self.ranges = ranges or partition_rows(indptr, world)
+        self.rank, self.world, self.device, self.n = rank, world, device, n
+        self.r0, self.r1 = self.ranges[rank]
+        slab = build_slab(data, indices, indptr, n, rank, world, self.ranges)
+        halo_total = torch.tensor([slab.n_halo], dtype=torch.int64, device=device)
+        dist.all_reduce(halo_total)
+        if mode == "auto":
+            mode = "halo" if int(halo_total.item()) * 4 < n else "allgather"
+        self.mode = mode
+        self.slab = slab
+        if mode == "halo":
+            self.local_indices = slab.indices
+            self.n_local_cols = slab.n_owned + slab.n_halo
+            send = np.zeros(world, np.int64)
+            recv = np.zeros(world, np.int64)
+            send[slab.peers] = slab.send_counts
+            recv[slab.peers] = slab.recv_counts
+            self.send_splits, self.recv_splits = send.tolist(), recv.tolist()
+            self.send_idx = torch.from_numpy(slab.send_idx.astype(np.int64)).to(device)
+        else:
+            self.local_indices, self.max_rows = allgather_layout(indices, indptr, self.ranges, self.r0, self.r1)
+            self.n_local_cols = self.max_rows * world
+        self._buf = {}
+
+    def _get(self, key, shape, dtype):
+        import torch
+
+        if key not in self._buf:
+            self._buf[key] = torch.zeros(shape, dtype=dtype, device=self.device)
+        return self._buf[key]
+
+    def exchange(self, x_owned):
+        """Returns the local operand for x_owned (rows r0:r1 of x or B): owned
+        entries and those read from other ranks, in ``local_indices``
+        numbering. The buffer is reused by the next call."""
+        import torch.distributed as dist
+
+        tail = tuple(x_owned.shape[1:])
+        buf = self._get(("buf", tail, x_owned.dtype), (self.n_local_cols,) + tail, x_owned.dtype)
+        n_own = self.r1 - self.r0
+        if self.mode == "halo":
+            buf[:n_own].copy_(x_owned)
+            send = x_owned.index_select(0, self.send_idx)
+            dist.all_to_all_single(buf[n_own:], send, self.recv_splits, self.send_splits)
+        else:
+            mine = self._get(("own", tail, x_owned.dtype), (self.max_rows,) + tail, x_owned.dtype)
+            mine[:n_own].copy_(x_owned)  # the padding is never read
+            dist.all_gather_into_tensor(buf, mine)
+        return buf
+
+
+class DistProduct(OperandExchange):
+    """``y = A @ x`` and ``Y = A @ B`` over row slabs with x (or the rows of B)
+    sharded by the same row ranges as A: the distributed form of the
+    reference's ``csr_matvec`` / ``csr_matmul`` (``src/sparse/csr_matvec/
+    csr_matvec.cpp:79-168``, ``src/sparse/csr_matmul/csr_matmul.cpp:83-222``),
+    whose CPU path splits rows by the same nnz-weighted ranges across threads
+    (``src/common/cpu_parallel.cpp:202-253``).
+
+    Each rank passes its owned entries of x and gets its owned entries of y.
+    The operand exchange (``OperandExchange``) runs over NCCL; the local
+    product is the library's SpMV (with a cached row-bin plan) or SpMM.
+    """
+
+    def __init__(self, data, indices, indptr, n: int, rank: int, world: int, device, *, mode: str = "auto",
+                 ranges=None, dtype=None):
+        import torch
+
+        import mlx_sparse as ms
+
+        super().__init__(data, indices, indptr, n, rank, world, device, mode=mode, ranges=ranges)
+        slab = self.slab
+        vals = torch.from_numpy(np.ascontiguousarray(slab.data)).to(device)
+        if dtype is not None:
+            vals = vals.to(dtype)
+        idx = torch.from_numpy(np.ascontiguousarray(self.local_indices)).to(device)
+        ip = torch.from_numpy(np.ascontiguousarray(slab.indptr)).to(device)
+        self.A = ms.csr_array((vals, idx, ip), shape=(slab.n_owned, self.n_local_cols), canonical=True)
+        if slab.n_owned > 0:
+            self.A.spmv_plan()
+
+    def matvec(self, x_owned):
+        return self.A @ self.exchange(x_owned)
+
+    def matmul(self, b_owned):
+        return self.A @ self.exchange(b_owned)

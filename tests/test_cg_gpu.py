@@ -161,3 +161,29 @@ def test_cached_context_matches_stateless_solve(ms, orc):
         assert torch.equal(x, xs)
         assert info.status == info_s and info.iterations == its_s
     assert len(A._solvers) == 1
+
+
+@pytest.mark.parametrize("grid", ["64", "256"])
+def test_baseline_pcg_poisson3d(ms, orc, grid):
+    """BASELINE config 4 (256^3, and the 64^3 grid of the same recipe): the
+    device solve against the oracle's committed result in
+    tests/golden/pcg_poisson3d.json - same status, iterations within +-2,
+    the first entries of x, and a true relative residual within the target."""
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "pcg_poisson3d.json")) as f:
+        g = json.load(f)[grid]
+    (d, i, p), shape = wl.poisson3d(g["grid"])
+    n = shape[0]
+    b = orc.csr_matvec(d, i, p, wl.uniform_vector(n, 1), n, workers=8)
+    assert float(np.linalg.norm(b.astype(np.float64))) == pytest.approx(g["b_norm"], rel=1e-9)
+    A = _csr(ms, d, i, p, shape)
+    bd = _dev(b)
+    x, info = ms.linalg.cg(A, bd, M=ms.linalg.preconditioners.jacobi(A), rtol=1e-6, maxiter=2000,
+                           return_info=True)
+    assert info.status == g["info"] == 0
+    assert abs(info.iterations - g["iterations"]) <= 2, (info.iterations, g["iterations"])
+    np.testing.assert_allclose(x[:8].cpu().numpy(), g["x_head"], rtol=1e-4, atol=1e-4)
+    r = (bd.double() - (A @ x).double()).norm().item()
+    assert r <= 1.05e-6 * g["b_norm"], r / g["b_norm"]

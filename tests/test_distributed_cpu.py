@@ -122,3 +122,53 @@ def test_landing_offsets_match_peer_halo_order(world, kind):
             assert h0 >= 0
             assert np.array_equal(t.halo_cols[h0:h0 + sc], cols)
             so += int(sc)
+
+
+def _exchange_worker(rank, world, port, kind, mode, results):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "mlx-sparse_b200"), os.path.join(root, "tests")]
+    from mlx_sparse.distributed import OperandExchange
+    from oracle import oracle
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        (d, i, p), (n, _) = _make(kind)
+        x = wl.uniform_vector(n, 7)
+        B = wl.uniform_matrix(n, 3, 8)
+        ex = OperandExchange(d, i, p, n, rank, world, torch.device("cpu"), mode=mode)
+        s = ex.slab
+        xl = ex.exchange(torch.from_numpy(x[s.r0:s.r1].copy())).numpy().copy()
+        y_local = oracle.csr_matvec(s.data, ex.local_indices, s.indptr, xl, s.n_owned)
+        Bl = ex.exchange(torch.from_numpy(B[s.r0:s.r1].copy())).numpy()
+        Y_local = oracle.csr_matmul(s.data, ex.local_indices, s.indptr, Bl, s.n_owned)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (s.r0, y_local, Y_local, ex.mode))
+        if rank == 0:
+            y = np.zeros(n, np.float32)
+            Y = np.zeros((n, 3), np.float32)
+            for r0, yl, Yl, _ in gathered:
+                y[r0:r0 + yl.size] = yl
+                Y[r0:r0 + yl.size] = Yl
+            ok = (np.array_equal(y, oracle.csr_matvec(d, i, p, x, n))
+                  and np.array_equal(Y, oracle.csr_matmul(d, i, p, B, n))
+                  and all(g[3] == (mode if mode != "auto" else g[3]) for g in gathered))
+            results.put(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("mode", ["halo", "allgather", "auto"])
+@pytest.mark.parametrize("kind", ["poisson", "random"])
+def test_sharded_operand_exchange_reproduces_global_products(world, mode, kind):
+    """DistProduct's operand exchange (x and B rows sharded like A's rows):
+    after the exchange, each rank's local SpMV / SpMM with the renumbered
+    columns equals its rows of the global product, bit for bit."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.spawn(_exchange_worker, args=(world, _free_port(), kind, mode, q), nprocs=world, join=True)
+    assert q.get(timeout=60) is True

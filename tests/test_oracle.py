@@ -5,6 +5,8 @@ reproduces every known-answer case of the reference's tests for this path
 (tests/golden/reference_cases.json) and agrees with SciPy on seeded inputs.
 """
 
+import os
+
 import numpy as np
 import pytest
 import scipy.sparse as sp
@@ -152,7 +154,11 @@ def test_workload_generators_are_canonical():
             assert row.size == 0 or (row[0] >= 0 and row[-1] < shape[1])
 
 
-_HB = "/root/reference/tests/fixtures/suitesparse/HB"
+# The reference's SuiteSparse fixtures, read in place: MSX_REFERENCE_ROOT
+# names the mlx-sparse checkout (default: a `reference` folder beside this
+# repository).
+_HB = os.path.join(os.environ.get("MSX_REFERENCE_ROOT", os.path.join(os.path.dirname(os.path.dirname(
+    os.path.dirname(os.path.abspath(__file__)))), "reference")), "tests", "fixtures", "suitesparse", "HB")
 
 
 def _hb_matrices():
@@ -222,3 +228,20 @@ def test_oracle_pcg_on_bcsstk03():
     if info == 0:
         r = b.astype(np.float64) - A.astype(np.float64) @ x.astype(np.float64)
         assert np.linalg.norm(r) <= 1e-3 * np.linalg.norm(b)
+
+
+def test_pcg_poisson3d_fixture_reproduces(orc):
+    """The committed PCG fixture (tests/golden/pcg_poisson3d.json, which the
+    GPU tests read for the 256^3 BASELINE solve) is the oracle's result: the
+    64^3 entry is recomputed here (0.5 s) and must match exactly."""
+    import json
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "pcg_poisson3d.json")) as f:
+        g = json.load(f)["64"]
+    (d, i, p), (n, _) = wl.poisson3d(64)
+    b = orc.csr_matvec(d, i, p, wl.uniform_vector(n, 1), n)
+    x, info, res, its = orc.csr_pcg_jacobi(d, i, p, b, np.zeros(n, np.float32), np.full(n, 1.0 / 6.0, np.float32),
+                                           rtol=1e-6, atol=0.0, maxiter=2000)
+    assert (info, its) == (g["info"], g["iterations"])
+    assert res == pytest.approx(g["residual"], rel=1e-6)
+    assert x[:8].tolist() == g["x_head"]
