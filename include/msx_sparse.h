@@ -18,7 +18,10 @@
  *    thread-local message. MSX_ERR_INVALID maps to ValueError, MSX_ERR_TYPE to
  *    TypeError, MSX_ERR_OVERFLOW to OverflowError, the rest to RuntimeError.
  *  - Temporary device memory comes from the stream-ordered allocator
- *    (cudaMallocAsync on `stream`), so calls are re-entrant per stream.
+ *    (cudaMallocAsync on `stream`), so calls are re-entrant per stream. The
+ *    library sets the release threshold of the device's default memory pool
+ *    to unlimited (once per device), so freed scratch stays reserved for the
+ *    next call instead of being unmapped at every synchronisation.
  */
 #ifndef MSX_SPARSE_H
 #define MSX_SPARSE_H
@@ -126,6 +129,78 @@ MSX_API int msx_csr_matmul(int value_dtype, int index_dtype, const void *data,
                    int64_t n_cols, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* COO entry, transposition and the backward products.                      */
+/* ------------------------------------------------------------------------ */
+/* COO -> CSR. Replaces `coo_tocsr(data, row, col, n_rows, n_cols)`
+ * (src/bindings.cpp -> src/sparse/coo_tocsr/coo_tocsr.cpp:94-237,
+ * mlx_sparse/_coo.py:126-154). `row`/`col` share `index_dtype`; the outputs
+ * (caller-allocated) are out_data[nnz] (may be NULL: structure only),
+ * out_indices[nnz] (col's dtype), out_indptr[n_rows + 1] (row's dtype) and,
+ * optionally, out_perm[nnz] (int64: source position of every output entry,
+ * which is what the reference's coo_tocsr data VJP gathers through,
+ * coo_tocsr.cpp:237-300). sort_columns = 1 orders each row by column, then
+ * source position (the reference's coo_tocsr, duplicates kept); 0 keeps each
+ * row in source order (the summation order of the reference's coo_matmul,
+ * src/sparse/coo_matmul/coo_matmul.cpp). Coordinates outside the shape
+ * return MSX_ERR_INVALID. Synchronises `stream` once. */
+MSX_API int msx_coo_tocsr(int value_dtype, int index_dtype, const void *data,
+                          const void *row, const void *col, int64_t nnz,
+                          int64_t n_rows, int64_t n_cols, int sort_columns,
+                          void *out_data, void *out_indices, void *out_indptr,
+                          int64_t *out_perm, void *stream);
+
+/* CSR of A^T (n_cols x n_rows): row c lists column c's entries of A by
+ * ascending row (so the result has sorted indices). Replaces
+ * `csr_transpose` (src/sparse/csr_transpose). out_perm as msx_coo_tocsr.
+ * Synchronises `stream` once. */
+MSX_API int msx_csr_transpose(int value_dtype, int index_dtype, const void *data,
+                              const void *indices, const void *indptr,
+                              int64_t nnz, int64_t n_rows, int64_t n_cols,
+                              void *out_data, void *out_indices,
+                              void *out_indptr, int64_t *out_perm,
+                              void *stream);
+
+/* out = A^T @ x (x[n_rows] -> out[n_cols]) and out = A^T @ B
+ * (B[n_rows, rhs_cols] -> out[n_cols, rhs_cols]). Replace
+ * `csr_matvec_transpose` (src/sparse/csr_matvec_transpose/
+ * csr_matvec_transpose.cpp:76-97, the VJP of csr_matvec with respect to x,
+ * src/sparse/csr_matvec/csr_matvec.cpp:247-257) and `csr_matmul_transpose`
+ * (src/sparse/csr_matmul_transpose). Every output element sums its column's
+ * entries in row-major order, as the reference's serial loop does. The
+ * transposed structure is built in stream scratch on every call (the Python
+ * layer caches it per matrix and calls the plain products instead);
+ * synchronises `stream` once. */
+MSX_API int msx_csr_matvec_transpose(int value_dtype, int index_dtype,
+                                     const void *data, const void *indices,
+                                     const void *indptr, int64_t nnz,
+                                     const void *x, void *out, int64_t n_rows,
+                                     int64_t n_cols, void *stream);
+MSX_API int msx_csr_matmul_transpose(int value_dtype, int index_dtype,
+                                     const void *data, const void *indices,
+                                     const void *indptr, int64_t nnz,
+                                     const void *rhs, int64_t rhs_cols,
+                                     void *out, int64_t n_rows, int64_t n_cols,
+                                     void *stream);
+
+/* Cotangent of the stored values. matvec: out[p] = cot[row(p)] * x[col(p)];
+ * matmul: out[p] = sum_j cot[row(p), j] * B[col(p), j], j in order, fp32
+ * accumulation. Replace `csr_matvec_data_vjp` (src/sparse/
+ * csr_matvec_data_vjp) and `csr_matmul_data_vjp` (src/sparse/
+ * csr_matmul_data_vjp/csr_matmul_data_vjp.cpp:88-100). */
+MSX_API int msx_csr_matvec_data_vjp(int value_dtype, int index_dtype,
+                                    const void *indices, const void *indptr,
+                                    int64_t nnz, const void *x,
+                                    const void *cotangent, void *out,
+                                    int64_t n_rows, int64_t n_cols,
+                                    void *stream);
+MSX_API int msx_csr_matmul_data_vjp(int value_dtype, int index_dtype,
+                                    const void *indices, const void *indptr,
+                                    int64_t nnz, const void *rhs,
+                                    const void *cotangent, int64_t rhs_cols,
+                                    void *out, int64_t n_rows, int64_t n_cols,
+                                    void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* SpGEMM C = A @ B, canonical (sorted, duplicate-free, exact zeros pruned). */
 /* ------------------------------------------------------------------------ */
 /* Batched products with one matrix, replacing csr_batched_matvec
@@ -211,6 +286,55 @@ MSX_API int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *i
                        int64_t n_rows, int64_t n_cols, float rtol, float atol,
                        int32_t maxiter, int32_t *info, float *residual,
                        int32_t *iterations, void *stream);
+
+/* Chebyshev-preconditioned CG. Replaces `csr_pcg_chebyshev(data, indices,
+ * indptr, b, x0, m_data, m_indices, m_indptr, n_rows, n_cols, degree,
+ * lambda_min, lambda_max, rtol, atol, maxiter)` (mlx_sparse/_native.py:
+ * 1211-1260 -> src/preconditioners/pcg/chebyshev.cpp:124-313): Jacobi-PCG's
+ * recurrence and statuses with z = p_d(M) r, the first-kind Chebyshev
+ * semi-iteration of `degree` terms on the preconditioner matrix M
+ * (m_*, square n_rows, same index dtype) over [lambda_min, lambda_max].
+ * Single GPU; synchronises `stream` at the end. */
+MSX_API int msx_csr_pcg_chebyshev(int index_dtype, const float *data,
+                                  const void *indices, const void *indptr,
+                                  int64_t nnz, const float *b, const float *x0,
+                                  const float *m_data, const void *m_indices,
+                                  const void *m_indptr, int64_t m_nnz,
+                                  float *x_out, int64_t n_rows, int64_t n_cols,
+                                  int32_t degree, float lambda_min,
+                                  float lambda_max, float rtol, float atol,
+                                  int32_t maxiter, int32_t *info,
+                                  float *residual, int32_t *iterations,
+                                  void *stream);
+
+/* out = p_d(M) rhs for rhs of n x rhs_cols (row-major; 1 column = a vector).
+ * Replaces `csr_chebyshev_preconditioner_apply` (src/preconditioners/
+ * chebyshev/chebyshev.cpp:262-300). */
+MSX_API int msx_csr_chebyshev_apply(int index_dtype, const float *m_data,
+                                    const void *m_indices, const void *m_indptr,
+                                    int64_t m_nnz, int64_t n, const float *rhs,
+                                    int64_t rhs_cols, float *out,
+                                    int32_t degree, float lambda_min,
+                                    float lambda_max, void *stream);
+
+/* out[row, c] = inv_diag[row] * rhs[row, c]. Replaces
+ * `diagonal_preconditioner_apply` (src/preconditioners/diagonal/
+ * diagonal.cpp:60-88, 120-161). */
+MSX_API int msx_diagonal_preconditioner_apply(const float *inv_diag,
+                                              const float *rhs, int64_t n,
+                                              int64_t rhs_cols, float *out,
+                                              void *stream);
+
+/* Gershgorin bounds and the diagonal range of a square fp32 CSR matrix into
+ * host out4 = {lower, upper, diag_min, diag_max}: the Gershgorin part of
+ * `csr_chebyshev_spectral_bounds` (src/preconditioners/chebyshev/
+ * chebyshev.cpp:120-161). Non-finite values return MSX_ERR_INVALID.
+ * Synchronises `stream`. */
+MSX_API int msx_csr_gershgorin_bounds(int index_dtype, const float *data,
+                                      const void *indices, const void *indptr,
+                                      int64_t nnz, int64_t n_rows,
+                                      int64_t n_cols, float *out4,
+                                      void *stream);
 
 /* Main diagonal of a CSR matrix into out[min(n_rows, n_cols)], duplicate
  * entries summed in stored order (fp32 accumulation). Replaces the native

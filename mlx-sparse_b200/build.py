@@ -54,6 +54,10 @@ def _flags():
         "-fPIC",
         "-Xcompiler",
         "-fvisibility=hidden",
+        # host-side float arithmetic that restates the reference (solver
+        # coefficients) keeps one rounding per operation
+        "-Xcompiler",
+        "-ffp-contract=off",
         "--expt-relaxed-constexpr",
         "-DMSX_SM=100",
         "-I" + INCLUDE,

@@ -1,6 +1,7 @@
 // C-ABI entry points (include/msx_sparse.h). Argument checks follow the
 // reference front-ends (e.g. src/sparse/csr_matvec/csr_matvec.cpp:326-356) and
 // map C++ exception kinds onto msx_status codes.
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -211,6 +212,126 @@ int msx_csr_matmul(int value_dtype, int index_dtype, const void *data, const voi
   });
 }
 
+int msx_coo_tocsr(int value_dtype, int index_dtype, const void *data, const void *row, const void *col, int64_t nnz,
+                  int64_t n_rows, int64_t n_cols, int sort_columns, void *out_data, void *out_indices,
+                  void *out_indptr, int64_t *out_perm, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0, MSX_ERR_INVALID, "coo_tocsr shape dimensions must be non-negative.");
+    require(nnz >= 0, MSX_ERR_INVALID, "coo_tocsr nnz must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    if (index_dtype == MSX_I32 && nnz > INT32_MAX)
+      fail(MSX_ERR_OVERFLOW, "coo_tocsr nnz exceeds the int32 index capacity.");
+    check_ptr(row, nnz, "coo_tocsr row");
+    check_ptr(col, nnz, "coo_tocsr col");
+    check_ptr(out_indices, nnz, "coo_tocsr out_indices");
+    check_ptr(out_indptr, n_rows + 1, "coo_tocsr out_indptr");
+    if (out_data) check_ptr(data, nnz, "coo_tocsr data");
+    coo_tocsr_run(value_dtype, index_dtype, data, row, col, nnz, n_rows, n_cols, sort_columns != 0, out_data,
+                  out_indices, out_indptr, out_perm, as_stream(stream));
+  });
+}
+
+int msx_csr_transpose(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+                      int64_t nnz, int64_t n_rows, int64_t n_cols, void *out_data, void *out_indices,
+                      void *out_indptr, int64_t *out_perm, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0, MSX_ERR_INVALID, "csr_transpose shape dimensions must be non-negative.");
+    require(nnz >= 0, MSX_ERR_INVALID, "csr_transpose nnz must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(indices, nnz, "csr_transpose indices");
+    check_ptr(indptr, n_rows + 1, "csr_transpose indptr");
+    check_ptr(out_indices, nnz, "csr_transpose out_indices");
+    check_ptr(out_indptr, n_cols + 1, "csr_transpose out_indptr");
+    if (out_data) check_ptr(data, nnz, "csr_transpose data");
+    csr_transpose_run(value_dtype, index_dtype, data, indices, indptr, nnz, n_rows, n_cols, out_data, out_indices,
+                      out_indptr, out_perm, as_stream(stream));
+  });
+}
+
+// A^T @ rhs (k = 0: rhs is a vector). Builds the transposed CSR in stream
+// scratch, then runs the product kernels over it.
+static void transposed_product(int value_dtype, int index_dtype, const void *data, const void *indices,
+                               const void *indptr, int64_t nnz, const void *rhs, int64_t k, void *out,
+                               int64_t n_rows, int64_t n_cols, cudaStream_t s) {
+  if (n_cols == 0) return;
+  size_t vb = 0, ib = index_dtype == MSX_I64 ? 8 : 4;
+  dispatch_value(value_dtype, [&](auto v) { vb = sizeof(v); });
+  Scratch t_data(vb * (size_t)nnz, s), t_idx(ib * (size_t)nnz, s), t_ptr(ib * (size_t)(n_cols + 1), s);
+  csr_transpose_run(value_dtype, index_dtype, data, indices, indptr, nnz, n_rows, n_cols, t_data.ptr, t_idx.ptr,
+                    t_ptr.ptr, nullptr, s);
+  if (k == 0) {
+    const int64_t n_tiles = spmv_num_tiles(n_cols, nnz);
+    const size_t plan_bytes = spmv_plan_device_bytes(n_tiles);
+    Scratch scratch(plan_bytes + sizeof(float) * 2 * n_tiles, s);
+    char *base = scratch.as<char>();
+    spmv_build_plan(index_dtype, t_ptr.ptr, n_cols, nnz, base, n_tiles, s);
+    spmv_run(value_dtype, index_dtype, t_data.ptr, t_idx.ptr, t_ptr.ptr, rhs, out, n_cols, nnz, base, n_tiles, true,
+             reinterpret_cast<float *>(base + plan_bytes), s);
+  } else {
+    spmm_run(value_dtype, index_dtype, t_data.ptr, t_idx.ptr, t_ptr.ptr, rhs, k, out, n_cols, n_rows, nnz, s);
+  }
+}
+
+int msx_csr_matvec_transpose(int value_dtype, int index_dtype, const void *data, const void *indices,
+                             const void *indptr, int64_t nnz, const void *x, void *out, int64_t n_rows,
+                             int64_t n_cols, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0 && nnz >= 0, MSX_ERR_INVALID,
+            "csr_matvec_transpose sizes must be non-negative.");
+    check_ptr(data, nnz, "csr_matvec_transpose data");
+    check_ptr(indices, nnz, "csr_matvec_transpose indices");
+    check_ptr(indptr, n_rows + 1, "csr_matvec_transpose indptr");
+    check_ptr(x, nnz > 0 ? n_rows : 0, "csr_matvec_transpose x");
+    check_ptr(out, n_cols, "csr_matvec_transpose out");
+    transposed_product(value_dtype, index_dtype, data, indices, indptr, nnz, x, 0, out, n_rows, n_cols,
+                       as_stream(stream));
+  });
+}
+
+int msx_csr_matmul_transpose(int value_dtype, int index_dtype, const void *data, const void *indices,
+                             const void *indptr, int64_t nnz, const void *rhs, int64_t rhs_cols, void *out,
+                             int64_t n_rows, int64_t n_cols, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0 && nnz >= 0 && rhs_cols >= 0, MSX_ERR_INVALID,
+            "csr_matmul_transpose sizes must be non-negative.");
+    check_ptr(data, nnz, "csr_matmul_transpose data");
+    check_ptr(indices, nnz, "csr_matmul_transpose indices");
+    check_ptr(indptr, n_rows + 1, "csr_matmul_transpose indptr");
+    check_ptr(rhs, nnz > 0 ? n_rows * rhs_cols : 0, "csr_matmul_transpose rhs");
+    check_ptr(out, n_cols * rhs_cols, "csr_matmul_transpose out");
+    if (rhs_cols == 0) return;
+    transposed_product(value_dtype, index_dtype, data, indices, indptr, nnz, rhs, rhs_cols, out, n_rows, n_cols,
+                       as_stream(stream));
+  });
+}
+
+int msx_csr_matmul_data_vjp(int value_dtype, int index_dtype, const void *indices, const void *indptr, int64_t nnz,
+                            const void *rhs, const void *cotangent, int64_t rhs_cols, void *out, int64_t n_rows,
+                            int64_t n_cols, void *stream) {
+  return guarded([&] {
+    require(n_rows >= 0 && n_cols >= 0 && nnz >= 0 && rhs_cols >= 0, MSX_ERR_INVALID,
+            "csr_matmul_data_vjp sizes must be non-negative.");
+    dispatch_value(value_dtype, [](auto) {});
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(indices, nnz, "csr_matmul_data_vjp indices");
+    check_ptr(indptr, n_rows + 1, "csr_matmul_data_vjp indptr");
+    check_ptr(rhs, nnz > 0 ? n_cols * rhs_cols : 0, "csr_matmul_data_vjp rhs");
+    check_ptr(cotangent, nnz > 0 ? n_rows * rhs_cols : 0, "csr_matmul_data_vjp cotangent");
+    check_ptr(out, nnz, "csr_matmul_data_vjp out");
+    csr_data_vjp_run(value_dtype, index_dtype, indices, indptr, nnz, n_rows, rhs, cotangent, rhs_cols, out,
+                     as_stream(stream));
+  });
+}
+
+int msx_csr_matvec_data_vjp(int value_dtype, int index_dtype, const void *indices, const void *indptr, int64_t nnz,
+                            const void *x, const void *cotangent, void *out, int64_t n_rows, int64_t n_cols,
+                            void *stream) {
+  return msx_csr_matmul_data_vjp(value_dtype, index_dtype, indices, indptr, nnz, x, cotangent, 1, out, n_rows, n_cols,
+                                 stream);
+}
+
 int msx_csr_batched_matvec(int value_dtype, int index_dtype, const void *data, const void *indices,
                            const void *indptr, int64_t nnz, const void *rhs, int64_t batch, void *out, int64_t n_rows,
                            int64_t n_cols, void *stream) {
@@ -354,6 +475,87 @@ int msx_csr_pcg_jacobi(int index_dtype, const float *data, const void *indices, 
     *info = r.info;
     *residual = r.residual;
     *iterations = r.iterations;
+  });
+}
+
+static void check_chebyshev(const char *op, int degree, float lambda_min, float lambda_max) {
+  // validate_chebyshev_interval, src/preconditioners/pcg/chebyshev.cpp:66-78
+  if (degree <= 0) fail(MSX_ERR_INVALID, std::string(op) + " degree must be positive.");
+  if (!std::isfinite(lambda_min) || !std::isfinite(lambda_max) || lambda_min <= 0.0f || lambda_max <= lambda_min)
+    fail(MSX_ERR_INVALID, std::string(op) + " requires finite bounds satisfying 0 < lambda_min < lambda_max.");
+}
+
+int msx_csr_pcg_chebyshev(int index_dtype, const float *data, const void *indices, const void *indptr, int64_t nnz,
+                          const float *b, const float *x0, const float *m_data, const void *m_indices,
+                          const void *m_indptr, int64_t m_nnz, float *x_out, int64_t n_rows, int64_t n_cols,
+                          int32_t degree, float lambda_min, float lambda_max, float rtol, float atol,
+                          int32_t maxiter, int32_t *info, float *residual, int32_t *iterations, void *stream) {
+  return guarded([&] {
+    check_solver_args("csr_pcg_chebyshev", index_dtype, data, indices, indptr, nnz, b, x0, x_out, n_rows, n_cols,
+                      maxiter, info, residual, iterations);
+    check_chebyshev("csr_pcg_chebyshev", degree, lambda_min, lambda_max);
+    require(m_nnz >= 0, MSX_ERR_INVALID, "csr_pcg_chebyshev preconditioner nnz must be non-negative.");
+    check_ptr(m_data, m_nnz, "csr_pcg_chebyshev m_data");
+    check_ptr(m_indices, m_nnz, "csr_pcg_chebyshev m_indices");
+    check_ptr(m_indptr, n_rows + 1, "csr_pcg_chebyshev m_indptr");
+    CgProblem prob{index_dtype, data, indices, indptr, nnz, n_rows, n_cols, b, x0, nullptr, x_out, rtol, atol,
+                   maxiter};
+    prob.m_data = m_data;
+    prob.m_indices = m_indices;
+    prob.m_indptr = m_indptr;
+    prob.m_nnz = m_nnz;
+    prob.degree = degree;
+    prob.lambda_min = lambda_min;
+    prob.lambda_max = lambda_max;
+    CgResult r = cg_solve(prob, as_stream(stream));
+    *info = r.info;
+    *residual = r.residual;
+    *iterations = r.iterations;
+  });
+}
+
+int msx_csr_chebyshev_apply(int index_dtype, const float *m_data, const void *m_indices, const void *m_indptr,
+                            int64_t m_nnz, int64_t n, const float *rhs, int64_t rhs_cols, float *out,
+                            int32_t degree, float lambda_min, float lambda_max, void *stream) {
+  return guarded([&] {
+    require(n > 0 && m_nnz >= 0, MSX_ERR_INVALID,
+            "csr_chebyshev_preconditioner_apply requires a non-empty square matrix.");
+    require(rhs_cols > 0, MSX_ERR_INVALID, "csr_chebyshev_preconditioner_apply rhs must have at least one column.");
+    dispatch_index(index_dtype, [](auto) {});
+    check_chebyshev("csr_chebyshev_preconditioner_apply", degree, lambda_min, lambda_max);
+    check_ptr(m_data, m_nnz, "csr_chebyshev_preconditioner_apply data");
+    check_ptr(m_indices, m_nnz, "csr_chebyshev_preconditioner_apply indices");
+    check_ptr(m_indptr, n + 1, "csr_chebyshev_preconditioner_apply indptr");
+    check_ptr(rhs, n * rhs_cols, "csr_chebyshev_preconditioner_apply rhs");
+    check_ptr(out, n * rhs_cols, "csr_chebyshev_preconditioner_apply out");
+    chebyshev_apply_run(index_dtype, m_data, m_indices, m_indptr, m_nnz, n, rhs, rhs_cols, out, degree, lambda_min,
+                        lambda_max, as_stream(stream));
+  });
+}
+
+int msx_diagonal_preconditioner_apply(const float *inv_diag, const float *rhs, int64_t n, int64_t rhs_cols,
+                                      float *out, void *stream) {
+  return guarded([&] {
+    require(n >= 0, MSX_ERR_INVALID, "diagonal_preconditioner_apply sizes must be non-negative.");
+    require(rhs_cols > 0, MSX_ERR_INVALID, "diagonal_preconditioner_apply rhs must have at least one column.");
+    check_ptr(inv_diag, n, "diagonal_preconditioner_apply inv_diag");
+    check_ptr(rhs, n * rhs_cols, "diagonal_preconditioner_apply rhs");
+    check_ptr(out, n * rhs_cols, "diagonal_preconditioner_apply out");
+    diagonal_apply_run(inv_diag, rhs, n, rhs_cols, out, as_stream(stream));
+  });
+}
+
+int msx_csr_gershgorin_bounds(int index_dtype, const float *data, const void *indices, const void *indptr,
+                              int64_t nnz, int64_t n_rows, int64_t n_cols, float *out4, void *stream) {
+  return guarded([&] {
+    require(n_rows > 0 && n_rows == n_cols, MSX_ERR_INVALID,
+            "csr_chebyshev_spectral_bounds requires a non-empty square matrix.");
+    dispatch_index(index_dtype, [](auto) {});
+    check_ptr(data, nnz, "csr_chebyshev_spectral_bounds data");
+    check_ptr(indices, nnz, "csr_chebyshev_spectral_bounds indices");
+    check_ptr(indptr, n_rows + 1, "csr_chebyshev_spectral_bounds indptr");
+    require(out4 != nullptr, MSX_ERR_INVALID, "csr_chebyshev_spectral_bounds out must not be null.");
+    gershgorin_run(index_dtype, data, indices, indptr, n_rows, out4, as_stream(stream));
   });
 }
 

@@ -52,7 +52,7 @@ namespace {
 
 constexpr int kThreads = 256;
 
-enum Kind { kCG = 0, kPCG = 1 };
+enum Kind { kCG = 0, kPCG = 1, kCheb = 2 };
 
 __device__ __forceinline__ bool finite_f(float v) { return isfinite(v); }
 __device__ __forceinline__ bool finite_d(double v) { return isfinite(v); }
@@ -374,6 +374,7 @@ __device__ void decide_update(CgState *st, int kind) {
       st->status = 0;
       return;
     }
+    if (kind == kCheb) return;  // r.z needs z = p_d(M) r first (decide_rho)
     const float rho_new = (float)st->red[1];
     if (!finite_f(rho_new) || rho_new <= 0.0f) {
       st->status = -2;
@@ -390,6 +391,25 @@ __device__ void decide_update(CgState *st, int kind) {
     if (it >= st->maxiter) st->status = st->maxiter;
     st->it = it + 1;
   }
+}
+
+// Chebyshev PCG after z = p_d(M) r: red = {r.r, r.z, -, -}
+// (chebyshev.cpp:283-297, the tail of Jacobi PCG's update).
+__device__ void decide_rho(CgState *st) {
+  const float rho_new = (float)st->red[1];
+  if (!finite_f(rho_new) || rho_new <= 0.0f) {
+    st->status = -2;
+    return;
+  }
+  const float beta = __fdiv_rn(rho_new, st->rho);
+  if (!finite_f(beta)) {
+    st->status = -3;
+    return;
+  }
+  st->beta_f = beta;
+  st->rho = rho_new;
+  if (st->it >= st->maxiter) st->status = st->maxiter;
+  st->it = st->it + 1;
 }
 
 // Plain CG after the p update: red = {nonfinite, -, -, -}.
@@ -420,6 +440,9 @@ init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, 
     if (kind == kCG) {
       p[i] = ri;
       if (!(finite_f(ri) && finite_f(ap[i]) && finite_f(bi) && finite_f(x[i]))) v[3] += 1.0;
+    } else if (kind == kCheb) {
+      // z = p_d(M) r and r.z follow once r is complete (chebyshev.cpp:207-222)
+      if (!(finite_f(ri) && finite_f(bi) && finite_f(x[i]))) v[3] += 1.0;
     } else {
       const float inv = inv_diag[i];
       const float zi = __fmul_rn(inv, ri);
@@ -429,7 +452,14 @@ init_kernel(int kind, const float *__restrict__ b, const float *__restrict__ x, 
       if (!(finite_f(ri) && finite_f(zi) && finite_f(inv))) v[3] += 1.0;
     }
   }
-  reduce_and_decide(v, partials, st, L, decide, [&] { decide_init(st, kind, rtol, atol); });
+  reduce_and_decide(v, partials, st, L, decide, [&] {
+    if (kind == kCheb) {
+      st->bb_init = st->red[0];
+      st->bad_init = st->red[3];
+    } else {
+      decide_init(st, kind, rtol, atol);
+    }
+  });
 }
 
 // Fuses p.Ap, p.p, Ap.Ap (and the non-finite count) into the SpMV row
@@ -504,6 +534,17 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
       x[i] = xf;
       r[i] = rf;
       v[0] += (double)rf * (double)rf;
+    }
+  } else if (kind == kCheb) {
+    const float alpha = st->alpha_f;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+      const float xo = __fadd_rn(x[i], __fmul_rn(alpha, p[i]));
+      const float ro = __fsub_rn(r[i], __fmul_rn(alpha, ap[i]));
+      x[i] = xo;
+      r[i] = ro;
+      v[0] += (double)ro * (double)ro;
+      if (!(finite_f(xo) && finite_f(ro))) v[2] += 1.0;
     }
   } else {
     const float alpha = st->alpha_f;
@@ -612,6 +653,63 @@ pupdate_kernel(int kind, const float *__restrict__ r, const float *__restrict__ 
   for (int64_t i = done + first; i < n; i += stride) p_next[i] = __fadd_rn(z[i], __fmul_rn(beta, p_cur[i]));
 }
 
+// r.r and r.z after the Chebyshev apply; at the start (`first`) also p = z
+// and the initial decision, in the solve loop the rho / beta decision.
+__global__ void __launch_bounds__(kThreads)
+cheb_dots_kernel(const float *__restrict__ r, const float *__restrict__ z, float *__restrict__ p, int64_t n,
+                 double *partials, CgState *st, bool first, float rtol, float atol) {
+  if (st->status != kStatusRunning) return;
+  double v[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float rv = r[i], zv = z[i];
+    v[0] += (double)rv * (double)rv;
+    v[1] += (double)rv * (double)zv;
+    if (first) p[i] = zv;
+  }
+  reduce_and_decide(v, partials, st, nullptr, true, [&] {
+    if (first) {
+      const double rr = st->red[0], rz = st->red[1];
+      st->red[0] = st->bb_init;
+      st->red[1] = rr;
+      st->red[2] = rz;
+      st->red[3] = st->bad_init;
+      decide_init(st, kPCG, rtol, atol);
+    } else {
+      decide_rho(st);
+    }
+  });
+}
+
+// Chebyshev semi-iteration (chebyshev.cpp:84-122): out = scale * rhs, then
+// per step next = (1 - w) prev + w out + w scale (rhs - M out). The kernels
+// return at once when a solve has stopped (st may be null: standalone).
+__global__ void cheb_first_kernel(const CgState *st, const float *__restrict__ rhs, float *__restrict__ out,
+                                  float *__restrict__ prev, int64_t n, float scale) {
+  if (st && st->status != kStatusRunning) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    out[i] = __fmul_rn(scale, rhs[i]);
+    if (prev) prev[i] = 0.0f;
+  }
+}
+
+__global__ void cheb_step_kernel(const CgState *st, const float *__restrict__ rhs, const float *__restrict__ ax,
+                                 const float *__restrict__ prev, const float *__restrict__ out,
+                                 float *__restrict__ next, int64_t n, float one_minus_omega, float omega,
+                                 float omega_scale) {
+  if (st && st->status != kStatusRunning) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float rv = __fsub_rn(rhs[i], ax[i]);
+    next[i] = __fadd_rn(__fadd_rn(__fmul_rn(one_minus_omega, prev[i]), __fmul_rn(omega, out[i])),
+                        __fmul_rn(omega_scale, rv));
+  }
+}
+
+// SpMV epilogue that only stores y and skips the launch once the solve stopped.
+struct StatusSkipEpilogue : NoEpilogue {
+  const CgState *st;
+  __device__ __forceinline__ bool skip() const { return st && st->status != kStatusRunning; }
+};
+
 // Multi-GPU: the reductions leave local sums in st->red; after the NCCL
 // all-reduce one thread makes the decision every rank makes identically.
 __global__ void decide_kernel(CgState *st, int which, int kind, float rtol, float atol) {
@@ -700,6 +798,14 @@ struct CgEngine {
   int batch = 4;
   bool pdl = false;          // programmatic dependent launch inside the iteration graph (MSX_CG_PDL=1)
   int *status_host = nullptr;
+  // Chebyshev preconditioner: plan of M, its chunk carry, the three
+  // semi-iteration buffers and the host-computed step coefficients
+  BinnedPlan plan_m;
+  void *plan_m_mem = nullptr;
+  float *carry_m = nullptr;
+  float *cheb[3] = {};
+  float cheb_scale = 0.f;
+  std::vector<float> cheb_coef;  // per step: 1 - omega, omega, omega * scale
 };
 
 namespace {
@@ -774,6 +880,34 @@ void engine_reduce_decide_nccl(CgEngine *e, int which, float rtol, float atol, c
 #endif
 }
 
+// z = p_d(M) r into e->z (chebyshev.cpp:84-122). The buffer that ends up
+// holding the result depends only on the degree, so e->z is fixed at setup.
+void engine_cheb_apply(CgEngine *e, cudaStream_t q) {
+  const CgEngineConfig &c = e->cfg;
+  const int g = elementwise_grid(e->n);
+  float *out = e->cheb[0], *prev = e->cheb[1], *next = e->cheb[2];
+  cheb_first_kernel<<<g, kThreads, 0, q>>>(e->st, e->r, out, c.degree > 1 ? prev : nullptr, e->n, e->cheb_scale);
+  MSX_CHECK_LAUNCH();
+  for (int it = 1; it < c.degree; ++it) {
+    dispatch_index(c.index_dtype, [&](auto ityp) {
+      using I = decltype(ityp);
+      StatusSkipEpilogue epi{};
+      epi.st = e->st;
+      launch_spmv_binned<float, I, StatusSkipEpilogue>(e->plan_m, c.m_data, static_cast<const I *>(c.m_indices),
+                                                       static_cast<const I *>(c.m_indptr), out, e->ap, e->carry_m,
+                                                       epi, q);
+    });
+    launch_spmv_long_fixup<float>(e->plan_m, e->carry_m, e->ap, q);
+    const float *k = &e->cheb_coef[3 * (it - 1)];
+    cheb_step_kernel<<<g, kThreads, 0, q>>>(e->st, e->r, e->ap, prev, out, next, e->n, k[0], k[1], k[2]);
+    MSX_CHECK_LAUNCH();
+    float *t = prev;
+    prev = out;
+    out = next;
+    next = t;
+  }
+}
+
 // One iteration reading direction buffer `par` and writing `par ^ 1` (the
 // same buffer unless P2P). Single GPU and P2P: three kernels, the scalar
 // all-reduce and the halo exchange fused into them.
@@ -809,6 +943,11 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   launch(update_kernel, dim3(e->red_grid), dim3(kThreads), 0, q, pdl, kind, e->x, e->r, e->z, pc, e->ap, e->inv, e->n,
          e->partials, e->st, decide, link_of(e));
   engine_reduce_decide_nccl(e, 2, 0.f, 0.f, q);
+  if (kind == kCheb) {
+    engine_cheb_apply(e, q);
+    cheb_dots_kernel<<<e->red_grid, kThreads, 0, q>>>(e->r, e->z, nullptr, e->n, e->partials, e->st, false, 0.f, 0.f);
+    MSX_CHECK_LAUNCH();
+  }
   launch(pupdate_kernel, dim3(e->red_grid + (p2p(e) ? e->push_grid : 0)), dim3(kThreads), 0, q, pdl, kind, e->r, e->z,
          pc, pn, e->n, e->partials, e->st, decide, link_of(e), push_of(e));
   if (kind == kCG) engine_reduce_decide_nccl(e, 3, 0.f, 0.f, q);
@@ -839,7 +978,9 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   std::unique_ptr<CgEngine, void (*)(CgEngine *)> e(new CgEngine(), cg_engine_destroy);
   CgEngine *E = e.get();
   E->cfg = cfg;
-  E->kind = cfg.preconditioned ? kPCG : kCG;
+  E->kind = cfg.m_data ? kCheb : (cfg.preconditioned ? kPCG : kCG);
+  if (E->kind == kCheb && cfg.comm != kCommNone)
+    fail(MSX_ERR_INVALID, "Chebyshev-preconditioned CG runs on one GPU.");
   E->n = cfg.n;
   E->n_cols = cfg.n + cfg.n_halo;
   MSX_CUDA(cudaGetDevice(&E->device));
@@ -855,6 +996,31 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
                     },
                     E->plan);
   E->fused = E->plan.n_long == 0;
+  if (E->kind == kCheb) {
+    build_binned_plan(cfg.index_dtype, cfg.m_indptr, E->n, cfg.m_nnz, s,
+                      [&](size_t bytes) -> void * {
+                        MSX_CUDA(cudaMalloc(&E->plan_m_mem, bytes));
+                        return E->plan_m_mem;
+                      },
+                      E->plan_m);
+    // step coefficients in the reference's float arithmetic (chebyshev.cpp:89-114)
+    const float lmin = cfg.lambda_min, lmax = cfg.lambda_max;
+    const float scale = 2.0f / (lmax + lmin);
+    const float alpha = 1.0f - scale * lmin;
+    const float mu = 1.0f / alpha;
+    const float omega_prod = 2.0f / alpha;
+    float c_prev = 1.0f, c_cur = mu;
+    E->cheb_scale = scale;
+    for (int it = 1; it < cfg.degree; ++it) {
+      const float c_next = 2.0f * mu * c_cur - c_prev;
+      const float omega = omega_prod * c_cur / c_next;
+      E->cheb_coef.push_back(1.0f - omega);
+      E->cheb_coef.push_back(omega);
+      E->cheb_coef.push_back(omega * scale);
+      c_prev = c_cur;
+      c_cur = c_next;
+    }
+  }
   E->red_grid = elementwise_grid(E->n);
   int64_t spmv_grid_n = 0;
   dispatch_index(cfg.index_dtype, [&](auto ityp) {
@@ -873,7 +1039,8 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   size_t bytes = 0;
   auto sz = [](size_t b) { return (b + 255) & ~size_t(255); };
   bytes += sz(sizeof(CgState)) + sz(sizeof(CommState)) + sz(sizeof(double) * 4 * max_grid) +
-           sz(sizeof(float) * std::max<int64_t>(E->plan.n_chunks, 1)) + 6 * sz(sizeof(float) * vec) +
+           sz(sizeof(float) * std::max<int64_t>(E->plan.n_chunks, 1)) +
+           sz(sizeof(float) * std::max<int64_t>(E->plan_m.n_chunks, 1)) + 9 * sz(sizeof(float) * vec) +
            sz(sizeof(float) * std::max<int64_t>(E->n_send, 1)) + sz(sizeof(P2pLink)) + sz(sizeof(PushPlan));
   MSX_CUDA(cudaMalloc(&E->mem, bytes));
   MSX_CUDA(cudaMemsetAsync(E->mem, 0, bytes, s));
@@ -882,6 +1049,8 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   E->cs = bump<CommState>(cur, 1);
   E->partials = bump<double>(cur, 4 * max_grid);
   E->carry = bump<float>(cur, std::max<int64_t>(E->plan.n_chunks, 1));
+  E->carry_m = bump<float>(cur, std::max<int64_t>(E->plan_m.n_chunks, 1));
+  for (float *&c : E->cheb) c = bump<float>(cur, vec);
   E->r = bump<float>(cur, vec);
   E->z = bump<float>(cur, vec);
   E->ap = bump<float>(cur, vec);
@@ -907,7 +1076,15 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
     MSX_CUDA(cudaMalloc(&E->halo_words, hb));
     MSX_CUDA(cudaMemsetAsync(E->halo_words, 0, hb, s));  // flag 0: no round (rounds start at 1)
   }
-  if (!cfg.preconditioned) E->z = nullptr, E->inv = nullptr;
+  if (E->kind == kCheb) {
+    // the semi-iteration rotates (out, prev, next) once per step
+    const int d = std::max(cfg.degree, 1);
+    const int final_slot[3] = {0, 2, 1};  // out after (d - 1) rotations
+    E->z = E->cheb[final_slot[(d - 1) % 3]];
+    E->inv = nullptr;
+  } else if (!cfg.preconditioned) {
+    E->z = nullptr, E->inv = nullptr;
+  }
   MSX_CUDA(cudaMallocHost(&E->status_host, sizeof(int)));
   E->link.world = 1;
   E->link.rank = 0;
@@ -945,6 +1122,7 @@ void cg_engine_destroy(CgEngine *e) {
   if (e->mbox) cudaFree(e->mbox);
   if (e->mem) cudaFree(e->mem);
   if (e->plan_mem) cudaFree(e->plan_mem);
+  if (e->plan_m_mem) cudaFree(e->plan_m_mem);
   if (e->ev) cudaEventDestroy(e->ev);
   if (e->s) cudaStreamDestroy(e->s);
   if (cur != e->device) cudaSetDevice(cur);
@@ -1041,6 +1219,11 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
                                                e->partials, e->st, rtol, atol, decide, link_of(e));
   MSX_CHECK_LAUNCH();
   engine_reduce_decide_nccl(e, 0, rtol, atol, s);
+  if (e->kind == kCheb) {  // z0 = p_d(M) r0, p0 = z0, then the initial decision
+    engine_cheb_apply(e, s);
+    cheb_dots_kernel<<<e->red_grid, kThreads, 0, s>>>(e->r, e->z, e->p[0], n, e->partials, e->st, true, rtol, atol);
+    MSX_CHECK_LAUNCH();
+  }
   if (p2p(e)) engine_push(e, e->p[0], 1, s);  // read by iteration 1
   CgState host{};
   MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
@@ -1095,6 +1278,13 @@ CgResult cg_solve(const CgProblem &prob, cudaStream_t user_stream) {
   cfg.n = prob.n;
   cfg.n_halo = prob.n_cols - prob.n;
   cfg.preconditioned = prob.inv_diag != nullptr;
+  cfg.m_data = prob.m_data;
+  cfg.m_indices = prob.m_indices;
+  cfg.m_indptr = prob.m_indptr;
+  cfg.m_nnz = prob.m_nnz;
+  cfg.degree = prob.degree;
+  cfg.lambda_min = prob.lambda_min;
+  cfg.lambda_max = prob.lambda_max;
   cfg.comm = kCommNone;
   cfg.rank = 0;
   cfg.world = 1;

@@ -27,6 +27,8 @@ struct CgState {
   unsigned int counter;  // last-block-done counter of the reductions
   unsigned int round_base;  // peer memory: flag of this solve's halo round 0
   int pad[2];
+  double bb_init;     // Chebyshev PCG: b.b and the non-finite count of the
+  double bad_init;    // initial residual, kept until r.z is known
 };
 
 constexpr int kMaxRanks = 8;  // one node
@@ -92,6 +94,13 @@ struct CgProblem {
   float rtol, atol;
   int maxiter;
   const CgDist *dist = nullptr;  // null: single GPU (NCCL when set)
+  // Chebyshev preconditioner (see CgEngineConfig); m_data null: none
+  const float *m_data = nullptr;
+  const void *m_indices = nullptr;
+  const void *m_indptr = nullptr;
+  int64_t m_nnz = 0;
+  int degree = 0;
+  float lambda_min = 0.f, lambda_max = 0.f;
 };
 
 struct CgResult {
@@ -123,6 +132,15 @@ struct CgEngineConfig {
   const int64_t *recv_counts;
   const int *send_idx;             // device
   const int64_t *peer_dst_offset;  // host, P2P: where this rank's entries land in each peer's p
+  // Chebyshev-preconditioned CG (single GPU): the preconditioner matrix M
+  // (same index dtype, square, n rows) and the polynomial's degree and
+  // spectral interval. m_data == nullptr: no Chebyshev preconditioner.
+  const float *m_data = nullptr;
+  const void *m_indices = nullptr;
+  const void *m_indptr = nullptr;
+  int64_t m_nnz = 0;
+  int degree = 0;
+  float lambda_min = 0.f, lambda_max = 0.f;
 };
 CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t stream);
 void cg_engine_destroy(CgEngine *e);
@@ -136,5 +154,20 @@ CgResult cg_engine_solve(CgEngine *e, const float *b, const float *x0, const flo
 
 // Single-GPU solve on `stream`; synchronises the stream at the end.
 CgResult cg_solve(const CgProblem &prob, cudaStream_t stream);
+
+// Chebyshev semi-iteration z = p_d(M) rhs for rhs of n x k (row-major), the
+// reference's chebyshev_apply (src/preconditioners/chebyshev/
+// chebyshev.cpp:262-300): degree - 1 products with M and fused vector
+// updates. Enqueued on `stream`.
+void chebyshev_apply_run(int index_dtype, const float *m_data, const void *m_indices, const void *m_indptr,
+                         int64_t m_nnz, int64_t n, const float *rhs, int64_t k, float *out, int degree,
+                         float lambda_min, float lambda_max, cudaStream_t stream);
+// out = inv_diag[row] * rhs (n x k), diagonal_preconditioner_apply.
+void diagonal_apply_run(const float *inv_diag, const float *rhs, int64_t n, int64_t k, float *out,
+                        cudaStream_t stream);
+// Gershgorin bounds and diagonal range {lower, upper, diag_min, diag_max}
+// (host); MSX_ERR_INVALID for a non-finite value. Synchronises `stream`.
+void gershgorin_run(int index_dtype, const float *data, const void *indices, const void *indptr, int64_t n_rows,
+                    float *out4, cudaStream_t stream);
 
 }  // namespace msx

@@ -84,13 +84,33 @@ template <typename Fn> int guarded(Fn &&fn) {
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Keeps memory freed into the current device's default stream-ordered pool
+// reserved (release threshold = unlimited) instead of returning it to the
+// driver at every synchronisation. Without this, the first scratch allocation
+// after a host sync maps fresh memory, which stalls the calling thread for
+// milliseconds while the GPU idles. Process-local; done once per device.
+inline void keep_pool_memory() {
+  static thread_local unsigned long long done = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || (done >> dev & 1ull)) return;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t threshold = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+  }
+  done |= 1ull << dev;
+}
+
 // Stream-ordered scratch: freed on the same stream when the guard goes out of
 // scope, so the memory is reusable by later work on that stream only.
 struct Scratch {
   void *ptr = nullptr;
   cudaStream_t stream = nullptr;
   Scratch(size_t bytes, cudaStream_t s) : stream(s) {
-    if (bytes) MSX_CUDA(cudaMallocAsync(&ptr, bytes, s));
+    if (bytes) {
+      keep_pool_memory();
+      MSX_CUDA(cudaMallocAsync(&ptr, bytes, s));
+    }
   }
   ~Scratch() {
     if (ptr) cudaFreeAsync(ptr, stream);

@@ -23,4 +23,19 @@ void csr_batched_matmul_run(int value_dtype, int index_dtype, const void *data, 
 void csr_diagonal_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
                       int64_t n_diag, void *out, cudaStream_t stream);
 
+// COO -> CSR (by_col: rows sorted by (column, source position) as the
+// reference's coo_tocsr; else by source position only). out_data may be null
+// (structure only); out_perm (int64[nnz], the source position of every output
+// entry) may be null. Synchronises `s` once (coordinate check).
+void coo_tocsr_run(int value_dtype, int index_dtype, const void *data, const void *row, const void *col, int64_t nnz,
+                   int64_t n_rows, int64_t n_cols, bool by_col, void *out_data, void *out_indices, void *out_indptr,
+                   int64_t *out_perm, cudaStream_t s);
+// CSR of A^T: row c lists A's entries of column c by ascending row.
+void csr_transpose_run(int value_dtype, int index_dtype, const void *data, const void *indices, const void *indptr,
+                       int64_t nnz, int64_t n_rows, int64_t n_cols, void *out_data, void *out_indices,
+                       void *out_indptr, int64_t *out_perm, cudaStream_t s);
+// out[p] = sum_j cot[row(p), j] * rhs[col(p), j], j in order (k = 1: matvec).
+void csr_data_vjp_run(int value_dtype, int index_dtype, const void *indices, const void *indptr, int64_t nnz,
+                      int64_t n_rows, const void *rhs, const void *cot, int64_t k, void *out, cudaStream_t s);
+
 }  // namespace msx

@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "scan.cuh"
 
 namespace msx {
 
@@ -316,72 +317,6 @@ spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_
   }
 }
 
-// ---- scan of row counts into indptr ----------------------------------------------
-constexpr int kScanThreads = 1024;
-
-__device__ __forceinline__ int64_t block_inclusive_scan(int64_t v, int64_t *smem) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int64_t o = __shfl_up_sync(0xffffffffu, v, off);
-    if (lane >= off) v += o;
-  }
-  if (lane == 31) smem[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int64_t w = lane < (kScanThreads / 32) ? smem[lane] : 0;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int64_t o = __shfl_up_sync(0xffffffffu, w, off);
-      if (lane >= off) w += o;
-    }
-    smem[lane] = w;
-  }
-  __syncthreads();
-  const int64_t add = warp > 0 ? smem[warp - 1] : 0;
-  __syncthreads();
-  return v + add;
-}
-
-__global__ void __launch_bounds__(kScanThreads)
-scan_block_sums(const int64_t *__restrict__ in, int64_t m, int64_t *__restrict__ sums) {
-  __shared__ int64_t smem[32];
-  const int64_t i = blockIdx.x * (int64_t)kScanThreads + threadIdx.x;
-  const int64_t v = i < m ? in[i] : 0;
-  const int64_t inc = block_inclusive_scan(v, smem);
-  if (threadIdx.x == kScanThreads - 1) sums[blockIdx.x] = inc;
-}
-
-__global__ void __launch_bounds__(kScanThreads)
-scan_sums_serial(int64_t *__restrict__ sums, int64_t nb, int64_t *__restrict__ total) {
-  __shared__ int64_t smem[32];
-  __shared__ int64_t chunk_total;
-  int64_t carry = 0;
-  for (int64_t base = 0; base < nb; base += kScanThreads) {
-    const int64_t i = base + threadIdx.x;
-    const int64_t v = i < nb ? sums[i] : 0;
-    const int64_t inc = block_inclusive_scan(v, smem);
-    if (i < nb) sums[i] = carry + inc - v;  // exclusive offsets of the blocks
-    if (threadIdx.x == kScanThreads - 1) chunk_total = inc;
-    __syncthreads();
-    carry += chunk_total;
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *total = carry;
-}
-
-template <typename OutI>
-__global__ void __launch_bounds__(kScanThreads)
-scan_write_indptr(const int64_t *__restrict__ in, int64_t m, const int64_t *__restrict__ sums,
-                  OutI *__restrict__ indptr) {
-  __shared__ int64_t smem[32];
-  const int64_t i = blockIdx.x * (int64_t)kScanThreads + threadIdx.x;
-  const int64_t v = i < m ? in[i] : 0;
-  const int64_t inc = block_inclusive_scan(v, smem) + sums[blockIdx.x];
-  if (i < m) indptr[i + 1] = (OutI)inc;
-  if (i == 0) indptr[0] = 0;
-}
-
 struct Bins {
   int counts[3];
 };
@@ -484,10 +419,7 @@ void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *r
   }
   if (write) return;
 
-  scan_block_sums<<<(unsigned)nb, kScanThreads, 0, s>>>(row_nnz, m, sums);
-  scan_sums_serial<<<1, kScanThreads, 0, s>>>(sums, nb, sums + nb);
-  scan_write_indptr<OutI><<<(unsigned)nb, kScanThreads, 0, s>>>(row_nnz, m, sums, out_indptr);
-  MSX_CHECK_LAUNCH();
+  scan_counts_to_indptr<OutI>(row_nnz, m, out_indptr, sums, s);
   int64_t total = 0;
   MSX_CUDA(cudaMemcpyAsync(&total, sums + nb, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));

@@ -10,21 +10,42 @@ place of MLX arrays. Every product runs in the hand-written CUDA library
 from mlx_sparse import linalg
 from mlx_sparse._coo import COOArray, coo_array
 from mlx_sparse._csr import CSRArray, csr_array
-from mlx_sparse._native import extension, library_path
-from mlx_sparse._ops import csr_batched_matmul, csr_batched_matvec, csr_matmat, csr_matmul, csr_matvec
+from mlx_sparse._native import check_device_errors, extension, library_path
+from mlx_sparse._ops import (
+    coo_matmat,
+    coo_matmul,
+    coo_matvec,
+    csr_batched_matmul,
+    csr_batched_matvec,
+    csr_matmat,
+    csr_matmul,
+    csr_matmul_data_vjp,
+    csr_matmul_transpose,
+    csr_matvec,
+    csr_matvec_data_vjp,
+    csr_matvec_transpose,
+)
 
 __version__ = "0.1.0"
 
 __all__ = [
     "COOArray",
     "CSRArray",
+    "check_device_errors",
     "coo_array",
+    "coo_matmat",
+    "coo_matmul",
+    "coo_matvec",
     "csr_array",
     "csr_matmat",
     "csr_batched_matmul",
     "csr_batched_matvec",
     "csr_matmul",
+    "csr_matmul_data_vjp",
+    "csr_matmul_transpose",
     "csr_matvec",
+    "csr_matvec_data_vjp",
+    "csr_matvec_transpose",
     "extension",
     "library_path",
     "linalg",

@@ -43,6 +43,7 @@ class CSRArray:
     has_canonical_format: bool = False
     _plan: list = field(default_factory=list, repr=False, compare=False)
     _solvers: dict = field(default_factory=dict, repr=False, compare=False)
+    _cache: dict = field(default_factory=dict, repr=False, compare=False)
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "shape", normalize_shape(self.shape))
@@ -107,6 +108,35 @@ class CSRArray:
         )
         data, indices, indptr = _native.csr_matmat(eye, self, prune_zeros=False)
         return CSRArray(data, indices, indptr, self.shape, sorted_indices=True, has_canonical_format=True)
+
+    def transpose_structure(self):
+        """``(indices, indptr, perm)`` of A^T (built once on the device by
+        ``msx_csr_transpose`` and cached): row c of A^T lists column c's
+        entries of A by ascending row, and ``perm`` maps them back to
+        positions in ``data``."""
+        if "t" not in self._cache:
+            self._cache["t"] = _native.csr_transpose_structure(self.indices, self.indptr, self.shape)
+        return self._cache["t"]
+
+    def transpose(self) -> "CSRArray":
+        """A^T as CSR (values gathered through the cached structure). Sorted
+        indices; canonical when ``self`` is."""
+        indices, indptr, perm = self.transpose_structure()
+        data = self.data.detach().index_select(0, perm) if perm.numel() else self.data.detach()[:0]
+        return CSRArray(data, indices, indptr, (self.shape[1], self.shape[0]), sorted_indices=True,
+                        has_canonical_format=self.has_canonical_format)
+
+    @property
+    def T(self) -> "CSRArray":
+        return self.transpose()
+
+    def tocoo(self):
+        """COO with the same entries in CSR order."""
+        from mlx_sparse._coo import COOArray
+
+        rows = torch.repeat_interleave(torch.arange(self.shape[0], device=self.device, dtype=self.indices.dtype),
+                                       torch.diff(self.indptr.to(torch.int64)))
+        return COOArray(self.data, rows, self.indices, self.shape, has_canonical_format=self.has_canonical_format)
 
     def diagonal(self) -> torch.Tensor:
         """Main diagonal as a dense vector (duplicate entries summed)."""

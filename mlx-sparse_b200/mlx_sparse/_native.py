@@ -67,6 +67,20 @@ def extension():
             L.msx_csr_pcg_jacobi.argtypes = [c_int, p, p, p, i64, p, p, p, p, i64, i64, c_float, c_float,
                                              ctypes.c_int32, p, p, p, p]
         L.msx_csr_diagonal.argtypes = [c_int, c_int, p, p, p, i64, i64, i64, p, p]
+        L.msx_check_device_errors.argtypes = [p]
+        L.msx_debug_set_spmv_poll_limit.argtypes = [i64]
+        L.msx_coo_tocsr.argtypes = [c_int, c_int, p, p, p, i64, i64, i64, c_int, p, p, p, p, p]
+        L.msx_csr_transpose.argtypes = [c_int, c_int, p, p, p, i64, i64, i64, p, p, p, p, p]
+        L.msx_csr_matvec_transpose.argtypes = [c_int, c_int, p, p, p, i64, p, p, i64, i64, p]
+        L.msx_csr_matmul_transpose.argtypes = [c_int, c_int, p, p, p, i64, p, i64, p, i64, i64, p]
+        L.msx_csr_matvec_data_vjp.argtypes = [c_int, c_int, p, p, i64, p, p, p, i64, i64, p]
+        L.msx_csr_matmul_data_vjp.argtypes = [c_int, c_int, p, p, i64, p, p, i64, p, i64, i64, p]
+        L.msx_csr_pcg_chebyshev.argtypes = [c_int, p, p, p, i64, p, p, p, p, p, i64, p, i64, i64, ctypes.c_int32,
+                                            c_float, c_float, c_float, c_float, ctypes.c_int32, p, p, p, p]
+        L.msx_csr_chebyshev_apply.argtypes = [c_int, p, p, p, i64, i64, p, i64, p, ctypes.c_int32, c_float, c_float,
+                                              p]
+        L.msx_diagonal_preconditioner_apply.argtypes = [p, p, i64, i64, p, p]
+        L.msx_csr_gershgorin_bounds.argtypes = [c_int, p, p, p, i64, i64, i64, p, p]
         L.msx_cg_context_create.argtypes = [c_int, p, p, p, i64, i64, i64, c_int, c_int, c_int, c_int, p, c_int, p,
                                             p, p, p, p, p, ctypes.POINTER(p)]
         L.msx_cg_context_ipc_handles.argtypes = [p, p, i64]
@@ -321,3 +335,156 @@ def csr_pcg_jacobi(data, indices, indptr, b, x0, inv_diag, shape, *, rtol, atol,
                                    float(atol), int(maxiter), ctypes.addressof(info), ctypes.addressof(res),
                                    ctypes.addressof(its), stream_ptr(dev)))
     return x, info.value, res.value, its.value
+
+
+def check_device_errors(device=None) -> None:
+    """Synchronises the current stream of ``device`` and raises RuntimeError if
+    a bounded device-side wait gave up since the last check (the flag is
+    cleared by the check)."""
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        check(extension().msx_check_device_errors(stream_ptr(dev)))
+
+
+def coo_tocsr(data, row, col, shape, *, sort_columns: bool = True, with_perm: bool = False):
+    """COO -> CSR on the device. ``sort_columns``: rows ordered by (column,
+    source position) as the reference's ``coo_tocsr``; else rows keep the
+    source order. Returns ``(data, indices, indptr)`` or, with ``with_perm``,
+    also the int64 source position of every output entry."""
+    L = extension()
+    dev = require_cuda(data, row, col)
+    data, row, col = (t.contiguous() for t in (data, row, col))
+    if row.dtype != col.dtype:
+        raise TypeError(f"coo_tocsr row and col must share an index dtype, got {row.dtype} and {col.dtype}.")
+    nnz = row.numel()
+    out_d = torch.empty(nnz, dtype=data.dtype, device=dev)
+    out_i = torch.empty(nnz, dtype=col.dtype, device=dev)
+    out_p = torch.empty(shape[0] + 1, dtype=row.dtype, device=dev)
+    perm = torch.empty(nnz, dtype=torch.int64, device=dev) if with_perm else None
+    with torch.cuda.device(dev):
+        check(L.msx_coo_tocsr(VALUE_CODES[data.dtype], INDEX_CODES[row.dtype], _p(data), _p(row), _p(col), nnz,
+                              shape[0], shape[1], int(bool(sort_columns)), _p(out_d), _p(out_i), _p(out_p),
+                              _p(perm), stream_ptr(dev)))
+    return (out_d, out_i, out_p, perm) if with_perm else (out_d, out_i, out_p)
+
+
+def csr_transpose_structure(indices, indptr, shape):
+    """Structure of A^T: ``(indices, indptr, perm)`` with ``perm[q]`` the
+    position in A of A^T's entry q (so A^T's values are ``data[perm]``)."""
+    L = extension()
+    dev = require_cuda(indices, indptr)
+    indices, indptr = indices.contiguous(), indptr.contiguous()
+    nnz = indices.numel()
+    out_i = torch.empty(nnz, dtype=indices.dtype, device=dev)
+    out_p = torch.empty(shape[1] + 1, dtype=indptr.dtype, device=dev)
+    perm = torch.empty(nnz, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_transpose(MSX_F32, INDEX_CODES[indices.dtype], None, _p(indices), _p(indptr), nnz, shape[0],
+                                  shape[1], None, _p(out_i), _p(out_p), _p(perm), stream_ptr(dev)))
+    return out_i, out_p, perm
+
+
+def csr_matvec_transpose(data, indices, indptr, x, shape):
+    """``A^T @ x`` (stateless: the transposed structure is rebuilt per call)."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr, x)
+    data, indices, indptr, x = (t.contiguous() for t in (data, indices, indptr, x))
+    out = torch.empty(shape[1], dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_matvec_transpose(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                                         _p(indptr), data.numel(), _p(x), _p(out), shape[0], shape[1],
+                                         stream_ptr(dev)))
+    return out
+
+
+def csr_matmul_transpose(data, indices, indptr, rhs, shape):
+    """``A^T @ B`` for a row-major ``B`` of shape ``(n_rows, k)``."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr, rhs)
+    data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
+    k = rhs.shape[1]
+    out = torch.empty((shape[1], k), dtype=data.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_matmul_transpose(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
+                                         _p(indptr), data.numel(), _p(rhs), k, _p(out), shape[0], shape[1],
+                                         stream_ptr(dev)))
+    return out
+
+
+def csr_data_vjp(indices, indptr, rhs, cotangent, shape):
+    """Cotangent of the stored values of ``A @ rhs``: ``out[p] =
+    cot[row(p)] * x[col(p)]`` (rank-1 rhs) or the row dot products
+    ``cot[row(p), :] . B[col(p), :]`` (rank-2)."""
+    L = extension()
+    dev = require_cuda(indices, indptr, rhs, cotangent)
+    indices, indptr, rhs, cotangent = (t.contiguous() for t in (indices, indptr, rhs, cotangent))
+    out = torch.empty(indices.numel(), dtype=rhs.dtype, device=dev)
+    with torch.cuda.device(dev):
+        if rhs.ndim == 1:
+            check(L.msx_csr_matvec_data_vjp(VALUE_CODES[rhs.dtype], INDEX_CODES[indices.dtype], _p(indices),
+                                            _p(indptr), indices.numel(), _p(rhs), _p(cotangent), _p(out), shape[0],
+                                            shape[1], stream_ptr(dev)))
+        else:
+            check(L.msx_csr_matmul_data_vjp(VALUE_CODES[rhs.dtype], INDEX_CODES[indices.dtype], _p(indices),
+                                            _p(indptr), indices.numel(), _p(rhs), _p(cotangent), rhs.shape[1],
+                                            _p(out), shape[0], shape[1], stream_ptr(dev)))
+    return out
+
+
+def csr_pcg_chebyshev(data, indices, indptr, b, x0, m, shape, *, degree, lambda_min, lambda_max, rtol, atol,
+                      maxiter):
+    """Chebyshev-preconditioned CG; ``m`` = (data, indices, indptr) of the
+    preconditioner matrix. Returns ``(x, info, residual, iterations)``."""
+    L = extension()
+    md, mi, mp = m
+    dev = require_cuda(data, indices, indptr, b, x0, md, mi, mp)
+    data, indices, indptr, b, x0, md, mi, mp = (t.contiguous() for t in (data, indices, indptr, b, x0, md, mi, mp))
+    x, info, res, its = _solver_outputs(dev, shape[0])
+    with torch.cuda.device(dev):
+        check(L.msx_csr_pcg_chebyshev(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(),
+                                      _p(b), _p(x0), _p(md), _p(mi), _p(mp), md.numel(), _p(x), shape[0], shape[1],
+                                      int(degree), float(lambda_min), float(lambda_max), float(rtol), float(atol),
+                                      int(maxiter), ctypes.addressof(info), ctypes.addressof(res),
+                                      ctypes.addressof(its), stream_ptr(dev)))
+    return x, info.value, res.value, its.value
+
+
+def csr_chebyshev_preconditioner_apply(data, indices, indptr, rhs, shape, *, degree, lambda_min, lambda_max):
+    """``p_d(M) rhs`` for rank-1 or rank-2 (row-major) ``rhs``."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr, rhs)
+    data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
+    k = 1 if rhs.ndim == 1 else int(rhs.shape[1])
+    out = torch.empty_like(rhs, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        check(L.msx_csr_chebyshev_apply(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(),
+                                        shape[0], _p(rhs), k, _p(out), int(degree), float(lambda_min),
+                                        float(lambda_max), stream_ptr(dev)))
+    return out
+
+
+def diagonal_preconditioner_apply(inv_diag, rhs):
+    """``inv_diag[:, None] * rhs`` (rank-1 or rank-2 ``rhs``), fp32."""
+    L = extension()
+    dev = require_cuda(inv_diag, rhs)
+    inv_diag, rhs = inv_diag.contiguous(), rhs.contiguous()
+    k = 1 if rhs.ndim == 1 else int(rhs.shape[1])
+    out = torch.empty_like(rhs)
+    with torch.cuda.device(dev):
+        check(L.msx_diagonal_preconditioner_apply(_p(inv_diag), _p(rhs), inv_diag.numel(), k, _p(out),
+                                                  stream_ptr(dev)))
+    return out
+
+
+def csr_gershgorin_bounds(data, indices, indptr, shape):
+    """(lower, upper, diag_min, diag_max) of a square fp32 CSR matrix."""
+    L = extension()
+    dev = require_cuda(data, indices, indptr)
+    data, indices, indptr = (t.contiguous() for t in (data, indices, indptr))
+    out = (ctypes.c_float * 4)()
+    with torch.cuda.device(dev):
+        check(L.msx_csr_gershgorin_bounds(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr),
+                                          data.numel(), shape[0], shape[1], out, stream_ptr(dev)))
+    return tuple(float(v) for v in out)

@@ -9,7 +9,10 @@ as in the reference's host path).
 
 from __future__ import annotations
 
+import torch
+
 from mlx_sparse import _native
+from mlx_sparse._coo import COOArray
 from mlx_sparse._csr import CSRArray
 from mlx_sparse._validation import (
     ensure_array,
@@ -18,12 +21,26 @@ from mlx_sparse._validation import (
 )
 
 
+def _wants_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(t.requires_grad for t in tensors)
+
+
 def csr_matvec(a: CSRArray, x):
-    """``y = A @ x`` for a rank-1 dense ``x`` (same dtype as ``a.data``)."""
+    """``y = A @ x`` for a rank-1 dense ``x`` (same dtype as ``a.data``).
+
+    Differentiable (torch autograd) in ``a.data`` and ``x``: the backward
+    products are the reference's VJPs (``src/sparse/csr_matvec/
+    csr_matvec.cpp:236-263``): ``csr_matvec_data_vjp`` and
+    ``csr_matvec_transpose``.
+    """
     if not isinstance(a, CSRArray):
         raise TypeError(f"csr_matvec expects CSRArray, got {type(a).__name__}.")
     x = ensure_array(x, device=a.device)
     validate_csr_matvec_inputs(a.data, a.indices, a.indptr, x, a.shape)
+    if _wants_grad(a.data, x):
+        from mlx_sparse._autodiff import CsrProduct
+
+        return CsrProduct.apply(a.data, x, a)
     plan = a.spmv_plan() if a.shape[0] > 0 else None
     return _native.csr_matvec(a.data, a.indices, a.indptr, x, a.shape, plan=plan)
 
@@ -36,6 +53,10 @@ def csr_matmul(a: CSRArray, rhs):
     rhs = ensure_array(rhs, device=a.device)
     if rhs.ndim == 2:
         validate_csr_matmul_inputs(a.data, a.indices, a.indptr, rhs, a.shape)
+        if _wants_grad(a.data, rhs):
+            from mlx_sparse._autodiff import CsrProduct
+
+            return CsrProduct.apply(a.data, rhs, a)
         return _native.csr_matmul(a.data, a.indices, a.indptr, rhs, a.shape)
     if rhs.ndim < 2:
         raise ValueError(f"csr_matmul expects rank-2 or higher RHS, got {tuple(rhs.shape)}.")
@@ -118,3 +139,99 @@ def csr_matmat(a: CSRArray, rhs: CSRArray) -> CSRArray:
     data, indices, indptr = _native.csr_matmat(a, rhs)
     return CSRArray(data, indices, indptr, (a.shape[0], rhs.shape[1]), sorted_indices=True,
                     has_canonical_format=True)
+
+
+# ---------------------------------------------------------------------------
+# Transposed products and data cotangents (the backward step of the products)
+# ---------------------------------------------------------------------------
+def csr_matvec_transpose(a: CSRArray, x):
+    """``A^T @ x``. Reference: ``csr_matvec_transpose`` (``src/sparse/
+    csr_matvec_transpose/csr_matvec_transpose.cpp:76-97``): each output entry
+    sums its column's entries in row-major order. Runs as an SpMV over the
+    matrix's cached transposed structure, which lists them in that order."""
+    if not isinstance(a, CSRArray):
+        raise TypeError(f"csr_matvec_transpose expects CSRArray, got {type(a).__name__}.")
+    x = ensure_array(x, device=a.device)
+    if x.ndim != 1 or x.shape[0] != a.shape[0]:
+        raise ValueError(f"csr_matvec_transpose x must have shape ({a.shape[0]},), got {tuple(x.shape)}.")
+    if x.dtype != a.data.dtype:
+        raise TypeError(f"csr_matvec_transpose requires matching dtypes, got {a.data.dtype} and {x.dtype}.")
+    return a.transpose() @ x
+
+
+def csr_matmul_transpose(a: CSRArray, rhs):
+    """``A^T @ B`` for ``B`` of shape ``(n_rows, k)`` (``src/sparse/
+    csr_matmul_transpose``)."""
+    if not isinstance(a, CSRArray):
+        raise TypeError(f"csr_matmul_transpose expects CSRArray, got {type(a).__name__}.")
+    rhs = ensure_array(rhs, device=a.device)
+    if rhs.ndim != 2 or rhs.shape[0] != a.shape[0]:
+        raise ValueError(f"csr_matmul_transpose rhs must have shape ({a.shape[0]}, k), got {tuple(rhs.shape)}.")
+    if rhs.dtype != a.data.dtype:
+        raise TypeError(f"csr_matmul_transpose requires matching dtypes, got {a.data.dtype} and {rhs.dtype}.")
+    return a.transpose() @ rhs
+
+
+def csr_matvec_data_vjp(a: CSRArray, x, cotangent):
+    """Cotangent of ``a.data`` for ``y = A @ x``: ``cot[row(p)] * x[col(p)]``
+    (``src/sparse/csr_matvec_data_vjp``)."""
+    x = ensure_array(x, device=a.device)
+    cotangent = ensure_array(cotangent, device=a.device)
+    if x.shape != (a.shape[1],) or cotangent.shape != (a.shape[0],):
+        raise ValueError("csr_matvec_data_vjp expects x of shape (n_cols,) and a cotangent of shape (n_rows,).")
+    return _native.csr_data_vjp(a.indices, a.indptr, x, cotangent, a.shape)
+
+
+def csr_matmul_data_vjp(a: CSRArray, rhs, cotangent):
+    """Cotangent of ``a.data`` for ``Y = A @ B``: ``sum_j cot[row(p), j] *
+    B[col(p), j]`` (``src/sparse/csr_matmul_data_vjp/
+    csr_matmul_data_vjp.cpp:88-100``)."""
+    rhs = ensure_array(rhs, device=a.device)
+    cotangent = ensure_array(cotangent, device=a.device)
+    if rhs.ndim != 2 or rhs.shape[0] != a.shape[1]:
+        raise ValueError("csr_matmul_data_vjp rhs first dimension must equal the sparse matrix column count.")
+    if cotangent.shape != (a.shape[0], rhs.shape[1]):
+        raise ValueError("csr_matmul_data_vjp cotangent must have shape (n_rows, rhs_cols).")
+    return _native.csr_data_vjp(a.indices, a.indptr, rhs, cotangent, a.shape)
+
+
+# ---------------------------------------------------------------------------
+# COO products
+# ---------------------------------------------------------------------------
+def _check_coo_rhs(a: COOArray, rhs, name):
+    if rhs.dtype != a.data.dtype:
+        raise TypeError(f"{name} requires sparse data and RHS to have the same dtype, got {a.data.dtype} and "
+                        f"{rhs.dtype}.")
+
+
+def coo_matvec(a: COOArray, x):
+    """``y = A @ x`` for COO ``A``. Reference: ``coo_matvec`` (``src/sparse/
+    coo_matmul/coo_matmul.cpp:343-357``), which sums every row over its
+    entries in source order; the cached source-order CSR copy makes the same
+    sums with the CSR SpMV kernels."""
+    if not isinstance(a, COOArray):
+        raise TypeError(f"coo_matvec expects COOArray, got {type(a).__name__}.")
+    x = ensure_array(x, device=a.device)
+    if x.ndim != 1 or x.shape[0] != a.shape[1]:
+        raise ValueError(f"coo_matvec x must have shape ({a.shape[1]},), got {tuple(x.shape)}.")
+    _check_coo_rhs(a, x, "coo_matvec")
+    return csr_matvec(a._stored_order_csr(), x)
+
+
+def coo_matmul(a: COOArray, rhs):
+    """``Y = A @ B`` for COO ``A`` and a dense ``B`` (rank >= 2: batched).
+    Reference: ``coo_matmul`` (``src/sparse/coo_matmul/coo_matmul.cpp:311-341``)."""
+    if not isinstance(a, COOArray):
+        raise TypeError(f"coo_matmul expects COOArray, got {type(a).__name__}.")
+    rhs = ensure_array(rhs, device=a.device)
+    if rhs.ndim < 2 or rhs.shape[-2] != a.shape[1]:
+        raise ValueError("coo_matmul rhs first dimension must equal the sparse matrix column count.")
+    _check_coo_rhs(a, rhs, "coo_matmul")
+    return csr_matmul(a._stored_order_csr(), rhs)
+
+
+def coo_matmat(a: COOArray, b: COOArray) -> COOArray:
+    """Sparse-sparse product of COO operands; canonical COO result (as the
+    reference's ``COOArray.__matmul__``), through the CSR SpGEMM kernels."""
+    c = csr_matmat(a.tocsr(canonical=True), b.tocsr(canonical=True))
+    return c.tocoo()

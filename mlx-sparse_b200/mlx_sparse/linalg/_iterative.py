@@ -101,6 +101,21 @@ def cg(A, b, *, x0=None, rtol: float = 1e-5, atol: float = 0.0, maxiter: int | N
     if M is not None:
         pc = preconditioners.aspreconditioner(M, csr)
         kind = pc.kind
+        if isinstance(pc, preconditioners.ChebyshevPreconditioner):
+            # csr_pcg_chebyshev, as the reference dispatches it (mlx_sparse/linalg/_iterative.py:266-283)
+            Mc = pc.A
+            if Mc.device != csr.device:
+                raise ValueError("the Chebyshev preconditioner must live on the matrix's device.")
+            if Mc.indices.dtype != csr.indices.dtype:
+                Mc = type(Mc)(Mc.data, Mc.indices.to(csr.indices.dtype), Mc.indptr.to(csr.indices.dtype), Mc.shape,
+                              Mc.sorted_indices, Mc.has_canonical_format)
+            x, info, residual, iterations = _native.csr_pcg_chebyshev(
+                csr.data, csr.indices, csr.indptr, rhs, guess, (Mc.data, Mc.indices, Mc.indptr), csr.shape,
+                degree=pc.degree, lambda_min=pc.lambda_min, lambda_max=pc.lambda_max, rtol=float(rtol),
+                atol=float(atol), maxiter=maxiter_value)
+            return finish_solver_result(x, info, residual, iterations, solver="cg", return_info=bool(return_info),
+                                        callback=callback, rtol=float(rtol), atol=float(atol),
+                                        maxiter=maxiter_value, preconditioner=kind)
         if isinstance(pc, preconditioners.DiagonalPreconditioner):
             x, info, residual, iterations = _solve(csr, rhs, guess, pc.inverse_diagonal.to(csr.device),
                                                    rtol, atol, maxiter_value)

@@ -1,11 +1,15 @@
-"""Preconditioners that the native CG path accepts: identity, diagonal, Jacobi.
+"""Preconditioners that the native CG path accepts: identity, diagonal,
+Jacobi and Chebyshev.
 
 Mirrors mlx-sparse's ``mlx_sparse/linalg/preconditioners.py`` for the CG path:
 ``DiagonalPreconditioner`` (:150-233), ``JacobiPreconditioner`` (:247-265),
-``identity`` (:998-1012), ``diagonal`` (:1015-1063), ``jacobi`` (:1066-1150)
-and ``aspreconditioner`` (:1546-1584). Setup runs with torch ops on the device
-and synchronises for the reference's validation checks (finite / near-zero
-diagonal), exactly where the reference calls ``host_bool``.
+``ChebyshevPreconditioner`` (:870-985), ``identity`` (:998-1012), ``diagonal``
+(:1015-1063), ``jacobi`` (:1066-1150), ``chebyshev`` (:1290-1428) and
+``aspreconditioner`` (:1546-1584). Setup runs on the device and synchronises
+for the reference's validation checks (finite / near-zero diagonal, spectral
+bounds), exactly where the reference reads values back to the host. Applying
+a diagonal or Chebyshev preconditioner (``solve``) runs in the CUDA library
+(``msx_diagonal_preconditioner_apply``, ``msx_csr_chebyshev_apply``).
 """
 
 from __future__ import annotations
@@ -13,6 +17,7 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from mlx_sparse._coo import COOArray
@@ -88,12 +93,22 @@ class DiagonalPreconditioner:
         return int(self.inverse_diagonal.shape[0])
 
     def solve(self, x):
+        """``inverse_diagonal * x`` for ``x`` of shape ``(n,)`` or ``(n, k)``
+        (the reference's ``diagonal_preconditioner_apply``,
+        ``src/preconditioners/diagonal/diagonal.cpp:60-88``)."""
+        from mlx_sparse import _native
+
         x = ensure_array(x, device=self.inverse_diagonal.device)
-        if x.ndim == 2:
-            return self.inverse_diagonal[:, None] * x
-        return self.inverse_diagonal * x
+        if x.ndim not in (1, 2):
+            raise ValueError("diagonal_preconditioner_apply rhs must be rank-1 or rank-2.")
+        if x.shape[0] != self.shape[0]:
+            raise ValueError("diagonal_preconditioner_apply rhs leading dimension must match inv_diag length.")
+        if x.dtype != torch.float32:
+            raise ValueError("diagonal_preconditioner_apply rhs currently requires dtype float32.")
+        return _native.diagonal_preconditioner_apply(self.inverse_diagonal, x)
 
     matvec = solve
+    __call__ = solve
 
 
 @dataclass(frozen=True)
@@ -105,6 +120,218 @@ class JacobiPreconditioner(DiagonalPreconditioner):
     zero_atol: float = 0.0
     checked: bool = False
     positive_diagonal: bool | None = None
+
+
+@dataclass(frozen=True)
+class ChebyshevPreconditioner:
+    """Fixed-degree first-kind Chebyshev polynomial preconditioner on a square
+    fp32 CSR operator over the spectral interval [lambda_min, lambda_max]."""
+
+    A: CSRArray
+    degree: int = 2
+    lambda_min: float = 0.0
+    lambda_max: float = 0.0
+    estimate: bool = True
+    spectral_info: dict = None
+    kind: str = "chebyshev"
+    is_symmetric: bool = True
+    is_positive_definite: bool = True
+
+    def __post_init__(self) -> None:
+        shape = _square_shape(self.A.shape)
+        if self.A.data.dtype != torch.float32:
+            raise TypeError("Chebyshev preconditioners require float32 CSR values.")
+        degree = int(self.degree)
+        if degree <= 0:
+            raise ValueError("degree must be positive.")
+        lmin = _finite_scalar("lambda_min", self.lambda_min)
+        lmax = _finite_scalar("lambda_max", self.lambda_max)
+        if lmin <= 0.0 or lmax <= lmin:
+            raise ValueError("Chebyshev spectral interval must satisfy 0 < lambda_min < lambda_max.")
+        object.__setattr__(self, "degree", degree)
+        object.__setattr__(self, "lambda_min", lmin)
+        object.__setattr__(self, "lambda_max", lmax)
+        object.__setattr__(self, "spectral_info", dict(self.spectral_info or {}))
+        if shape != self.A.shape:
+            raise ValueError("Chebyshev operator shape must be square.")
+
+    @property
+    def shape(self):
+        return self.A.shape
+
+    @property
+    def dtype(self):
+        return torch.float32
+
+    @property
+    def nnz(self) -> int:
+        return int(self.A.nnz)
+
+    def solve(self, x):
+        """``p_d(A) x`` for ``x`` of shape ``(n,)`` or ``(n, k)``
+        (``csr_chebyshev_preconditioner_apply``)."""
+        from mlx_sparse import _native
+
+        x = ensure_array(x, device=self.A.device)
+        if x.ndim not in (1, 2) or x.shape[0] != self.shape[0]:
+            raise ValueError(f"Chebyshev apply expects a right-hand side with leading dimension {self.shape[0]}.")
+        x = x.to(torch.float32)
+        if not bool(torch.isfinite(x).all().item()):
+            raise ValueError("right-hand side must contain only finite values.")
+        return _native.csr_chebyshev_preconditioner_apply(self.A.data, self.A.indices, self.A.indptr, x, self.shape,
+                                                          degree=self.degree, lambda_min=self.lambda_min,
+                                                          lambda_max=self.lambda_max)
+
+    matvec = solve
+    __call__ = solve
+
+
+_LANCZOS_STEPS = 20  # kDefaultEstimateSteps, src/preconditioners/chebyshev/chebyshev.cpp:41
+
+
+def _jacobi_symmetric_values(a: np.ndarray) -> np.ndarray:
+    """Eigenvalues of a small symmetric float32 matrix by cyclic-pivot Jacobi
+    rotations (restates ``jacobi_symmetric``, ``src/linalg/common/common.h:
+    259-313``: largest off-diagonal pivot, stop at 1e-6)."""
+    a = np.array(a, dtype=np.float32)
+    n = a.shape[0]
+    iu = np.triu_indices(n, 1)
+    for _ in range(max(32, 12 * n * n)):
+        if n < 2:
+            break
+        off = np.abs(a[iu])
+        k = int(np.argmax(off))
+        if off[k] <= np.float32(1e-6):
+            break
+        p, q = int(iu[0][k]), int(iu[1][k])
+        app, aqq, apq = a[p, p], a[q, q], a[p, q]
+        tau = np.float32((aqq - app) / (np.float32(2.0) * apq))
+        t = np.float32((np.float32(1.0) if tau >= 0 else np.float32(-1.0)) /
+                       (abs(tau) + np.sqrt(np.float32(1.0) + tau * tau)))
+        c = np.float32(np.float32(1.0) / np.sqrt(np.float32(1.0) + t * t))
+        s = np.float32(t * c)
+        cp, cq = a[:, p].copy(), a[:, q].copy()
+        a[:, p], a[:, q] = c * cp - s * cq, s * cp + c * cq
+        rp, rq = a[p, :].copy(), a[q, :].copy()
+        a[p, :], a[q, :] = c * rp - s * rq, s * rp + c * rq
+    return np.diag(a).astype(np.float32)
+
+
+def _lanczos_ritz_bounds(csr: CSRArray, steps: int):
+    """(ritz_min, ritz_max, used) of ``steps`` Lanczos steps with full
+    reorthogonalisation from the normalised ones vector (restates
+    ``host_lanczos_operator``, ``src/linalg/common/common.h:345-410``, and
+    ``lanczos_ritz_bounds``, ``chebyshev.cpp:163-203``). Products run in the
+    CUDA SpMV; the vector updates are fp32 with fp64 inner products."""
+    n = csr.shape[0]
+    steps = min(n, steps)
+    if steps <= 0:
+        return float("nan"), float("nan"), 0
+    dev = csr.device
+    basis = torch.zeros((steps, n), dtype=torch.float32, device=dev)
+    basis[0] = 1.0 / float(np.sqrt(np.float32(n)))
+    alphas, betas = [], []
+    beta_prev = 0.0
+    used = 0
+    eps = float(np.finfo(np.float32).eps)
+    for j in range(steps):
+        q = basis[j]
+        w = csr @ q
+        if j > 0:
+            w = w - np.float32(beta_prev) * basis[j - 1]
+        alpha = float(torch.dot(q.double(), w.double()).item())
+        alphas.append(np.float32(alpha))
+        w = w - np.float32(alpha) * q
+        for _ in range(2):
+            for col in range(j + 1):
+                coeff = float(torch.dot(basis[col].double(), w.double()).item())
+                w = w - np.float32(coeff) * basis[col]
+        beta = float(np.float32(np.sqrt(max(float(torch.dot(w.double(), w.double()).item()), 0.0))))
+        betas.append(np.float32(beta))
+        used = j + 1
+        if j + 1 == steps or beta <= eps:
+            break
+        basis[j + 1] = w / np.float32(beta)
+        beta_prev = beta
+    tri = np.zeros((used, used), dtype=np.float32)
+    for i in range(used):
+        tri[i, i] = alphas[i]
+        if i > 0:
+            tri[i, i - 1] = tri[i - 1, i] = betas[i - 1]
+    values = _jacobi_symmetric_values(tri)
+    values = values[np.isfinite(values)]
+    if values.size == 0:
+        return float("nan"), float("nan"), used
+    return float(values.min()), float(values.max()), used
+
+
+def spectral_bounds(csr: CSRArray, *, estimate: bool = True, estimate_steps: int = 0):
+    """``(gershgorin_min, gershgorin_max, ritz_min, ritz_max, diagonal_min,
+    diagonal_max, estimate_steps)`` as the reference's
+    ``csr_chebyshev_spectral_bounds`` (``chebyshev.cpp:374-425``)."""
+    from mlx_sparse import _native
+
+    if estimate_steps < 0:
+        raise ValueError("csr_chebyshev_spectral_bounds estimate_steps must be non-negative.")
+    gmin, gmax, dmin, dmax = _native.csr_gershgorin_bounds(csr.data, csr.indices, csr.indptr, csr.shape)
+    if estimate:
+        rmin, rmax, used = _lanczos_ritz_bounds(csr, estimate_steps or _LANCZOS_STEPS)
+    else:
+        rmin, rmax, used = float("nan"), float("nan"), 0
+    return gmin, gmax, rmin, rmax, dmin, dmax, used
+
+
+def chebyshev(A, *, degree: int = 2, lambda_min: float | None = None, lambda_max: float | None = None,
+              estimate: bool = True) -> ChebyshevPreconditioner:
+    """Chebyshev polynomial preconditioner of canonical fp32 ``A``; missing
+    bounds come from the Gershgorin interval, else from Lanczos Ritz values
+    (upper 1.1 x, lower max(tiny, min(0.5 x ritz_min, 0.1 x lambda_max))), as
+    the reference's ``chebyshev()`` chooses them."""
+    degree_value = int(degree)
+    if degree_value <= 0:
+        raise ValueError("degree must be positive.")
+    csr = A.tocsr(canonical=True) if isinstance(A, COOArray) else A
+    if not isinstance(csr, CSRArray):
+        raise TypeError(f"chebyshev expects a sparse matrix, got {type(A).__name__}.")
+    csr = csr.canonicalize()
+    if csr.data.dtype != torch.float32:
+        csr = csr.astype(torch.float32)
+    if csr.shape[0] != csr.shape[1]:
+        raise ValueError(f"chebyshev requires a square matrix, got {csr.shape}.")
+    gmin, gmax, rmin, rmax, dmin, dmax, steps = spectral_bounds(csr, estimate=bool(estimate))
+
+    def positive_finite(v) -> bool:
+        return math.isfinite(float(v)) and float(v) > 0.0
+
+    if lambda_max is None:
+        if positive_finite(gmax):
+            lmax, lmax_src = float(gmax), "gershgorin"
+        elif estimate and positive_finite(rmax):
+            lmax, lmax_src = 1.1 * float(rmax), "lanczos_1.1"
+        else:
+            raise ValueError("could not determine a positive Chebyshev upper spectral bound; pass lambda_max "
+                             "explicitly.")
+    else:
+        lmax, lmax_src = _finite_scalar("lambda_max", lambda_max), "explicit"
+    tiny = max(1.0e-12, 16.0 * 1.1920928955078125e-7)
+    if lambda_min is None:
+        if positive_finite(gmin):
+            lmin, lmin_src = float(gmin), "gershgorin"
+        elif estimate and positive_finite(rmin):
+            lmin, lmin_src = max(tiny, min(0.5 * float(rmin), 0.1 * lmax)), "lanczos_0.5"
+        else:
+            raise ValueError("could not determine a positive Chebyshev lower spectral bound; pass lambda_min "
+                             "explicitly or use estimate=True for SPD matrices whose Gershgorin lower bound is "
+                             "non-positive.")
+    else:
+        lmin, lmin_src = _finite_scalar("lambda_min", lambda_min), "explicit"
+    if not math.isfinite(lmin) or not math.isfinite(lmax) or lmin <= 0.0 or lmax <= lmin:
+        raise ValueError("Chebyshev spectral interval must satisfy 0 < lambda_min < lambda_max.")
+    info = {"gershgorin_min": gmin, "gershgorin_max": gmax, "ritz_min": rmin, "ritz_max": rmax,
+            "diagonal_min": dmin, "diagonal_max": dmax, "estimate_steps": int(steps),
+            "lambda_min_source": lmin_src, "lambda_max_source": lmax_src}
+    return ChebyshevPreconditioner(A=csr, degree=degree_value, lambda_min=lmin, lambda_max=lmax,
+                                   estimate=bool(estimate), spectral_info=info)
 
 
 def identity(A_or_shape, *, dtype=None) -> IdentityPreconditioner:
@@ -169,7 +396,7 @@ def aspreconditioner(M, A=None):
         if A is None:
             raise ValueError("A is required when M is None.")
         return identity(A)
-    if isinstance(M, (IdentityPreconditioner, DiagonalPreconditioner)):
+    if isinstance(M, (IdentityPreconditioner, DiagonalPreconditioner, ChebyshevPreconditioner)):
         if A is not None and M.shape != _square_shape(A):
             raise ValueError(f"preconditioner shape {M.shape} does not match A.shape.")
         return M
@@ -179,5 +406,5 @@ def aspreconditioner(M, A=None):
             "preconditioners.jacobi(A) or preconditioners.diagonal(...)."
         )
     raise TypeError(
-        "cg currently supports only identity, diagonal and Jacobi native-backed preconditioners."
+        "cg currently supports only identity, diagonal, Jacobi and Chebyshev native-backed preconditioners."
     )

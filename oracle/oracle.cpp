@@ -469,6 +469,220 @@ void pcg_jacobi(const float *data, const I *indices, const I *indptr, const floa
   *iterations = completed;
 }
 
+// ---- COO -> CSR (src/sparse/coo_tocsr/coo_tocsr.cpp:94-237, serial path) ----
+// Counting sort by row in source order, then a stable sort of every row by
+// column (sort_columns) - or no sort (source order, the summation order of
+// coo_matmul, src/sparse/coo_matmul/coo_matmul.cpp:~95-115).
+template <typename T, typename I>
+void coo_tocsr(const T *data, const I *row, const I *col, int64_t nnz, int64_t n_rows, bool sort_columns, T *out_data,
+               I *out_indices, I *out_indptr, int64_t *out_perm) {
+  std::fill(out_indptr, out_indptr + n_rows + 1, I{0});
+  for (int64_t p = 0; p < nnz; ++p) {
+    if (row[p] < 0 || (int64_t)row[p] >= n_rows) throw std::invalid_argument("coo_tocsr row out of range");
+    out_indptr[(int64_t)row[p] + 1] += I{1};
+  }
+  for (int64_t r = 0; r < n_rows; ++r) out_indptr[r + 1] += out_indptr[r];
+  std::vector<int64_t> next(out_indptr, out_indptr + n_rows), perm((size_t)nnz);
+  for (int64_t p = 0; p < nnz; ++p) perm[(size_t)next[(size_t)row[p]]++] = p;
+  if (sort_columns) {
+    for (int64_t r = 0; r < n_rows; ++r)
+      std::stable_sort(perm.begin() + (int64_t)out_indptr[r], perm.begin() + (int64_t)out_indptr[r + 1],
+                       [&](int64_t a, int64_t b) { return col[a] < col[b]; });
+  }
+  for (int64_t q = 0; q < nnz; ++q) {
+    if (out_data) out_data[q] = data[perm[(size_t)q]];
+    out_indices[q] = col[perm[(size_t)q]];
+    if (out_perm) out_perm[q] = perm[(size_t)q];
+  }
+}
+
+// ---- COO products (src/sparse/coo_matmul/coo_matmul.cpp:~90-140) -------------
+// out[row[p], :] += data[p] * rhs[col[p], :] over p in source order, fp32
+// accumulation for the half types.
+template <typename T, typename I>
+void coo_matmul(const T *data, const I *row, const I *col, int64_t nnz, const T *rhs, int64_t k, T *out,
+                int64_t n_rows) {
+  std::vector<float> acc((size_t)(n_rows * k), 0.0f);
+  for (int64_t p = 0; p < nnz; ++p) {
+    const float a = Acc<T>::load(data[p]);
+    float *o = acc.data() + (int64_t)row[p] * k;
+    const T *b = rhs + (int64_t)col[p] * k;
+    for (int64_t c = 0; c < k; ++c) o[c] += a * Acc<T>::load(b[c]);
+  }
+  for (int64_t i = 0; i < n_rows * k; ++i) out[i] = Acc<T>::store(acc[(size_t)i]);
+}
+
+// ---- transposed products (src/sparse/csr_matvec_transpose/
+// csr_matvec_transpose.cpp:76-97 and csr_matmul_transpose, serial path) -------
+template <typename T, typename I>
+void matmul_transpose(const T *data, const I *indices, const I *indptr, int64_t n_rows, int64_t n_cols, const T *rhs,
+                      int64_t k, T *out) {
+  std::vector<float> acc((size_t)(n_cols * k), 0.0f);
+  for (int64_t r = 0; r < n_rows; ++r)
+    for (I p = indptr[r]; p < indptr[r + 1]; ++p) {
+      const float a = Acc<T>::load(data[p]);
+      float *o = acc.data() + (int64_t)indices[p] * k;
+      for (int64_t c = 0; c < k; ++c) o[c] += a * Acc<T>::load(rhs[r * k + c]);
+    }
+  for (int64_t i = 0; i < n_cols * k; ++i) out[i] = Acc<T>::store(acc[(size_t)i]);
+}
+
+// ---- data cotangents (src/sparse/csr_matmul_data_vjp/
+// csr_matmul_data_vjp.cpp:88-100; csr_matvec_data_vjp is the k = 1 case) ----
+template <typename T, typename I>
+void data_vjp(const I *indices, const I *indptr, int64_t n_rows, const T *rhs, const T *cot, int64_t k, T *out) {
+  for (int64_t r = 0; r < n_rows; ++r)
+    for (I p = indptr[r]; p < indptr[r + 1]; ++p) {
+      float acc = 0.0f;
+      for (int64_t c = 0; c < k; ++c) acc += Acc<T>::load(cot[r * k + c]) * Acc<T>::load(rhs[(int64_t)indices[p] * k + c]);
+      out[p] = Acc<T>::store(acc);
+    }
+}
+
+// ---- Chebyshev preconditioner and Chebyshev PCG --------------------------------
+// chebyshev_apply_vector: src/preconditioners/pcg/chebyshev.cpp:84-122 (and the
+// standalone apply, src/preconditioners/chebyshev/chebyshev.cpp:262-300, which
+// runs the same recurrence column by column).
+template <typename I>
+void cheb_apply(const float *md, const I *mi, const I *mp, const float *rhs, float *out, std::vector<float> &prev,
+                std::vector<float> &next, std::vector<float> &ax, int64_t n, int degree, float lmin, float lmax) {
+  const float scale = 2.0f / (lmax + lmin);
+  const float alpha = 1.0f - scale * lmin;
+  const float mu = 1.0f / alpha;
+  const float omega_prod = 2.0f / alpha;
+  float c_prev = 1.0f, c_cur = mu;
+  std::fill(prev.begin(), prev.end(), 0.0f);
+  std::fill(next.begin(), next.end(), 0.0f);
+  for (int64_t i = 0; i < n; ++i) out[i] = scale * rhs[i];
+  if (degree == 1) return;
+  for (int it = 1; it < degree; ++it) {
+    spmv_f32(md, mi, mp, out, ax.data(), n);
+    const float c_next = 2.0f * mu * c_cur - c_prev;
+    const float omega = omega_prod * c_cur / c_next;
+    const float one_minus_omega = 1.0f - omega;
+    const float omega_scale = omega * scale;
+    for (int64_t i = 0; i < n; ++i) {
+      const float r = rhs[i] - ax[(size_t)i];
+      next[(size_t)i] = one_minus_omega * prev[(size_t)i] + omega * out[i] + omega_scale * r;
+    }
+    std::copy(out, out + n, prev.begin());
+    std::copy(next.begin(), next.end(), out);
+    c_prev = c_cur;
+    c_cur = c_next;
+  }
+}
+
+// csr_pcg_chebyshev_cpu_impl: src/preconditioners/pcg/chebyshev.cpp:124-313.
+template <typename I>
+void pcg_chebyshev(const float *data, const I *indices, const I *indptr, const float *b, const float *x0,
+                   const float *md, const I *mi, const I *mp, float *x, int64_t n, int degree, float lmin, float lmax,
+                   float rtol, float atol, int maxiter, int *info, float *residual, int *iterations) {
+  std::vector<float> r(n), z(n), p(n), ap(n), cp(n), cn(n), cax(n);
+  std::copy(x0, x0 + n, x);
+  spmv_f32(data, indices, indptr, x, ap.data(), n);
+  double b_norm2 = 0.0;
+  bool finite = true;
+  for (int64_t i = 0; i < n; ++i) {
+    const float ri = b[i] - ap[i];
+    r[i] = ri;
+    b_norm2 += (double)b[i] * (double)b[i];
+    finite = finite && finite_f(ri) && finite_f(b[i]) && finite_f(x[i]);
+  }
+  cheb_apply(md, mi, mp, r.data(), z.data(), cp, cn, cax, n, degree, lmin, lmax);
+  p = z;
+  float true_rr = dot_f(r, r);
+  float rho = dot_f(r, z);
+  const float b_norm = std::sqrt(std::max(b_norm2, 0.0));
+  const float tol = std::max(atol, rtol * b_norm);
+  const float true_residual = std::sqrt(std::max(true_rr, 0.0f));
+  if (!finite || !finite_f(true_rr) || !finite_f(rho)) {
+    *info = -3; *residual = true_residual; *iterations = 0;
+    return;
+  }
+  if (true_residual <= tol) {
+    *info = 0; *residual = true_residual; *iterations = 0;
+    return;
+  }
+  if (rho <= 0.0f) {
+    *info = -2; *residual = true_residual; *iterations = 0;
+    return;
+  }
+  const float eps = std::numeric_limits<float>::epsilon();
+  int status = maxiter > 0 ? maxiter : 1;
+  int completed = 0;
+  for (int it = 1; it <= maxiter; ++it) {
+    spmv_f32(data, indices, indptr, p.data(), ap.data(), n);
+    const float denom = dot_f(p, ap);
+    const float pn = dot_f(p, p);
+    const float apn = dot_f(ap, ap);
+    const float scale = std::sqrt(std::max(pn * apn, 0.0f));
+    const float dtol = eps * std::max(1.0f, scale);
+    if (!finite_f(denom) || !finite_f(scale) || std::abs(denom) <= dtol) {
+      status = -1; completed = it - 1;
+      break;
+    }
+    const float alpha = rho / denom;
+    if (!finite_f(alpha)) {
+      status = -3; completed = it - 1;
+      break;
+    }
+    double rr_acc = 0.0;
+    finite = true;
+    for (int64_t i = 0; i < n; ++i) {
+      x[i] += alpha * p[i];
+      const float ri = r[i] - alpha * ap[i];
+      r[i] = ri;
+      rr_acc += (double)ri * (double)ri;
+      finite = finite && finite_f(x[i]) && finite_f(ri);
+    }
+    true_rr = (float)rr_acc;
+    const float r_norm = std::sqrt(std::max(true_rr, 0.0f));
+    completed = it;
+    if (!finite || !finite_f(true_rr) || !finite_f(r_norm)) {
+      status = -3;
+      break;
+    }
+    if (r_norm <= tol) {
+      status = 0;
+      break;
+    }
+    cheb_apply(md, mi, mp, r.data(), z.data(), cp, cn, cax, n, degree, lmin, lmax);
+    const float rho_new = dot_f(r, z);
+    if (!finite_f(rho_new) || rho_new <= 0.0f) {
+      status = -2;
+      break;
+    }
+    const float beta = rho_new / rho;
+    if (!finite_f(beta)) {
+      status = -3;
+      break;
+    }
+    for (int64_t i = 0; i < n; ++i) p[i] = z[i] + beta * p[i];
+    rho = rho_new;
+  }
+  *info = status;
+  *residual = std::sqrt(std::max(true_rr, 0.0f));
+  *iterations = completed;
+}
+
+// Gershgorin and diagonal bounds: src/preconditioners/chebyshev/chebyshev.cpp:120-161.
+template <typename I>
+void gershgorin(const float *data, const I *indices, const I *indptr, int64_t n_rows, float *out4) {
+  double lower = std::numeric_limits<double>::infinity(), upper = -lower, dmin = lower, dmax = -lower;
+  for (int64_t r = 0; r < n_rows; ++r) {
+    double diag = 0.0, off = 0.0;
+    for (I p = indptr[r]; p < indptr[r + 1]; ++p) {
+      if ((int64_t)indices[p] == r) diag += (double)data[p];
+      else off += std::abs((double)data[p]);
+    }
+    lower = std::min(lower, diag - off);
+    upper = std::max(upper, diag + off);
+    dmin = std::min(dmin, diag);
+    dmax = std::max(dmax, diag);
+  }
+  out4[0] = (float)lower; out4[1] = (float)upper; out4[2] = (float)dmin; out4[3] = (float)dmax;
+}
+
 template <typename Fn> void by_value(int vt, Fn fn) {
   if (vt == 0) fn(float{});
   else if (vt == 1) fn(f16{});
@@ -588,6 +802,97 @@ int orc_weighted_ranges(const int64_t *work, int64_t n, int parts, int64_t *out_
     out_pairs[2 * i + 1] = r[i].end;
   }
   return (int)r.size();
+}
+
+int orc_coo_tocsr(int vt, int it, const void *data, const void *row, const void *col, int64_t nnz, int64_t n_rows,
+                  int sort_columns, void *out_data, void *out_indices, void *out_indptr, int64_t *out_perm) {
+  return guard([&] {
+    by_value(vt, [&](auto v) {
+      using T = decltype(v);
+      by_index(it, [&](auto i) {
+        using I = decltype(i);
+        coo_tocsr<T, I>((const T *)data, (const I *)row, (const I *)col, nnz, n_rows, sort_columns != 0, (T *)out_data,
+                        (I *)out_indices, (I *)out_indptr, out_perm);
+      });
+    });
+  });
+}
+
+int orc_coo_matmul(int vt, int it, const void *data, const void *row, const void *col, int64_t nnz, const void *rhs,
+                   int64_t k, void *out, int64_t n_rows) {
+  return guard([&] {
+    by_value(vt, [&](auto v) {
+      using T = decltype(v);
+      by_index(it, [&](auto i) {
+        using I = decltype(i);
+        coo_matmul<T, I>((const T *)data, (const I *)row, (const I *)col, nnz, (const T *)rhs, k, (T *)out, n_rows);
+      });
+    });
+  });
+}
+
+int orc_csr_matmul_transpose(int vt, int it, const void *data, const void *indices, const void *indptr,
+                             int64_t n_rows, int64_t n_cols, const void *rhs, int64_t k, void *out) {
+  return guard([&] {
+    by_value(vt, [&](auto v) {
+      using T = decltype(v);
+      by_index(it, [&](auto i) {
+        using I = decltype(i);
+        matmul_transpose<T, I>((const T *)data, (const I *)indices, (const I *)indptr, n_rows, n_cols, (const T *)rhs,
+                               k, (T *)out);
+      });
+    });
+  });
+}
+
+int orc_csr_data_vjp(int vt, int it, const void *indices, const void *indptr, int64_t n_rows, const void *rhs,
+                     const void *cot, int64_t k, void *out) {
+  return guard([&] {
+    by_value(vt, [&](auto v) {
+      using T = decltype(v);
+      by_index(it, [&](auto i) {
+        using I = decltype(i);
+        data_vjp<T, I>((const I *)indices, (const I *)indptr, n_rows, (const T *)rhs, (const T *)cot, k, (T *)out);
+      });
+    });
+  });
+}
+
+int orc_chebyshev_apply(int it, const float *md, const void *mi, const void *mp, int64_t n, const float *rhs,
+                        int64_t k, float *out, int degree, float lmin, float lmax) {
+  return guard([&] {
+    by_index(it, [&](auto i) {
+      using I = decltype(i);
+      std::vector<float> prev(n), next(n), ax(n), col(n), res(n);
+      for (int64_t c = 0; c < k; ++c) {  // column by column, as the recurrence is per column
+        for (int64_t r = 0; r < n; ++r) col[r] = rhs[r * k + c];
+        cheb_apply<I>(md, (const I *)mi, (const I *)mp, col.data(), res.data(), prev, next, ax, n, degree, lmin, lmax);
+        for (int64_t r = 0; r < n; ++r) out[r * k + c] = res[r];
+      }
+    });
+  });
+}
+
+int orc_csr_pcg_chebyshev(int it, const float *data, const void *indices, const void *indptr, const float *b,
+                          const float *x0, const float *md, const void *mi, const void *mp, float *x, int64_t n,
+                          int degree, float lmin, float lmax, float rtol, float atol, int maxiter, int *info,
+                          float *residual, int *iterations) {
+  return guard([&] {
+    by_index(it, [&](auto i) {
+      using I = decltype(i);
+      pcg_chebyshev<I>(data, (const I *)indices, (const I *)indptr, b, x0, md, (const I *)mi, (const I *)mp, x, n,
+                       degree, lmin, lmax, rtol, atol, maxiter, info, residual, iterations);
+    });
+  });
+}
+
+int orc_gershgorin(int it, const float *data, const void *indices, const void *indptr, int64_t n_rows, float *out4) {
+  return guard([&] {
+    by_index(it, [&](auto i) {
+      using I = decltype(i);
+      gershgorin<I>(data, (const I *)indices, (const I *)indptr, n_rows, out4);
+    });
+  });
 }
 
 }  // extern "C"

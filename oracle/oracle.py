@@ -60,6 +60,14 @@ def lib():
         L.orc_csr_cg.argtypes = [c_int, p, p, p, p, p, p, c_i64, c_float, c_float, c_int, p, p, p]
         L.orc_csr_pcg_jacobi.argtypes = [c_int, p, p, p, p, p, p, p, c_i64, c_float, c_float, c_int, p, p, p, c_int]
         L.orc_weighted_ranges.argtypes = [p, c_i64, c_int, p]
+        L.orc_coo_tocsr.argtypes = [c_int, c_int, p, p, p, c_i64, c_i64, c_int, p, p, p, p]
+        L.orc_coo_matmul.argtypes = [c_int, c_int, p, p, p, c_i64, p, c_i64, p, c_i64]
+        L.orc_csr_matmul_transpose.argtypes = [c_int, c_int, p, p, p, c_i64, c_i64, p, c_i64, p]
+        L.orc_csr_data_vjp.argtypes = [c_int, c_int, p, p, c_i64, p, p, c_i64, p]
+        L.orc_chebyshev_apply.argtypes = [c_int, p, p, p, c_i64, p, c_i64, p, c_int, c_float, c_float]
+        L.orc_csr_pcg_chebyshev.argtypes = [c_int, p, p, p, p, p, p, p, p, p, c_i64, c_int, c_float, c_float,
+                                            c_float, c_float, c_int, p, p, p]
+        L.orc_gershgorin.argtypes = [c_int, p, p, p, c_i64, p]
         _lib = L
     return _lib
 
@@ -155,6 +163,87 @@ def csr_pcg_jacobi(data, indices, indptr, b, x0, inv_diag, *, rtol, atol, maxite
                                     _ptr(x0), _ptr(inv_diag), _ptr(x), n, rtol, atol, maxiter, ctypes.byref(info),
                                     ctypes.byref(res), ctypes.byref(its), stop_after))
     return x, info.value, res.value, its.value
+
+
+def coo_tocsr(data, row, col, n_rows, *, sort_columns=True, bf16=False):
+    """(data, indices, indptr, perm): coo_tocsr.cpp:94-237 (sort_columns) or
+    rows in source order (the coo_matmul summation order)."""
+    data, row, col = (np.ascontiguousarray(a) for a in (data, row, col))
+    nnz = row.shape[0]
+    od = np.empty(nnz, dtype=data.dtype)
+    oi = np.empty(nnz, dtype=col.dtype)
+    op = np.empty(n_rows + 1, dtype=row.dtype)
+    perm = np.empty(nnz, dtype=np.int64)
+    _check(lib().orc_coo_tocsr(_vt(data, bf16), _IT[row.dtype], _ptr(data), _ptr(row), _ptr(col), nnz, n_rows,
+                               int(sort_columns), _ptr(od), _ptr(oi), _ptr(op), _ptr(perm)))
+    return od, oi, op, perm
+
+
+def coo_matmul(data, row, col, rhs, n_rows, *, bf16=False):
+    """coo_matmul.cpp: rows accumulated over entries in source order; rhs is
+    (n_cols,) or (n_cols, k)."""
+    data, row, col, rhs = (np.ascontiguousarray(a) for a in (data, row, col, rhs))
+    k = 1 if rhs.ndim == 1 else rhs.shape[1]
+    out = np.empty((n_rows, k), dtype=data.dtype)
+    _check(lib().orc_coo_matmul(_vt(data, bf16), _IT[row.dtype], _ptr(data), _ptr(row), _ptr(col), row.shape[0],
+                                _ptr(rhs), k, _ptr(out), n_rows))
+    return out.reshape(n_rows) if rhs.ndim == 1 else out
+
+
+def csr_matmul_transpose(data, indices, indptr, rhs, n_cols, *, bf16=False):
+    """A^T @ rhs (csr_matvec_transpose.cpp:76-97 serial order); rhs (n_rows,)
+    or (n_rows, k)."""
+    data, indices, indptr, rhs = (np.ascontiguousarray(a) for a in (data, indices, indptr, rhs))
+    n_rows = indptr.shape[0] - 1
+    k = 1 if rhs.ndim == 1 else rhs.shape[1]
+    out = np.empty((n_cols, k), dtype=data.dtype)
+    _check(lib().orc_csr_matmul_transpose(_vt(data, bf16), _IT[indices.dtype], _ptr(data), _ptr(indices),
+                                          _ptr(indptr), n_rows, n_cols, _ptr(rhs), k, _ptr(out)))
+    return out.reshape(n_cols) if rhs.ndim == 1 else out
+
+
+def csr_data_vjp(indices, indptr, rhs, cot, *, bf16=False):
+    """csr_matvec_data_vjp (rhs, cot rank 1) / csr_matmul_data_vjp (rank 2)."""
+    indices, indptr, rhs, cot = (np.ascontiguousarray(a) for a in (indices, indptr, rhs, cot))
+    n_rows = indptr.shape[0] - 1
+    k = 1 if rhs.ndim == 1 else rhs.shape[1]
+    out = np.empty(indices.shape[0], dtype=rhs.dtype)
+    _check(lib().orc_csr_data_vjp(_vt(rhs, bf16), _IT[indices.dtype], _ptr(indices), _ptr(indptr), n_rows,
+                                  _ptr(rhs), _ptr(cot), k, _ptr(out)))
+    return out
+
+
+def chebyshev_apply(data, indices, indptr, rhs, *, degree, lambda_min, lambda_max):
+    data, indices, indptr, rhs = (np.ascontiguousarray(a) for a in (data, indices, indptr, rhs))
+    n = indptr.shape[0] - 1
+    k = 1 if rhs.ndim == 1 else rhs.shape[1]
+    out = np.empty((n, k), dtype=np.float32)
+    _check(lib().orc_chebyshev_apply(_IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr), n, _ptr(rhs), k,
+                                     _ptr(out), int(degree), float(lambda_min), float(lambda_max)))
+    return out.reshape(n) if rhs.ndim == 1 else out
+
+
+def csr_pcg_chebyshev(data, indices, indptr, b, x0, m, *, degree, lambda_min, lambda_max, rtol, atol, maxiter):
+    """m = (data, indices, indptr) of the preconditioner matrix."""
+    data, indices, indptr, b, x0 = (np.ascontiguousarray(a) for a in (data, indices, indptr, b, x0))
+    md, mi, mp = (np.ascontiguousarray(a) for a in m)
+    n = b.shape[0]
+    x = np.empty(n, dtype=np.float32)
+    info, res, its = ctypes.c_int(), ctypes.c_float(), ctypes.c_int()
+    _check(lib().orc_csr_pcg_chebyshev(_IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr), _ptr(b),
+                                       _ptr(x0), _ptr(md), _ptr(mi), _ptr(mp), _ptr(x), n, int(degree),
+                                       float(lambda_min), float(lambda_max), rtol, atol, maxiter,
+                                       ctypes.byref(info), ctypes.byref(res), ctypes.byref(its)))
+    return x, info.value, res.value, its.value
+
+
+def gershgorin(data, indices, indptr):
+    """(lower, upper, diag_min, diag_max) of chebyshev.cpp:120-161."""
+    data, indices, indptr = (np.ascontiguousarray(a) for a in (data, indices, indptr))
+    out = np.empty(4, dtype=np.float32)
+    _check(lib().orc_gershgorin(_IT[indices.dtype], _ptr(data), _ptr(indices), _ptr(indptr), indptr.shape[0] - 1,
+                                _ptr(out)))
+    return tuple(float(v) for v in out)
 
 
 def weighted_ranges(work, parts):

@@ -128,6 +128,50 @@ def main():
         "source": "tests/test_linalg_preconditioners.py:2094-2123",
     }
 
+    # tests/test_coo_tocsr.py:23-36 (sorted by row, then column)
+    cases["coo_tocsr_sort"] = {
+        "data": [10.0, 20.0, 30.0, 40.0], "row": [2, 0, 1, 0], "col": [1, 3, 2, 0], "shape": [3, 4],
+        "indptr": [0, 2, 3, 4], "indices": [0, 3, 2, 1], "out_data": [40.0, 20.0, 30.0, 10.0],
+        "source": "tests/test_coo_tocsr.py:23-36",
+    }
+    # tests/test_coo_tocsr.py:38-51 (duplicates summed by canonicalize)
+    cases["coo_canonical_dups"] = {
+        "data": [2.0, 3.0, 5.0], "row": [0, 0, 0], "col": [1, 1, 0], "shape": [1, 3],
+        "indptr": [0, 2], "indices": [0, 1], "out_data": [5.0, 5.0],
+        "source": "tests/test_coo_tocsr.py:38-51",
+    }
+    # tests/test_coo_tocsr.py:53-60 (empty)
+    cases["coo_empty"] = {"data": [], "row": [], "col": [], "shape": [4, 5], "indptr": [0, 0, 0, 0, 0],
+                          "indices": [], "out_data": [], "source": "tests/test_coo_tocsr.py:53-60"}
+
+    # tests/test_grad.py:180-223 (loss = sum((A x)^2); gradients of the dense
+    # product restricted to the stored coordinates, as the test compares)
+    row = np.array([0, 0, 2, 2])
+    col = np.array([0, 2, 1, 3])
+    vals = np.array([2.0, -1.0, 4.0, 5.0])
+    dense = np.zeros((3, 4))
+    dense[row, col] = vals
+    x = np.array([3.0, 10.0, 7.0, -2.0])
+    y = dense @ x
+    cases["grad_csr_matvec"] = {
+        "A": {"data": vals.tolist(), "indices": col.tolist(), "indptr": [0, 2, 2, 4], "shape": [3, 4]},
+        "x": x.tolist(), "grad_data": (2 * y[row] * x[col]).tolist(), "grad_x": (2 * dense.T @ y).tolist(),
+        "source": "tests/test_grad.py:180-223",
+    }
+    # tests/test_grad.py:358-404 (COO @ B, loss = sum(Y^2))
+    row = np.array([0, 0, 1, 2, 2])
+    col = np.array([0, 2, 1, 0, 3])
+    vals = np.array([2.0, -1.0, 0.5, 3.0, -2.0])
+    B = np.arange(12, dtype=np.float64).reshape(4, 3) / 7.0
+    dense = np.zeros((3, 4))
+    dense[row, col] = vals
+    Y = dense @ B
+    cases["grad_coo_matmul"] = {
+        "data": vals.tolist(), "row": row.tolist(), "col": col.tolist(), "shape": [3, 4],
+        "B": B.astype(np.float32).tolist(), "grad_data": (2 * np.sum(Y[row] * B[col], axis=1)).tolist(),
+        "grad_B": (2 * dense.T @ Y).tolist(), "source": "tests/test_grad.py:358-404",
+    }
+
     path = os.path.join(HERE, "reference_cases.json")
     with open(path, "w") as f:
         json.dump(cases, f, indent=1)

@@ -245,3 +245,66 @@ def test_pcg_poisson3d_fixture_reproduces(orc):
     assert (info, its) == (g["info"], g["iterations"])
     assert res == pytest.approx(g["residual"], rel=1e-6)
     assert x[:8].tolist() == g["x_head"]
+
+
+@pytest.mark.parametrize("name", ["coo_tocsr_sort", "coo_empty"])
+def test_coo_tocsr_known_answers(orc, golden, name):
+    c = golden[name]
+    d, i, p, _ = orc.coo_tocsr(np.asarray(c["data"], np.float32), np.asarray(c["row"], np.int32),
+                               np.asarray(c["col"], np.int32), c["shape"][0])
+    assert p.tolist() == c["indptr"] and i.tolist() == c["indices"] and d.tolist() == c["out_data"]
+
+
+@pytest.mark.parametrize("it", [np.int32, np.int64])
+def test_coo_oracle_matches_numpy_and_scipy(orc, it):
+    rng = np.random.default_rng(3)
+    n, m, nnz = 400, 300, 5000
+    row = rng.integers(0, n, nnz).astype(it)
+    col = rng.integers(0, m, nnz).astype(it)
+    d = rng.standard_normal(nnz).astype(np.float32)
+    od, oi, op, perm = orc.coo_tocsr(d, row, col, n)
+    assert np.array_equal(perm, np.lexsort((np.arange(nnz), col, row)))  # (row, col, source) order
+    assert np.array_equal(oi, col[perm]) and np.array_equal(od, d[perm])
+    assert np.array_equal(op, np.concatenate([[0], np.cumsum(np.bincount(row, minlength=n))]))
+    _, _, _, perm_s = orc.coo_tocsr(d, row, col, n, sort_columns=False)
+    assert np.array_equal(perm_s, np.argsort(row, kind="stable"))
+    S = sp.coo_matrix((d, (row, col)), shape=(n, m)).tocsr()
+    x = wl.uniform_vector(m, 1)
+    B = wl.uniform_matrix(m, 5, 2)
+    np.testing.assert_allclose(orc.coo_matmul(d, row, col, x, n), S @ x, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(orc.coo_matmul(d, row, col, B, n), S @ B, rtol=1e-5, atol=1e-5)
+
+
+def test_transpose_and_data_vjp_oracle_match_scipy(orc):
+    (d, i, p), shape = wl.ragged_csr(300, 200, 4, 20)
+    S = sp.csr_matrix((d, i, p), shape=shape)
+    x = wl.uniform_vector(shape[0], 1)
+    B = wl.uniform_matrix(shape[0], 4, 2)
+    np.testing.assert_allclose(orc.csr_matmul_transpose(d, i, p, x, shape[1]), S.T @ x, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(orc.csr_matmul_transpose(d, i, p, B, shape[1]), S.T @ B, rtol=1e-5, atol=1e-5)
+    xc, cot = wl.uniform_vector(shape[1], 3), wl.uniform_vector(shape[0], 4)
+    rows = np.repeat(np.arange(shape[0]), np.diff(p))
+    np.testing.assert_array_equal(orc.csr_data_vjp(i, p, xc, cot), cot[rows] * xc[i])
+    Bc, C = wl.uniform_matrix(shape[1], 3, 5), wl.uniform_matrix(shape[0], 3, 6)
+    np.testing.assert_allclose(orc.csr_data_vjp(i, p, Bc, C), np.sum(C[rows] * Bc[i], axis=1), rtol=1e-6, atol=1e-6)
+
+
+def test_chebyshev_oracle_approaches_the_solve(orc):
+    """A high-degree Chebyshev semi-iteration over the exact spectral
+    interval approximates A^-1 r, and the oracle's Chebyshev PCG converges to
+    SciPy's solution."""
+    (d, i, p), shape = wl.lap2d(12)
+    S = sp.csr_matrix((d, i, p), shape=shape).toarray().astype(np.float64)
+    ev = np.linalg.eigvalsh(S)
+    r = wl.uniform_vector(shape[0], 1)
+    z = orc.chebyshev_apply(d, i, p, r, degree=60, lambda_min=float(ev[0]), lambda_max=float(ev[-1]))
+    np.testing.assert_allclose(z, np.linalg.solve(S, r), rtol=1e-3, atol=1e-3)
+    x, info, _, its = orc.csr_pcg_chebyshev(d, i, p, r, np.zeros(shape[0], np.float32), (d, i, p), degree=3,
+                                            lambda_min=float(ev[0]), lambda_max=float(ev[-1]), rtol=1e-4, atol=0.0,
+                                            maxiter=500)
+    # (at tighter rtol the reference's unscaled breakdown test, chebyshev.cpp:
+    # 236-245, stops this fast solve with status -1 first)
+    assert info == 0 and its < 60
+    np.testing.assert_allclose(x, np.linalg.solve(S, r), rtol=1e-4, atol=1e-4)
+    lo, hi, dmin, dmax = orc.gershgorin(d, i, p)
+    assert (lo, hi, dmin, dmax) == (0.0, 8.0, 4.0, 4.0)
