@@ -50,6 +50,33 @@ typedef enum {
   MSX_ERR_CUDA = 5      /* CUDA runtime failure    -> RuntimeError */
 } msx_status;
 
+/* ------------------------------------------------------------------------ */
+/* DLPack tensors (the boundary the reference's Python layer crosses with    */
+/* device arrays). The layout is the public DLPack ABI (dlpack.h, v0.6-1.x:  */
+/* DLTensor has not changed); a caller that already includes dlpack.h gets   */
+/* its definitions instead of these.                                         */
+/* ------------------------------------------------------------------------ */
+#if !defined(DLPACK_VERSION)
+typedef struct {
+  int32_t device_type; /* kDLCUDA = 2, kDLCUDAManaged = 13 accepted here */
+  int32_t device_id;
+} DLDevice;
+typedef struct {
+  uint8_t code; /* kDLInt = 0, kDLFloat = 2, kDLBfloat = 4 */
+  uint8_t bits;
+  uint16_t lanes;
+} DLDataType;
+typedef struct {
+  void *data;
+  DLDevice device;
+  int32_t ndim;
+  DLDataType dtype;
+  int64_t *shape;
+  int64_t *strides; /* NULL = compact row-major */
+  uint64_t byte_offset;
+} DLTensor;
+#endif
+
 /* Thread-local message of the last failing call on this thread ("" if none). */
 MSX_API const char *msx_last_error(void);
 
@@ -415,6 +442,58 @@ MSX_API int msx_cg_context_solve(msx_cg_context *ctx, const float *b,
                                  int32_t maxiter, int32_t *info, float *residual,
                                  int32_t *iterations, void *stream);
 MSX_API int msx_cg_context_destroy(msx_cg_context *ctx);
+
+/* ------------------------------------------------------------------------ */
+/* DLPack entry points: the same operations with every array passed as a     */
+/* DLTensor (borrowed; outputs caller-allocated). They check what the raw    */
+/* entry points cannot: device (CUDA, the current device), dtype codes,      */
+/* ranks, shapes against n_rows / n_cols, compact strides, and that indices  */
+/* and indptr share an index dtype; byte_offset is honoured. Errors follow    */
+/* the same status codes and messages as the reference's front-ends.         */
+/* ------------------------------------------------------------------------ */
+/* csr_matvec (src/bindings.cpp:874-883, mlx_sparse/_native.py:179-189). */
+MSX_API int msx_dl_csr_matvec(const DLTensor *data, const DLTensor *indices,
+                              const DLTensor *indptr, const DLTensor *x,
+                              DLTensor *y, int64_t n_rows, int64_t n_cols,
+                              const msx_spmv_plan *plan, void *stream);
+/* csr_matmul (src/bindings.cpp:965-975, mlx_sparse/_native.py:286-296). */
+MSX_API int msx_dl_csr_matmul(const DLTensor *data, const DLTensor *indices,
+                              const DLTensor *indptr, const DLTensor *rhs,
+                              DLTensor *out, int64_t n_rows, int64_t n_cols,
+                              void *stream);
+/* csr_matmat, two calls (src/bindings.cpp:1116-1131,
+ * mlx_sparse/_native.py:393-408): the symbolic call fills out_indptr
+ * (int32 when both operands are int32, else int64) and *out_nnz; the numeric
+ * call fills out_data and out_indices (same index dtype as out_indptr). */
+MSX_API int msx_dl_csr_matmat_symbolic(
+    const DLTensor *lhs_data, const DLTensor *lhs_indices,
+    const DLTensor *lhs_indptr, const DLTensor *rhs_data,
+    const DLTensor *rhs_indices, const DLTensor *rhs_indptr, int64_t lhs_n_rows,
+    int64_t lhs_n_cols, int64_t rhs_n_rows, int64_t rhs_n_cols,
+    DLTensor *out_indptr, int64_t *out_nnz, int prune_zeros, void *stream);
+MSX_API int msx_dl_csr_matmat_numeric(
+    const DLTensor *lhs_data, const DLTensor *lhs_indices,
+    const DLTensor *lhs_indptr, const DLTensor *rhs_data,
+    const DLTensor *rhs_indices, const DLTensor *rhs_indptr, int64_t lhs_n_rows,
+    int64_t lhs_n_cols, int64_t rhs_n_rows, int64_t rhs_n_cols,
+    const DLTensor *out_indptr, DLTensor *out_data, DLTensor *out_indices,
+    int prune_zeros, void *stream);
+/* csr_cg / csr_pcg_jacobi (src/bindings.cpp:1133-1161,
+ * mlx_sparse/_native.py:883-909, 1139-1167); scalars as msx_csr_cg. */
+MSX_API int msx_dl_csr_cg(const DLTensor *data, const DLTensor *indices,
+                          const DLTensor *indptr, const DLTensor *b,
+                          const DLTensor *x0, DLTensor *x_out, int64_t n_rows,
+                          int64_t n_cols, float rtol, float atol,
+                          int32_t maxiter, int32_t *info, float *residual,
+                          int32_t *iterations, void *stream);
+MSX_API int msx_dl_csr_pcg_jacobi(const DLTensor *data, const DLTensor *indices,
+                                  const DLTensor *indptr, const DLTensor *b,
+                                  const DLTensor *x0, const DLTensor *inv_diag,
+                                  DLTensor *x_out, int64_t n_rows,
+                                  int64_t n_cols, float rtol, float atol,
+                                  int32_t maxiter, int32_t *info,
+                                  float *residual, int32_t *iterations,
+                                  void *stream);
 
 #ifdef __cplusplus
 }

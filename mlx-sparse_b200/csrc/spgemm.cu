@@ -9,23 +9,32 @@
 // zero (:613-641). Output index dtype: the inputs' when both agree, else int64
 // (:1354-1356); nnz must fit int32 and the index dtype (:478-488).
 //
-// B200 design: two passes (symbolic count, numeric fill) over rows binned by
-// their product count W:
-//   W <= 256     one warp per row: expand the W products into shared memory
-//                with 64-bit keys (column << 32 | position), bitonic-sort them,
-//                then sum each column's run in position order - the reference's
-//                exact accumulation order - and compact with warp ballots;
+// B200 design: one expansion pass over rows binned by their product count W,
+// writing every finished row (sorted, summed, pruned) into a temporary buffer
+// at an upper-bound offset (the prefix sum of W), then a scan of the exact row
+// counts gives indptr; the numeric call of the two-call protocol only copies
+// the rows into the caller's arrays. Rows are processed by
+//   W <= 256     one warp: the row's lhs entries and their rhs row bounds are
+//                read by the lanes in parallel (one round trip), each lane
+//                expands its products with a shuffle search over the prefix of
+//                rhs row lengths, so every gather of the row is in flight at
+//                once; the 64-bit keys (column << 32 | position) are
+//                bitonic-sorted in shared memory and each column's run is
+//                summed in position order - the reference's exact
+//                accumulation order - and compacted with warp ballots;
 //   W <= 4096    the same with one CTA per row;
 //   W  > 4096    one CTA per row over a dense global accumulator (marker +
 //                value per column): lhs entries are applied one after another,
 //                the entries of one rhs row in parallel (rhs rows without
 //                repeated columns) or by one thread (otherwise), then columns
 //                are extracted in ascending order.
-// The symbolic pass computes the exact pruned counts (it must evaluate the
-// values to know which cancel), a device scan builds indptr, and the numeric
-// pass writes each row at its offset. No atomics touch values, so results are
-// deterministic.
+// The symbolic call synchronises twice (the total product count sizes the
+// temporary buffer; the output nnz is returned) and keeps the finished rows
+// for the numeric call on the same thread, which then needs no recomputation
+// (it recomputes only if the cached product does not match its arguments).
+// No atomics touch values, so results are deterministic.
 #include <algorithm>
+#include <memory>
 #include <vector>
 
 #include "common.cuh"
@@ -43,7 +52,7 @@ constexpr int kDenseThreads = 512;
 __device__ __forceinline__ uint32_t key_col(uint64_t k) { return (uint32_t)(k >> 32); }
 __device__ __forceinline__ uint32_t key_seq(uint64_t k) { return (uint32_t)(k & 0xffffffffu); }
 
-// ---- row work and binning ------------------------------------------------------
+// ---- row work, checks and binning --------------------------------------------
 template <typename LI, typename RI>
 __global__ void row_work_kernel(const LI *__restrict__ li, const LI *__restrict__ lp, const RI *__restrict__ rp,
                                 int64_t m, int64_t rhs_rows, int64_t *__restrict__ work, int *__restrict__ err) {
@@ -86,7 +95,7 @@ __global__ void bin_kernel(const int64_t *__restrict__ work, int64_t m, int *__r
   const int64_t w = work[row];
   int bin;
   if (w == 0) {
-    if (row_nnz) row_nnz[row] = 0;
+    row_nnz[row] = 0;
     return;
   } else if (w <= kWarpCap) {
     bin = 0;
@@ -122,18 +131,162 @@ __device__ __forceinline__ void bitonic_sort(uint64_t *key, int len, int tid, in
   }
 }
 
-template <typename T, typename LI, typename RI, typename OutI, bool kWrite, int kCap, bool kWarp>
-struct EscRow {
-  // Processes one row with `nthreads` cooperating threads (a warp or a CTA).
-  __device__ static void run(int64_t row, int tid, int nthreads, uint64_t *key, float *val, int *scratch_cnt,
-                             const T *__restrict__ ld, const LI *__restrict__ li, const LI *__restrict__ lp,
-                             const T *__restrict__ rd, const RI *__restrict__ ri, const RI *__restrict__ rp,
-                             const OutI *__restrict__ out_indptr, OutI *__restrict__ out_idx,
-                             T *__restrict__ out_data, int64_t *__restrict__ row_nnz, bool prune) {
-    auto sync = [&]() {
-      if (kWarp) __syncwarp();
-      else __syncthreads();
-    };
+// Where finished rows go: at the row's upper-bound offset in the temporary
+// arrays (column as int32, value as T); row_nnz receives the exact count.
+template <typename T>
+struct RowSink {
+  const int64_t *off;
+  int *col;
+  T *val;
+  int64_t *row_nnz;
+};
+
+// Sorts the cnt keys (already in shared memory), sums every column's run in
+// position order, prunes exact zeros and writes the row to the sink.
+template <typename T, bool kWarp>
+__device__ void finish_row(int64_t row, int cnt, int tid, int nthreads, uint64_t *key, const float *val,
+                           int *scratch_cnt, RowSink<T> sink, bool prune) {
+  auto sync = [&]() {
+    if (kWarp) __syncwarp();
+    else __syncthreads();
+  };
+  int pw = 1;
+  while (pw < cnt) pw <<= 1;
+  for (int j = cnt + tid; j < pw; j += nthreads) key[j] = ~0ull;
+  sync();
+  bitonic_sort(key, pw, tid, nthreads, sync);
+  const int64_t out0 = sink.off[row];
+  int count = 0;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = (nthreads + 31) >> 5;
+  for (int base = 0; base < cnt; base += nthreads) {
+    const int j = base + tid;
+    bool keep = false;
+    uint32_t col = 0;
+    T out_v{};
+    if (j < cnt) {
+      col = key_col(key[j]);
+      const bool head = (j == 0) || key_col(key[j - 1]) != col;
+      if (head) {
+        float s = val[key_seq(key[j])];
+        for (int t = j + 1; t < cnt && key_col(key[t]) == col; ++t) s = __fadd_rn(s, val[key_seq(key[t])]);
+        out_v = VT<T>::store(s);
+        keep = !prune || VT<T>::load(out_v) != 0.0f;
+      }
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, keep);
+    int pos;
+    if (kWarp) {
+      pos = count + __popc(mask & ((1u << lane) - 1u));
+      count += __popc(mask);
+    } else {
+      if (lane == 0) scratch_cnt[warp] = __popc(mask);
+      __syncthreads();
+      int before = 0, total = 0;
+      for (int w = 0; w < nwarps; ++w) {
+        const int c = scratch_cnt[w];
+        if (w < warp) before += c;
+        total += c;
+      }
+      pos = count + before + __popc(mask & ((1u << lane) - 1u));
+      count += total;
+      __syncthreads();
+    }
+    if (keep) {
+      sink.col[out0 + pos] = (int)col;
+      sink.val[out0 + pos] = out_v;
+    }
+  }
+  if (tid == 0) sink.row_nnz[row] = count;
+  sync();
+}
+
+// One warp per row with W <= kWarpCap products. The lanes read up to 32 lhs
+// entries of the row and their rhs row bounds at once; a warp-wide prefix sum
+// of the rhs row lengths lets every lane find, by a shuffle search, which lhs
+// entry each of its products belongs to, so all the row's rhs gathers are in
+// flight together. Rows with more than 32 lhs entries take the entries in
+// chunks of 32.
+template <typename T, typename LI, typename RI>
+__global__ void __launch_bounds__(kBlockThreads)
+spgemm_warp_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
+                   const T *__restrict__ ld, const LI *__restrict__ li, const LI *__restrict__ lp,
+                   const T *__restrict__ rd, const RI *__restrict__ ri, const RI *__restrict__ rp, RowSink<T> sink,
+                   bool prune) {
+  __shared__ uint64_t keys[kBlockThreads / 32][kWarpCap];
+  __shared__ float vals[kBlockThreads / 32][kWarpCap];
+  if (*flags & 3) return;  // invalid indices: the host reports them
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int count = *count_ptr;
+  uint64_t *key = keys[warp];
+  float *val = vals[warp];
+  for (int w = blockIdx.x * (kBlockThreads / 32) + warp; w < count; w += gridDim.x * (kBlockThreads / 32)) {
+    const int64_t row = list[w];
+    const int64_t q0 = (int64_t)lp[row], q1 = (int64_t)lp[row + 1];
+    int cnt = 0;
+    for (int64_t qc = q0; qc < q1; qc += 32) {
+      const int nq = (int)min((int64_t)32, q1 - qc);
+      int64_t rb = 0;
+      int len = 0;
+      float lv = 0.f;
+      if (lane < nq) {
+        const int64_t k = (int64_t)li[qc + lane];
+        lv = VT<T>::load(ld[qc + lane]);
+        rb = (int64_t)rp[k];
+        len = (int)((int64_t)rp[k + 1] - rb);
+      }
+      int incl = len;  // inclusive prefix of the lengths over the lanes
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int chunk = __shfl_sync(0xffffffffu, incl, 31);
+      // all lanes run every round (the shuffles need the full warp)
+      for (int base = 0; base < chunk; base += 32) {
+        const int s = base + lane;
+        // e = number of entries whose inclusive prefix is <= s, i.e. the
+        // entry product s belongs to (binary lifting over the lanes)
+        int e = 0;
+#pragma unroll
+        for (int b = 16; b > 0; b >>= 1) {
+          const int v = __shfl_sync(0xffffffffu, incl, (e + b - 1) & 31);
+          if (e + b <= nq && v <= s) e += b;
+        }
+        const int ev = e & 31;
+        const int excl = __shfl_sync(0xffffffffu, incl, ev) - __shfl_sync(0xffffffffu, len, ev);
+        const int64_t erb = __shfl_sync(0xffffffffu, rb, ev);
+        const float elv = __shfl_sync(0xffffffffu, lv, ev);
+        if (s < chunk) {
+          const int64_t src = erb + (s - excl);
+          const int pos = cnt + s;
+          key[pos] = ((uint64_t)(uint32_t)ri[src] << 32) | (uint32_t)pos;
+          val[pos] = __fmul_rn(elv, VT<T>::load(rd[src]));
+        }
+      }
+      cnt += chunk;
+    }
+    __syncwarp();
+    finish_row<T, true>(row, cnt, lane, 32, key, val, nullptr, sink, prune);
+  }
+}
+
+template <typename T, typename LI, typename RI>
+__global__ void __launch_bounds__(kBlockThreads)
+spgemm_block_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
+                    const T *__restrict__ ld, const LI *__restrict__ li, const LI *__restrict__ lp,
+                    const T *__restrict__ rd, const RI *__restrict__ ri, const RI *__restrict__ rp, RowSink<T> sink,
+                    bool prune) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  uint64_t *key = reinterpret_cast<uint64_t *>(dyn);
+  float *val = reinterpret_cast<float *>(key + kBlockCap);
+  __shared__ int cnt_s[kBlockThreads / 32];
+  if (*flags & 3) return;
+  const int count = *count_ptr;
+  const int tid = threadIdx.x;
+  for (int b = blockIdx.x; b < count; b += gridDim.x) {
+    const int64_t row = list[b];
     // expand in (lhs position, rhs position) order
     int cnt = 0;
     for (int64_t q = (int64_t)lp[row]; q < (int64_t)lp[row + 1]; ++q) {
@@ -141,114 +294,28 @@ struct EscRow {
       const float lv = VT<T>::load(ld[q]);
       const int64_t rb = (int64_t)rp[k];
       const int len = (int)((int64_t)rp[k + 1] - rb);
-      for (int j = tid; j < len; j += nthreads) {
+      for (int j = tid; j < len; j += kBlockThreads) {
         const int s = cnt + j;
         key[s] = ((uint64_t)(uint32_t)ri[rb + j] << 32) | (uint32_t)s;
         val[s] = __fmul_rn(lv, VT<T>::load(rd[rb + j]));
       }
       cnt += len;
     }
-    int pw = 1;
-    while (pw < cnt) pw <<= 1;
-    for (int j = cnt + tid; j < pw; j += nthreads) key[j] = ~0ull;
-    sync();
-    bitonic_sort(key, pw, tid, nthreads, sync);
-    // sum runs in position order and compact
-    const int64_t out0 = kWrite ? (int64_t)out_indptr[row] : 0;
-    int count = 0;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    const int nwarps = (nthreads + 31) >> 5;
-    for (int base = 0; base < cnt; base += nthreads) {
-      const int j = base + tid;
-      bool keep = false;
-      uint32_t col = 0;
-      T out_v{};
-      if (j < cnt) {
-        col = key_col(key[j]);
-        const bool head = (j == 0) || key_col(key[j - 1]) != col;
-        if (head) {
-          float s = val[key_seq(key[j])];
-          for (int t = j + 1; t < cnt && key_col(key[t]) == col; ++t) s = __fadd_rn(s, val[key_seq(key[t])]);
-          out_v = VT<T>::store(s);
-          keep = !prune || VT<T>::load(out_v) != 0.0f;
-        }
-      }
-      const unsigned mask = __ballot_sync(0xffffffffu, keep);
-      int pos;
-      if (kWarp) {
-        pos = count + __popc(mask & ((1u << lane) - 1u));
-        count += __popc(mask);
-      } else {
-        // block-wide exclusive count over warps in order
-        if (lane == 0) scratch_cnt[warp] = __popc(mask);
-        __syncthreads();
-        int before = 0, total = 0;
-        for (int w = 0; w < nwarps; ++w) {
-          const int c = scratch_cnt[w];
-          if (w < warp) before += c;
-          total += c;
-        }
-        pos = count + before + __popc(mask & ((1u << lane) - 1u));
-        count += total;
-        __syncthreads();
-      }
-      if (kWrite && keep) {
-        out_idx[out0 + pos] = (OutI)col;
-        out_data[out0 + pos] = out_v;
-      }
-    }
-    if (!kWrite && tid == 0) row_nnz[row] = count;
-    sync();
-  }
-};
-
-template <typename T, typename LI, typename RI, typename OutI, bool kWrite>
-__global__ void __launch_bounds__(kBlockThreads)
-spgemm_warp_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const T *__restrict__ ld,
-                   const LI *__restrict__ li, const LI *__restrict__ lp, const T *__restrict__ rd,
-                   const RI *__restrict__ ri, const RI *__restrict__ rp, const OutI *__restrict__ out_indptr,
-                   OutI *__restrict__ out_idx, T *__restrict__ out_data, int64_t *__restrict__ row_nnz, bool prune) {
-  __shared__ uint64_t keys[kBlockThreads / 32][kWarpCap];
-  __shared__ float vals[kBlockThreads / 32][kWarpCap];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int count = *count_ptr;
-  for (int w = blockIdx.x * (kBlockThreads / 32) + warp; w < count; w += gridDim.x * (kBlockThreads / 32)) {
-    EscRow<T, LI, RI, OutI, kWrite, kWarpCap, true>::run(list[w], lane, 32, keys[warp], vals[warp], nullptr, ld, li,
-                                                         lp, rd, ri, rp, out_indptr, out_idx, out_data, row_nnz,
-                                                         prune);
-  }
-}
-
-template <typename T, typename LI, typename RI, typename OutI, bool kWrite>
-__global__ void __launch_bounds__(kBlockThreads)
-spgemm_block_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const T *__restrict__ ld,
-                    const LI *__restrict__ li, const LI *__restrict__ lp, const T *__restrict__ rd,
-                    const RI *__restrict__ ri, const RI *__restrict__ rp, const OutI *__restrict__ out_indptr,
-                    OutI *__restrict__ out_idx, T *__restrict__ out_data, int64_t *__restrict__ row_nnz,
-                    bool prune) {
-  extern __shared__ __align__(16) unsigned char dyn[];
-  uint64_t *keys = reinterpret_cast<uint64_t *>(dyn);
-  float *vals = reinterpret_cast<float *>(keys + kBlockCap);
-  __shared__ int cnt[kBlockThreads / 32];
-  const int count = *count_ptr;
-  for (int b = blockIdx.x; b < count; b += gridDim.x) {
-    EscRow<T, LI, RI, OutI, kWrite, kBlockCap, false>::run(list[b], threadIdx.x, kBlockThreads, keys, vals, cnt,
-                                                           ld, li, lp, rd, ri, rp, out_indptr, out_idx, out_data,
-                                                           row_nnz, prune);
+    __syncthreads();
+    finish_row<T, false>(row, cnt, tid, kBlockThreads, key, val, cnt_s, sink, prune);
   }
 }
 
 // Rows with more than kBlockCap products: dense per-CTA accumulator slot.
-template <typename T, typename LI, typename RI, typename OutI, bool kWrite>
+template <typename T, typename LI, typename RI>
 __global__ void __launch_bounds__(kDenseThreads)
 spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const T *__restrict__ ld,
                     const LI *__restrict__ li, const LI *__restrict__ lp, const T *__restrict__ rd,
                     const RI *__restrict__ ri, const RI *__restrict__ rp, int64_t n_cols,
                     int *__restrict__ marker_base, float *__restrict__ accum_base, const int *__restrict__ flags,
-                    const OutI *__restrict__ out_indptr, OutI *__restrict__ out_idx, T *__restrict__ out_data,
-                    int64_t *__restrict__ row_nnz, bool prune) {
+                    RowSink<T> sink, bool prune) {
   __shared__ int wcnt[kDenseThreads / 32];
+  if (*flags & 3) return;
   int *marker = marker_base + (int64_t)blockIdx.x * n_cols;
   float *accum = accum_base + (int64_t)blockIdx.x * n_cols;
   const bool parallel_rhs = ((*flags) & 4) == 0;  // rhs rows have no repeated columns
@@ -286,7 +353,7 @@ spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_
       __syncthreads();
     }
     // ordered extraction
-    const int64_t out0 = kWrite ? (int64_t)out_indptr[row] : 0;
+    const int64_t out0 = sink.off[row];
     int64_t written = 0;
     for (int64_t base = 0; base < n_cols; base += kDenseThreads) {
       const int64_t c = base + tid;
@@ -304,22 +371,37 @@ spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_
         if (w < warp) before += wcnt[w];
         total += wcnt[w];
       }
-      if (kWrite && keep) {
+      if (keep) {
         const int64_t pos = out0 + written + before + __popc(mask & ((1u << lane) - 1u));
-        out_idx[pos] = (OutI)c;
-        out_data[pos] = v;
+        sink.col[pos] = (int)c;
+        sink.val[pos] = v;
       }
       written += total;
       __syncthreads();
     }
-    if (!kWrite && tid == 0) row_nnz[row] = written;
+    if (tid == 0) sink.row_nnz[row] = written;
     __syncthreads();
   }
 }
 
-struct Bins {
-  int counts[3];
-};
+// Copies every finished row from its upper-bound slot to its final place.
+// One warp per row; lanes copy consecutive entries.
+template <typename T, typename OutI>
+__global__ void copy_rows_kernel(const int64_t *__restrict__ off, const int64_t *__restrict__ row_nnz,
+                                 const int *__restrict__ col, const T *__restrict__ val, int64_t m,
+                                 const OutI *__restrict__ out_indptr, OutI *__restrict__ out_idx,
+                                 T *__restrict__ out_data) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < m; row += warps) {
+    const int64_t n = row_nnz[row];
+    const int64_t src = off[row], dst = (int64_t)out_indptr[row];
+    for (int64_t j = lane; j < n; j += 32) {
+      out_idx[dst + j] = (OutI)col[src + j];
+      out_data[dst + j] = val[src + j];
+    }
+  }
+}
 
 int dense_slots(int64_t n_cols) {
   const int64_t budget = (int64_t)256 << 20;
@@ -328,105 +410,180 @@ int dense_slots(int64_t n_cols) {
   return (int)slots;
 }
 
-template <typename T, typename LI, typename RI, typename OutI>
-void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *rd, const RI *ri, const RI *rp,
-                 int64_t m, int64_t rhs_rows, int64_t n_cols, OutI *out_indptr, OutI *out_idx, T *out_data,
-                 int64_t *out_nnz, bool prune, cudaStream_t s) {
-  if (m == 0) {
-    if (!write) {
-      OutI zero = 0;
-      MSX_CUDA(cudaMemcpyAsync(out_indptr, &zero, sizeof(OutI), cudaMemcpyHostToDevice, s));
-      MSX_CUDA(cudaStreamSynchronize(s));
-      *out_nnz = 0;
-    }
-    return;
+// Finished rows of one product (device memory from the stream-ordered pool).
+struct Product {
+  // what was multiplied
+  const void *ptrs[6] = {};
+  int64_t m = 0, rhs_rows = 0, n_cols = 0;
+  int types[4] = {};
+  bool prune = false;
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  // results
+  void *mem = nullptr;
+  int64_t *off = nullptr, *row_nnz = nullptr;
+  int *col = nullptr;
+  void *val = nullptr;
+  int64_t nnz = 0;
+  ~Product() {
+    if (mem) cudaFreeAsync(mem, stream);
   }
+  bool same(const Product &o) const {
+    for (int i = 0; i < 6; ++i)
+      if (ptrs[i] != o.ptrs[i]) return false;
+    for (int i = 0; i < 4; ++i)
+      if (types[i] != o.types[i]) return false;
+    return m == o.m && rhs_rows == o.rhs_rows && n_cols == o.n_cols && prune == o.prune && device == o.device &&
+           stream == o.stream;
+  }
+};
+
+// The finished rows of this thread's last symbolic call, for its numeric call.
+thread_local std::unique_ptr<Product> g_last_product;
+
+// Expands, sorts and sums every row into a new Product; synchronises `s`
+// twice (total product count, output nnz) and validates the indices.
+template <typename T, typename LI, typename RI, typename OutI>
+std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld, const LI *li, const LI *lp,
+                                         const T *rd, const RI *ri, const RI *rp, OutI *out_indptr,
+                                         cudaStream_t s) {
+  const int64_t m = P->m, rhs_rows = P->rhs_rows, n_cols = P->n_cols;
+  const bool prune = P->prune;
   const int slots = dense_slots(n_cols);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
-  const int64_t nb = ceil_div(m, kScanThreads);
+  const int64_t n_sums = scan_scratch_elems(m);
   size_t off = 0;
   const size_t o_work = off; off += al(sizeof(int64_t) * m);
-  const size_t o_rownnz = off; off += al(sizeof(int64_t) * m);
   const size_t o_lists = off; off += al(sizeof(int) * 3 * m);
   const size_t o_counts = off; off += al(sizeof(int) * 8);
-  const size_t o_sums = off; off += al(sizeof(int64_t) * (nb + 1));
-  const size_t o_marker = off; off += al(sizeof(int) * (size_t)slots * n_cols);
-  const size_t o_accum = off; off += al(sizeof(float) * (size_t)slots * n_cols);
+  const size_t o_sums = off; off += al(sizeof(int64_t) * n_sums);
   Scratch scratch(off, s);
   char *base = scratch.as<char>();
   int64_t *work = reinterpret_cast<int64_t *>(base + o_work);
-  int64_t *row_nnz = reinterpret_cast<int64_t *>(base + o_rownnz);
   int *lists = reinterpret_cast<int *>(base + o_lists);
   int *counts = reinterpret_cast<int *>(base + o_counts);  // [0..2] bins, [3] flags
   int64_t *sums = reinterpret_cast<int64_t *>(base + o_sums);
-  int *marker = reinterpret_cast<int *>(base + o_marker);
-  float *accum = reinterpret_cast<float *>(base + o_accum);
   int *flags = counts + 3;
 
+  // the product's own memory: offsets (m + 1), exact counts (m), then the
+  // rows' columns and values at the offsets (sized after the first sync)
   MSX_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * 8, s));
   const int t = 256;
+  size_t head = al(sizeof(int64_t) * (m + 1)) + al(sizeof(int64_t) * m);
+  Scratch head_mem(head, s);
+  int64_t *row_off = head_mem.as<int64_t>();
+  int64_t *row_nnz = reinterpret_cast<int64_t *>(head_mem.as<char>() + al(sizeof(int64_t) * (m + 1)));
   row_work_kernel<LI, RI><<<(unsigned)ceil_div(m, t), t, 0, s>>>(li, lp, rp, m, rhs_rows, work, flags);
   if (rhs_rows > 0)
     rhs_check_kernel<RI><<<(unsigned)ceil_div(rhs_rows, t), t, 0, s>>>(ri, rp, rhs_rows, n_cols, flags);
   bin_kernel<<<(unsigned)ceil_div(m, t), t, 0, s>>>(work, m, lists, counts, row_nnz);
   MSX_CHECK_LAUNCH();
-  int host_counts[4];
-  MSX_CUDA(cudaMemcpyAsync(host_counts, counts, sizeof(host_counts), cudaMemcpyDeviceToHost, s));
+  scan_counts_to_indptr<int64_t>(work, m, row_off, sums, s);
+  struct {
+    int counts[4];
+    int64_t total;
+  } h{};
+  MSX_CUDA(cudaMemcpyAsync(h.counts, counts, sizeof(h.counts), cudaMemcpyDeviceToHost, s));
+  MSX_CUDA(cudaMemcpyAsync(&h.total, sums + n_sums - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
-  if (host_counts[3] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
-  if (host_counts[3] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
+  if (h.counts[3] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
+  if (h.counts[3] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
+  const int64_t total = h.total;
+
+  const size_t o_col = 0;
+  size_t bytes = al(sizeof(int) * std::max<int64_t>(total, 1));
+  const size_t o_val = bytes;
+  bytes += al(sizeof(T) * std::max<int64_t>(total, 1));
+  const size_t o_head = bytes;
+  bytes += head;
+  MSX_CUDA(cudaMallocAsync(&P->mem, bytes, s));
+  char *pm = static_cast<char *>(P->mem);
+  P->col = reinterpret_cast<int *>(pm + o_col);
+  P->val = pm + o_val;
+  P->off = reinterpret_cast<int64_t *>(pm + o_head);
+  P->row_nnz = reinterpret_cast<int64_t *>(pm + o_head + al(sizeof(int64_t) * (m + 1)));
+  MSX_CUDA(cudaMemcpyAsync(P->off, row_off, head, cudaMemcpyDeviceToDevice, s));
+  RowSink<T> sink{P->off, P->col, static_cast<T *>(P->val), P->row_nnz};
 
   const int sms = num_sms();
-  if (host_counts[0] > 0) {
-    const int warps_per_block = kBlockThreads / 32;
-    const int grid = (int)std::min<int64_t>(ceil_div(host_counts[0], warps_per_block), (int64_t)sms * 8);
-    if (write)
-      spgemm_warp_kernel<T, LI, RI, OutI, true><<<grid, kBlockThreads, 0, s>>>(
-          lists, counts + 0, ld, li, lp, rd, ri, rp, out_indptr, out_idx, out_data, row_nnz, prune);
-    else
-      spgemm_warp_kernel<T, LI, RI, OutI, false><<<grid, kBlockThreads, 0, s>>>(
-          lists, counts + 0, ld, li, lp, rd, ri, rp, out_indptr, out_idx, out_data, row_nnz, prune);
+  if (h.counts[0] > 0) {
+    const int wpb = kBlockThreads / 32;
+    const int grid = (int)std::min<int64_t>(ceil_div(h.counts[0], wpb), (int64_t)sms * 8);
+    spgemm_warp_kernel<T, LI, RI><<<grid, kBlockThreads, 0, s>>>(lists, counts + 0, flags, ld, li, lp, rd, ri, rp,
+                                                                  sink, prune);
     MSX_CHECK_LAUNCH();
   }
-  if (host_counts[1] > 0) {
+  if (h.counts[1] > 0) {
     const size_t smem = (size_t)kBlockCap * (sizeof(uint64_t) + sizeof(float));
-    const int grid = (int)std::min<int64_t>(host_counts[1], (int64_t)sms * 4);
-    if (write) {
-      auto kern = spgemm_block_kernel<T, LI, RI, OutI, true>;
-      MSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      kern<<<grid, kBlockThreads, smem, s>>>(lists + m, counts + 1, ld, li, lp, rd, ri, rp, out_indptr, out_idx,
-                                             out_data, row_nnz, prune);
-    } else {
-      auto kern = spgemm_block_kernel<T, LI, RI, OutI, false>;
-      MSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      kern<<<grid, kBlockThreads, smem, s>>>(lists + m, counts + 1, ld, li, lp, rd, ri, rp, out_indptr, out_idx,
-                                             out_data, row_nnz, prune);
-    }
+    const int grid = (int)std::min<int64_t>(h.counts[1], (int64_t)sms * 4);
+    auto kern = spgemm_block_kernel<T, LI, RI>;
+    MSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, kBlockThreads, smem, s>>>(lists + m, counts + 1, flags, ld, li, lp, rd, ri, rp, sink, prune);
     MSX_CHECK_LAUNCH();
   }
-  if (host_counts[2] > 0) {
+  if (h.counts[2] > 0) {
+    Scratch dense((sizeof(int) + sizeof(float)) * (size_t)slots * n_cols, s);
+    int *marker = dense.as<int>();
+    float *accum = reinterpret_cast<float *>(marker + (size_t)slots * n_cols);
     MSX_CUDA(cudaMemsetAsync(marker, 0xff, sizeof(int) * (size_t)slots * n_cols, s));
-    const int grid = std::min(host_counts[2], slots);
-    if (write)
-      spgemm_dense_kernel<T, LI, RI, OutI, true><<<grid, kDenseThreads, 0, s>>>(
-          lists + 2 * m, counts + 2, ld, li, lp, rd, ri, rp, n_cols, marker, accum, flags, out_indptr, out_idx,
-          out_data, row_nnz, prune);
-    else
-      spgemm_dense_kernel<T, LI, RI, OutI, false><<<grid, kDenseThreads, 0, s>>>(
-          lists + 2 * m, counts + 2, ld, li, lp, rd, ri, rp, n_cols, marker, accum, flags, out_indptr, out_idx,
-          out_data, row_nnz, prune);
+    const int grid = std::min(h.counts[2], slots);
+    spgemm_dense_kernel<T, LI, RI><<<grid, kDenseThreads, 0, s>>>(lists + 2 * m, counts + 2, ld, li, lp, rd, ri, rp,
+                                                                   n_cols, marker, accum, flags, sink, prune);
     MSX_CHECK_LAUNCH();
   }
-  if (write) return;
+  if (out_indptr) {
+    scan_counts_to_indptr<OutI>(P->row_nnz, m, out_indptr, sums, s);
+    MSX_CUDA(cudaMemcpyAsync(&P->nnz, sums + n_sums - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    MSX_CUDA(cudaStreamSynchronize(s));
+  }
+  return P;
+}
 
-  scan_counts_to_indptr<OutI>(row_nnz, m, out_indptr, sums, s);
-  int64_t total = 0;
-  MSX_CUDA(cudaMemcpyAsync(&total, sums + nb, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
-  MSX_CUDA(cudaStreamSynchronize(s));
-  if (total > (int64_t)INT32_MAX) fail(MSX_ERR_OVERFLOW, "csr_matmat output nnz exceeds MLX shape limits.");
-  if (sizeof(OutI) == 4 && total > (int64_t)INT32_MAX)
-    fail(MSX_ERR_OVERFLOW, "csr_matmat output nnz exceeds index dtype capacity.");
-  *out_nnz = total;
+template <typename T, typename LI, typename RI, typename OutI>
+void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *rd, const RI *ri, const RI *rp,
+                 int64_t m, int64_t rhs_rows, int64_t n_cols, const int types[4], OutI *out_indptr, OutI *out_idx,
+                 T *out_data, int64_t *out_nnz, bool prune, cudaStream_t s) {
+  if (m == 0) {
+    if (!write) {
+      MSX_CUDA(cudaMemsetAsync(out_indptr, 0, sizeof(OutI), s));
+      MSX_CUDA(cudaStreamSynchronize(s));
+      *out_nnz = 0;
+    }
+    return;
+  }
+  auto key = std::make_unique<Product>();
+  const void *ptrs[6] = {ld, li, lp, rd, ri, rp};
+  for (int i = 0; i < 6; ++i) key->ptrs[i] = ptrs[i];
+  for (int i = 0; i < 4; ++i) key->types[i] = types[i];
+  key->m = m;
+  key->rhs_rows = rhs_rows;
+  key->n_cols = n_cols;
+  key->prune = prune;
+  key->stream = s;
+  MSX_CUDA(cudaGetDevice(&key->device));
+  if (!write) {
+    g_last_product.reset();
+    auto P = compute_product<T, LI, RI, OutI>(std::move(key), ld, li, lp, rd, ri, rp, out_indptr, s);
+    const int64_t total = P->nnz;
+    if (total > (int64_t)INT32_MAX) fail(MSX_ERR_OVERFLOW, "csr_matmat output nnz exceeds MLX shape limits.");
+    if (sizeof(OutI) == 4 && total > (int64_t)INT32_MAX)
+      fail(MSX_ERR_OVERFLOW, "csr_matmat output nnz exceeds index dtype capacity.");
+    *out_nnz = total;
+    g_last_product = std::move(P);
+    return;
+  }
+  std::unique_ptr<Product> P;
+  if (g_last_product && g_last_product->same(*key)) {
+    P = std::move(g_last_product);
+  } else {
+    // not the product the last symbolic call computed: recompute its rows
+    // (the caller's indptr already holds the output layout)
+    P = compute_product<T, LI, RI, OutI>(std::move(key), ld, li, lp, rd, ri, rp, nullptr, s);
+  }
+  const int grid = (int)std::min<int64_t>(ceil_div(m, 8), (int64_t)num_sms() * 16);
+  copy_rows_kernel<T, OutI><<<grid, 256, 0, s>>>(P->off, P->row_nnz, P->col, static_cast<const T *>(P->val), m,
+                                                 out_indptr, out_idx, out_data);
+  MSX_CHECK_LAUNCH();
 }
 
 }  // namespace
@@ -435,6 +592,7 @@ void spgemm_run(bool write, int value_dtype, int lhs_it, const void *ld, const v
                 const void *rd, const void *ri, const void *rp, int64_t m, int64_t rhs_rows, int64_t n_cols,
                 int out_it, void *out_indptr, void *out_idx, void *out_data, int64_t *out_nnz, bool prune,
                 cudaStream_t s) {
+  const int types[4] = {value_dtype, lhs_it, rhs_it, out_it};
   dispatch_value(value_dtype, [&](auto vt) {
     using T = decltype(vt);
     dispatch_index(lhs_it, [&](auto a) {
@@ -446,7 +604,7 @@ void spgemm_run(bool write, int value_dtype, int lhs_it, const void *ld, const v
           spgemm_pass<T, LI, RI, OutI>(write, static_cast<const T *>(ld), static_cast<const LI *>(li),
                                        static_cast<const LI *>(lp), static_cast<const T *>(rd),
                                        static_cast<const RI *>(ri), static_cast<const RI *>(rp), m, rhs_rows,
-                                       n_cols, static_cast<OutI *>(out_indptr), static_cast<OutI *>(out_idx),
+                                       n_cols, types, static_cast<OutI *>(out_indptr), static_cast<OutI *>(out_idx),
                                        static_cast<T *>(out_data), out_nnz, prune, s);
         });
       });

@@ -212,7 +212,8 @@ __global__ void spmv_long_fixup_kernel(const int *__restrict__ rows, BinInfo inf
 // Every row has at most 8 nonzeros and the row list is the identity (stencil
 // matrices such as the 2D Laplacian and 3D Poisson operators). A CTA takes 256
 // consecutive rows: it copies their row offsets and then their contiguous
-// nonzero range into shared memory with cp.async (4/8-byte async copies, so the
+// nonzero range into shared memory with cp.async (16-byte copies of the range's
+// aligned window - 4x fewer copy instructions than per-element copies - so the
 // loads in flight hold no registers and 8 CTAs fit an SM), then each thread
 // sums its row left to right - the reference's order - with every x gather of
 // the row issued at once.
@@ -235,13 +236,43 @@ __device__ __forceinline__ void stage_elem(V *dst, const V *src) {
 
 constexpr int kShortRowsPerBlock = 256;
 
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+// Stages elements [k0, k0 + K) of `src` (an array of `total` elements) into
+// shared memory `dst` (16-byte aligned, room for K + 16 / sizeof(V) - 1
+// elements) with 16-byte cp.async copies: the copied window starts at the
+// 16-byte boundary at or below k0, so element k0 + e lands at
+// dst[e + shift]; returns shift. Chunks that would read past the array's end
+// (or start before its beginning) are copied element by element.
+template <typename V>
+__device__ __forceinline__ int stage_range16(V *dst, const V *src, int64_t k0, int K, int64_t total, int tid,
+                                             int nthreads) {
+  constexpr int kPer = 16 / (int)sizeof(V);
+  const int shift = (int)(((reinterpret_cast<uintptr_t>(src + k0)) & 15u) / sizeof(V));
+  const int64_t w0 = k0 - shift;  // first element of the window (16-byte aligned)
+  const int chunks = (shift + K + kPer - 1) / kPer;
+  for (int c = tid; c < chunks; c += nthreads) {
+    const int64_t g = w0 + (int64_t)c * kPer;
+    if (g >= 0 && g + kPer <= total) {
+      cp_async_16(dst + c * kPer, src + g);
+    } else {  // the window would start before the array or end past it
+      for (int u = 0; u < kPer; ++u)
+        if (g + u >= k0 && g + u < k0 + K) stage_elem(dst + c * kPer + u, src + g + u);
+    }
+  }
+  return shift;
+}
+
 template <typename T, typename I, typename Epi>
 __global__ void __launch_bounds__(kShortRowsPerBlock, Epi::kMinBlocks)
 spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
-                  const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
+                  const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, int64_t nnz, Epi epi) {
   __shared__ I ptr_s[kShortRowsPerBlock + 1];
-  __shared__ I idx_s[kShortRowsPerBlock * 8];
-  __shared__ T val_s[kShortRowsPerBlock * 8];
+  __shared__ __align__(16) I idx_s[kShortRowsPerBlock * 8 + 16 / sizeof(I)];
+  __shared__ __align__(16) T val_s[kShortRowsPerBlock * 8 + 16 / sizeof(T)];
   pdl_wait();
   pdl_trigger();
   if (epi.skip()) return;
@@ -257,14 +288,8 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
     __syncthreads();
     const int64_t k0 = (int64_t)ptr_s[0];
     const int K = (int)((int64_t)ptr_s[nr] - k0);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int e = tid + q * kShortRowsPerBlock;
-      if (e < K) {
-        stage_elem(&idx_s[e], indices + k0 + e);
-        stage_elem(&val_s[e], data + k0 + e);
-      }
-    }
+    const int si = stage_range16(idx_s, indices, k0, K, nnz, tid, kShortRowsPerBlock);
+    const int sv = stage_range16(val_s, data, k0, K, nnz, tid, kShortRowsPerBlock);
     cp_async_wait_all();
     __syncthreads();
     if (tid < nr) {
@@ -274,7 +299,7 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (q0 + u < q1) {
-          const I c = idx_s[q0 + u];
+          const I c = idx_s[si + q0 + u];
           if constexpr (Epi::kHalo)
             xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
           else
@@ -283,7 +308,7 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[q0 + u]), xv[u]));
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[sv + q0 + u]), xv[u]));
       const T out = VT<T>::store(acc);
       y[r0 + tid] = out;
       epi.row(r0 + tid, VT<T>::load(out));
@@ -302,22 +327,25 @@ template <typename I>
 constexpr size_t short_ptr_bytes() {
   return ((3 * (kShortRowsPerBlock + 1) * sizeof(I)) + 15) & ~size_t(15);
 }
+// nonzero buffers hold a block's range plus the alignment shift (one 16-byte chunk)
+template <typename V>
+constexpr int kShortBufElems = kShortRowsPerBlock * 8 + 16 / (int)sizeof(V);
 template <typename T, typename I>
 constexpr size_t short_pipe_smem_bytes() {
-  return short_ptr_bytes<I>() + 2 * kShortRowsPerBlock * 8 * (sizeof(I) + sizeof(T));
+  return short_ptr_bytes<I>() + 2 * (size_t)kShortBufElems<I> * sizeof(I) + 2 * (size_t)kShortBufElems<T> * sizeof(T);
 }
 
 template <typename T, typename I, typename Epi>
 __global__ void __launch_bounds__(kShortRowsPerBlock)
 spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
-                       const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, Epi epi) {
+                       const T *__restrict__ x, T *__restrict__ y, int64_t n_rows, int64_t nnz, Epi epi) {
   extern __shared__ __align__(16) unsigned char short_smem[];
   using PtrBuf = I[kShortRowsPerBlock + 1];
-  using IdxBuf = I[kShortRowsPerBlock * 8];
-  using ValBuf = T[kShortRowsPerBlock * 8];
+  constexpr int kIdxElems = kShortRowsPerBlock * 8 + 16 / (int)sizeof(I);
+  constexpr int kValElems = kShortRowsPerBlock * 8 + 16 / (int)sizeof(T);
   PtrBuf *ptr_s = reinterpret_cast<PtrBuf *>(short_smem);
-  IdxBuf *idx_s = reinterpret_cast<IdxBuf *>(short_smem + short_ptr_bytes<I>());
-  ValBuf *val_s = reinterpret_cast<ValBuf *>(short_smem + short_ptr_bytes<I>() + 2 * sizeof(IdxBuf));
+  I *idx_base = reinterpret_cast<I *>(short_smem + short_ptr_bytes<I>());
+  T *val_base = reinterpret_cast<T *>(short_smem + short_ptr_bytes<I>() + 2 * sizeof(I) * kIdxElems);
   pdl_wait();
   pdl_trigger();
   if (epi.skip()) return;
@@ -337,14 +365,8 @@ spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices
     const int nr = rows_of(blk);
     const int64_t k0 = (int64_t)ptr_s[pbuf][0];
     const int K = (int)((int64_t)ptr_s[pbuf][nr] - k0);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int e = tid + q * kShortRowsPerBlock;
-      if (e < K) {
-        stage_elem(&idx_s[dbuf][e], indices + k0 + e);
-        stage_elem(&val_s[dbuf][e], data + k0 + e);
-      }
-    }
+    stage_range16(idx_base + dbuf * kIdxElems, indices, k0, K, nnz, tid, kShortRowsPerBlock);
+    stage_range16(val_base + dbuf * kValElems, data, k0, K, nnz, tid, kShortRowsPerBlock);
   };
   const int64_t G = gridDim.x;
   int64_t blk = blockIdx.x;
@@ -363,13 +385,16 @@ spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices
     const int nr = rows_of(blk);
     if (tid < nr) {
       const int64_t k0 = (int64_t)ptr_s[pc][0];
+      // the same alignment shifts stage_range16 used for this block
+      const int si = (int)(((reinterpret_cast<uintptr_t>(indices + k0)) & 15u) / sizeof(I));
+      const int sv = (int)(((reinterpret_cast<uintptr_t>(data + k0)) & 15u) / sizeof(T));
       const int q0 = (int)((int64_t)ptr_s[pc][tid] - k0);
       const int q1 = (int)((int64_t)ptr_s[pc][tid + 1] - k0);
       float xv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (q0 + u < q1) {
-          const I c = idx_s[dc][q0 + u];
+          const I c = idx_base[dc * kIdxElems + si + q0 + u];
           if constexpr (Epi::kHalo)
             xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
           else
@@ -378,7 +403,7 @@ spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_s[dc][q0 + u]), xv[u]));
+        if (q0 + u < q1) acc = add_rn(acc, mul_rn(VT<T>::load(val_base[dc * kValElems + sv + q0 + u]), xv[u]));
       const T out = VT<T>::store(acc);
       y[r0 + tid] = out;
       epi.row(r0 + tid, VT<T>::load(out));
@@ -464,10 +489,10 @@ void launch_spmv_binned(const BinnedPlan &plan, const T *data, const I *indices,
   if (short_rows_plan(plan)) {
     if (short_launch<T, I, Epi>(plan.n_rows).pipe)
       launch(spmv_short_pipe_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock),
-             short_pipe_smem_bytes<T, I>(), stream, pdl, data, indices, indptr, x, y, plan.n_rows, epi);
+             short_pipe_smem_bytes<T, I>(), stream, pdl, data, indices, indptr, x, y, plan.n_rows, plan.nnz, epi);
     else
       launch(spmv_short_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kShortRowsPerBlock), 0, stream, pdl, data,
-             indices, indptr, x, y, plan.n_rows, epi);
+             indices, indptr, x, y, plan.n_rows, plan.nnz, epi);
     return;
   }
   launch(spmv_binned_kernel<T, I, Epi>, dim3((unsigned)grid), dim3(kBinThreads), 0, stream, pdl, data, indices, indptr,

@@ -3,8 +3,11 @@
 Mirrors mlx-sparse's ``mlx_sparse/_native.py`` (csr_matvec :179-189, csr_matmul
 :286-296, csr_matmat :393-408, csr_cg :883-909, csr_pcg_jacobi :1139-1167):
 same function names and argument meaning, torch CUDA tensors in place of MLX
-arrays. There is no CPU fallback: if the library or a CUDA device is missing,
-every op raises ``RuntimeError``.
+arrays. Those five cross the boundary as DLPack tensors (``msx_dl_*``: each
+argument is the ``DLTensor`` of a ``torch.utils.dlpack`` capsule, kept alive
+for the call), as the reference hands device arrays to its native module; the
+other entry points take raw device pointers. There is no CPU fallback: if the
+library or a CUDA device is missing, every op raises ``RuntimeError``.
 """
 
 from __future__ import annotations
@@ -14,6 +17,7 @@ import os
 import threading
 
 import torch
+from torch.utils.dlpack import to_dlpack
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libmsx_b200.so")
@@ -87,6 +91,13 @@ def extension():
         L.msx_cg_context_connect.argtypes = [p, p, i64]
         L.msx_cg_context_solve.argtypes = [p, p, p, p, p, c_float, c_float, ctypes.c_int32, p, p, p, p]
         L.msx_cg_context_destroy.argtypes = [p]
+        dl = [p, p, p, p, p]
+        L.msx_dl_csr_matvec.argtypes = dl + [i64, i64, p, p]
+        L.msx_dl_csr_matmul.argtypes = dl + [i64, i64, p]
+        L.msx_dl_csr_matmat_symbolic.argtypes = [p] * 6 + [i64] * 4 + [p, ctypes.POINTER(i64), c_int, p]
+        L.msx_dl_csr_matmat_numeric.argtypes = [p] * 6 + [i64] * 4 + [p, p, p, c_int, p]
+        L.msx_dl_csr_cg.argtypes = [p] * 6 + [i64, i64, c_float, c_float, ctypes.c_int32, p, p, p, p]
+        L.msx_dl_csr_pcg_jacobi.argtypes = [p] * 7 + [i64, i64, c_float, c_float, ctypes.c_int32, p, p, p, p]
         if hasattr(L, "msx_dist_pcg"):
             L.msx_dist_unique_id.argtypes = [p, i64]
             L.msx_dist_comm_create.argtypes = [p, c_int, c_int, ctypes.POINTER(p)]
@@ -126,6 +137,36 @@ def _p(t) -> int:
     return t.data_ptr() if t is not None else 0
 
 
+_capsule_ptr = ctypes.pythonapi.PyCapsule_GetPointer
+_capsule_ptr.restype = ctypes.c_void_p
+_capsule_ptr.argtypes = [ctypes.py_object, ctypes.c_char_p]
+_capsule_name = ctypes.pythonapi.PyCapsule_GetName
+_capsule_name.restype = ctypes.c_char_p
+_capsule_name.argtypes = [ctypes.py_object]
+# DLManagedTensorVersioned puts {version, manager_ctx, deleter, flags} (32
+# bytes) before its DLTensor; the legacy DLManagedTensor starts with it.
+_VERSIONED_OFFSET = 32
+
+
+class _DL:
+    """DLTensor pointers of torch tensors for one native call; the capsules
+    (and so the tensors' DLPack views) stay alive as long as this object."""
+
+    __slots__ = ("caps",)
+
+    def __init__(self):
+        self.caps = []
+
+    def __call__(self, t):
+        if t is None:
+            return None
+        cap = to_dlpack(t.detach())
+        self.caps.append(cap)
+        name = _capsule_name(cap)
+        ptr = _capsule_ptr(cap, name)
+        return ptr + (_VERSIONED_OFFSET if name == b"dltensor_versioned" else 0)
+
+
 class SpmvPlan:
     """Owns an ``msx_spmv_plan`` (row-length bins of one matrix)."""
 
@@ -159,10 +200,10 @@ def csr_matvec(data, indices, indptr, x, shape, *, plan: SpmvPlan | None = None,
     dev = require_cuda(data, indices, indptr, x)
     data, indices, indptr, x = (t.contiguous() for t in (data, indices, indptr, x))
     y = out if out is not None else torch.empty(shape[0], dtype=data.dtype, device=dev)
+    dl = _DL()
     with torch.cuda.device(dev):
-        check(L.msx_csr_matvec(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
-                               _p(indptr), data.numel(), _p(x), _p(y), shape[0], shape[1],
-                               plan.handle if plan is not None else None, stream_ptr(dev)))
+        check(L.msx_dl_csr_matvec(dl(data), dl(indices), dl(indptr), dl(x), dl(y), shape[0], shape[1],
+                                  plan.handle if plan is not None else None, stream_ptr(dev)))
     return y
 
 
@@ -172,10 +213,10 @@ def csr_matmul(data, indices, indptr, rhs, shape, *, out=None):
     data, indices, indptr, rhs = (t.contiguous() for t in (data, indices, indptr, rhs))
     k = rhs.shape[1]
     y = out if out is not None else torch.empty((shape[0], k), dtype=data.dtype, device=dev)
+    dl = _DL()
     with torch.cuda.device(dev):
-        check(L.msx_csr_matmul(VALUE_CODES[data.dtype], INDEX_CODES[indices.dtype], _p(data), _p(indices),
-                               _p(indptr), data.numel(), _p(rhs), k, _p(y), shape[0], shape[1],
-                               stream_ptr(dev)))
+        check(L.msx_dl_csr_matmul(dl(data), dl(indices), dl(indptr), dl(rhs), dl(y), shape[0], shape[1],
+                                  stream_ptr(dev)))
     return y
 
 
@@ -214,19 +255,17 @@ def csr_matmat(lhs, rhs, *, prune_zeros: bool = True):
     ld, li, lp = (t.contiguous() for t in (lhs.data, lhs.indices, lhs.indptr))
     rd, ri, rp = (t.contiguous() for t in (rhs.data, rhs.indices, rhs.indptr))
     out_it = li.dtype if li.dtype == ri.dtype else torch.int64
-    m, n = lhs.shape[0], rhs.shape[1]
-    args = [VALUE_CODES[ld.dtype], INDEX_CODES[li.dtype], _p(ld), _p(li), _p(lp), ld.numel(),
-            INDEX_CODES[ri.dtype], _p(rd), _p(ri), _p(rp), rd.numel(), lhs.shape[0], lhs.shape[1],
-            rhs.shape[0], rhs.shape[1], INDEX_CODES[out_it]]
+    m = lhs.shape[0]
     out_indptr = torch.empty(m + 1, dtype=out_it, device=dev)
     nnz = ctypes.c_int64()
+    dl = _DL()
+    args = [dl(ld), dl(li), dl(lp), dl(rd), dl(ri), dl(rp), lhs.shape[0], lhs.shape[1], rhs.shape[0], rhs.shape[1]]
     with torch.cuda.device(dev):
         s = stream_ptr(dev)
-        check(L.msx_csr_matmat_symbolic(*args, _p(out_indptr), ctypes.byref(nnz), int(prune_zeros), s))
+        check(L.msx_dl_csr_matmat_symbolic(*args, dl(out_indptr), ctypes.byref(nnz), int(prune_zeros), s))
         out_data = torch.empty(nnz.value, dtype=ld.dtype, device=dev)
         out_indices = torch.empty(nnz.value, dtype=out_it, device=dev)
-        check(L.msx_csr_matmat_numeric(*args, _p(out_indptr), nnz.value, _p(out_data), _p(out_indices),
-                                       int(prune_zeros), s))
+        check(L.msx_dl_csr_matmat_numeric(*args, dl(out_indptr), dl(out_data), dl(out_indices), int(prune_zeros), s))
     return out_data, out_indices, out_indptr
 
 
@@ -317,10 +356,11 @@ def csr_cg(data, indices, indptr, b, x0, shape, *, rtol, atol, maxiter):
     dev = require_cuda(data, indices, indptr, b, x0)
     data, indices, indptr, b, x0 = (t.contiguous() for t in (data, indices, indptr, b, x0))
     x, info, res, its = _solver_outputs(dev, shape[0])
+    dl = _DL()
     with torch.cuda.device(dev):
-        check(L.msx_csr_cg(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(), _p(b),
-                           _p(x0), _p(x), shape[0], shape[1], float(rtol), float(atol), int(maxiter),
-                           ctypes.addressof(info), ctypes.addressof(res), ctypes.addressof(its), stream_ptr(dev)))
+        check(L.msx_dl_csr_cg(dl(data), dl(indices), dl(indptr), dl(b), dl(x0), dl(x), shape[0], shape[1],
+                              float(rtol), float(atol), int(maxiter), ctypes.addressof(info), ctypes.addressof(res),
+                              ctypes.addressof(its), stream_ptr(dev)))
     return x, info.value, res.value, its.value
 
 
@@ -329,11 +369,12 @@ def csr_pcg_jacobi(data, indices, indptr, b, x0, inv_diag, shape, *, rtol, atol,
     dev = require_cuda(data, indices, indptr, b, x0, inv_diag)
     data, indices, indptr, b, x0, inv_diag = (t.contiguous() for t in (data, indices, indptr, b, x0, inv_diag))
     x, info, res, its = _solver_outputs(dev, shape[0])
+    dl = _DL()
     with torch.cuda.device(dev):
-        check(L.msx_csr_pcg_jacobi(INDEX_CODES[indices.dtype], _p(data), _p(indices), _p(indptr), data.numel(),
-                                   _p(b), _p(x0), _p(inv_diag), _p(x), shape[0], shape[1], float(rtol),
-                                   float(atol), int(maxiter), ctypes.addressof(info), ctypes.addressof(res),
-                                   ctypes.addressof(its), stream_ptr(dev)))
+        check(L.msx_dl_csr_pcg_jacobi(dl(data), dl(indices), dl(indptr), dl(b), dl(x0), dl(inv_diag), dl(x),
+                                      shape[0], shape[1], float(rtol), float(atol), int(maxiter),
+                                      ctypes.addressof(info), ctypes.addressof(res), ctypes.addressof(its),
+                                      stream_ptr(dev)))
     return x, info.value, res.value, its.value
 
 

@@ -112,3 +112,50 @@ def test_batched_and_context_entry_points_validate_without_gpu():
                                    None, None, ctypes.byref(out))
     assert rc == 1 and b"landing offsets" in lib.msx_last_error()
     assert lib.msx_cg_context_ipc_handles(None, None, 0) == 1
+
+
+class _DLDevice(ctypes.Structure):
+    _fields_ = [("device_type", ctypes.c_int32), ("device_id", ctypes.c_int32)]
+
+
+class _DLDataType(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_uint8), ("bits", ctypes.c_uint8), ("lanes", ctypes.c_uint16)]
+
+
+class _DLTensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("device", _DLDevice), ("ndim", ctypes.c_int32),
+                ("dtype", _DLDataType), ("shape", ctypes.POINTER(ctypes.c_int64)),
+                ("strides", ctypes.POINTER(ctypes.c_int64)), ("byte_offset", ctypes.c_uint64)]
+
+
+def test_dlpack_structs_match_the_capsules_torch_produces():
+    """The header's DLTensor is the public DLPack layout: reading a torch
+    capsule through it gives back the tensor's pointer, shape and dtype."""
+    from mlx_sparse import _native
+
+    assert ctypes.sizeof(_DLTensor) == 48
+    t = torch.arange(12, dtype=torch.float32).reshape(3, 4)
+    dl = _native._DL()
+    v = _DLTensor.from_address(dl(t))
+    assert v.data + v.byte_offset == t.data_ptr()
+    assert (v.ndim, v.shape[0], v.shape[1]) == (2, 3, 4)
+    assert (v.dtype.code, v.dtype.bits, v.dtype.lanes) == (2, 32, 1)
+    assert v.device.device_type == 1  # kDLCPU
+    b = _DLTensor.from_address(dl(torch.zeros(2, dtype=torch.bfloat16)))
+    assert (b.dtype.code, b.dtype.bits) == (4, 16)
+
+
+def test_dlpack_entry_points_reject_host_tensors_without_gpu():
+    """The DLPack entry points check the device before anything else, so a CPU
+    tensor is refused with the no-fallback message (no GPU needed)."""
+    from mlx_sparse import _native
+
+    lib = _native.extension()
+    dl = _native._DL()
+    d, i, p = torch.ones(2), torch.tensor([0, 1], dtype=torch.int32), torch.tensor([0, 1, 2], dtype=torch.int32)
+    x, y = torch.ones(2), torch.empty(2)
+    rc = lib.msx_dl_csr_matvec(dl(d), dl(i), dl(p), dl(x), dl(y), 2, 2, None, None)
+    assert rc == 1
+    assert b"CUDA device tensor" in lib.msx_last_error() and b"no CPU fallback" in lib.msx_last_error()
+    rc = lib.msx_dl_csr_matvec(None, dl(i), dl(p), dl(x), dl(y), 2, 2, None, None)
+    assert rc == 1 and b"must not be null" in lib.msx_last_error()
