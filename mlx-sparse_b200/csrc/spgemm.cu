@@ -35,6 +35,7 @@
 // No atomics touch values, so results are deterministic.
 #include <algorithm>
 #include <memory>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -88,24 +89,36 @@ __global__ void rhs_check_kernel(const RI *__restrict__ ri, const RI *__restrict
   if (flags) atomicOr(err, flags);
 }
 
-__global__ void bin_kernel(const int64_t *__restrict__ work, int64_t m, int *__restrict__ lists,
-                           int *__restrict__ counts, int64_t *__restrict__ row_nnz) {
+// Appends every row to the list of its bin. The lanes of a warp that fall in
+// the same bin take their slots with one atomic per bin and warp (a single
+// counter hit by every row serialises).
+template <typename LI>
+__global__ void bin_kernel(const int64_t *__restrict__ work, const LI *__restrict__ lp, int64_t m, bool reg_ok,
+                           int *__restrict__ lists, int *__restrict__ counts, int64_t *__restrict__ row_nnz) {
   const int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (row >= m) return;
-  const int64_t w = work[row];
-  int bin;
-  if (w == 0) {
-    row_nnz[row] = 0;
-    return;
-  } else if (w <= kWarpCap) {
-    bin = 0;
-  } else if (w <= kBlockCap) {
-    bin = 1;
-  } else {
-    bin = 2;
+  const int lane = threadIdx.x & 31;
+  int bin = -1;
+  if (row < m) {
+    const int64_t w = work[row];
+    if (w == 0) {
+      row_nnz[row] = 0;
+    } else if (w <= kWarpCap) {
+      // bin 3: one warp with the keys in registers (<= 32 lhs entries)
+      bin = (reg_ok && (int64_t)lp[row + 1] - (int64_t)lp[row] <= 32) ? 3 : 0;
+    } else {
+      bin = w <= kBlockCap ? 1 : 2;
+    }
   }
-  const int slot = atomicAdd(counts + bin, 1);
-  lists[bin * m + slot] = (int)row;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const unsigned mask = __ballot_sync(0xffffffffu, bin == b);
+    if (mask == 0) continue;
+    const int leader = __ffs(mask) - 1;
+    int base = 0;
+    if (lane == leader) base = atomicAdd(counts + b, __popc(mask));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (bin == b) lists[b * m + base + __popc(mask & ((1u << lane) - 1u))] = (int)row;
+  }
 }
 
 // ---- expand / sort / compress ---------------------------------------------------
@@ -144,6 +157,10 @@ struct RowSink {
 // Sorts the cnt keys (already in shared memory), sums every column's run in
 // position order, prunes exact zeros and writes the row to the sink.
 template <typename T, bool kWarp>
+__device__ void compact_sorted_row(int64_t row, int cnt, int tid, int nthreads, const uint64_t *key,
+                                   const float *val, int *scratch_cnt, RowSink<T> sink, bool prune);
+
+template <typename T, bool kWarp>
 __device__ void finish_row(int64_t row, int cnt, int tid, int nthreads, uint64_t *key, const float *val,
                            int *scratch_cnt, RowSink<T> sink, bool prune) {
   auto sync = [&]() {
@@ -155,6 +172,18 @@ __device__ void finish_row(int64_t row, int cnt, int tid, int nthreads, uint64_t
   for (int j = cnt + tid; j < pw; j += nthreads) key[j] = ~0ull;
   sync();
   bitonic_sort(key, pw, tid, nthreads, sync);
+  compact_sorted_row<T, kWarp>(row, cnt, tid, nthreads, key, val, scratch_cnt, sink, prune);
+}
+
+// Sums each column's run of the sorted keys in position order, prunes exact
+// zeros and writes the row to the sink.
+template <typename T, bool kWarp>
+__device__ void compact_sorted_row(int64_t row, int cnt, int tid, int nthreads, const uint64_t *key,
+                                   const float *val, int *scratch_cnt, RowSink<T> sink, bool prune) {
+  auto sync = [&]() {
+    if (kWarp) __syncwarp();
+    else __syncthreads();
+  };
   const int64_t out0 = sink.off[row];
   int count = 0;
   const int lane = tid & 31;
@@ -269,6 +298,161 @@ spgemm_warp_kernel(const int *__restrict__ list, const int *__restrict__ count_p
     }
     __syncwarp();
     finish_row<T, true>(row, cnt, lane, 32, key, val, nullptr, sink, prune);
+  }
+}
+
+// Rows of W <= 32 R products and at most 32 lhs entries, with the sort keys
+// in registers: key = column << 8 | position (n_cols < 2^24, W <= 256), one
+// key per lane and register, element i = lane * R + r of a bitonic network
+// whose cross-lane stages are shuffles. A row without repeated columns is
+// then compacted straight from the registers; a row with repeats takes the
+// shared-memory run summation.
+template <typename T, int R>
+__device__ __forceinline__ void reg_sort_row(int64_t row, int W, uint32_t (&key)[R], uint64_t *skey,
+                                             const float *val, RowSink<T> sink, bool prune) {
+  const int lane = threadIdx.x & 31;
+  constexpr int N = 32 * R;
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= R) {
+        const int lm = j / R;
+        const bool lower = (lane & lm) == 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint32_t other = __shfl_xor_sync(0xffffffffu, key[r], lm);
+          const bool up = (((lane * R + r) & k) == 0);
+          key[r] = (lower == up) ? min(key[r], other) : max(key[r], other);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if ((r & j) == 0) {
+            const bool up = (((lane * R + r) & k) == 0);
+            const uint32_t a = key[r], b = key[r | j];
+            if ((a > b) == up) {
+              key[r] = b;
+              key[r | j] = a;
+            }
+          }
+        }
+      }
+    }
+  }
+  // repeated columns (rare for random patterns): sum runs in shared memory
+  const uint32_t next_first = __shfl_down_sync(0xffffffffu, key[0], 1);
+  bool dup = false;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane * R + r;
+    const uint32_t nk = r + 1 < R ? key[r + 1] : next_first;
+    if (i + 1 < W && (key[r] >> 8) == (nk >> 8)) dup = true;
+  }
+  if (__any_sync(0xffffffffu, dup)) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = lane * R + r;
+      if (i < W) skey[i] = ((uint64_t)(key[r] >> 8) << 32) | (key[r] & 0xffu);
+    }
+    __syncwarp();
+    compact_sorted_row<T, true>(row, W, lane, 32, skey, val, nullptr, sink, prune);
+    return;
+  }
+  bool keep[R];
+  T outv[R];
+  int mine = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane * R + r;
+    keep[r] = false;
+    if (i < W) {
+      outv[r] = VT<T>::store(val[key[r] & 0xffu]);
+      keep[r] = !prune || VT<T>::load(outv[r]) != 0.0f;
+    }
+    mine += keep[r] ? 1 : 0;
+  }
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  int64_t pos = sink.off[row] + (incl - mine);
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (keep[r]) {
+      sink.col[pos] = (int)(key[r] >> 8);
+      sink.val[pos] = outv[r];
+      ++pos;
+    }
+  if (lane == 31) sink.row_nnz[row] = incl;
+  __syncwarp();
+}
+
+template <typename T, typename LI, typename RI>
+__global__ void __launch_bounds__(kBlockThreads)
+spgemm_warp_reg_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
+                       const int64_t *__restrict__ work, const T *__restrict__ ld, const LI *__restrict__ li,
+                       const LI *__restrict__ lp, const T *__restrict__ rd, const RI *__restrict__ ri,
+                       const RI *__restrict__ rp, RowSink<T> sink, bool prune) {
+  __shared__ uint64_t keys[kBlockThreads / 32][kWarpCap];
+  __shared__ float vals[kBlockThreads / 32][kWarpCap];
+  if (*flags & 3) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int count = *count_ptr;
+  float *val = vals[warp];
+  for (int w = blockIdx.x * (kBlockThreads / 32) + warp; w < count; w += gridDim.x * (kBlockThreads / 32)) {
+    const int64_t row = list[w];
+    const int W = (int)work[row];
+    const int64_t q0 = (int64_t)lp[row];
+    const int nq = (int)((int64_t)lp[row + 1] - q0);
+    int64_t rb = 0;
+    int len = 0;
+    float lv = 0.f;
+    if (lane < nq) {
+      const int64_t k = (int64_t)li[q0 + lane];
+      lv = VT<T>::load(ld[q0 + lane]);
+      rb = (int64_t)rp[k];
+      len = (int)((int64_t)rp[k + 1] - rb);
+    }
+    int incl = len;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    // product s = 32 u + lane goes to register u
+    auto expand = [&](auto rtag) {
+      constexpr int RR = decltype(rtag)::value;
+      uint32_t key[RR];
+#pragma unroll
+      for (int u = 0; u < RR; ++u) {
+        const int s = 32 * u + lane;
+        int e = 0;
+#pragma unroll
+        for (int b = 16; b > 0; b >>= 1) {
+          const int v = __shfl_sync(0xffffffffu, incl, (e + b - 1) & 31);
+          if (e + b <= nq && v <= s) e += b;
+        }
+        const int ev = e & 31;
+        const int excl = __shfl_sync(0xffffffffu, incl, ev) - __shfl_sync(0xffffffffu, len, ev);
+        const int64_t erb = __shfl_sync(0xffffffffu, rb, ev);
+        const float elv = __shfl_sync(0xffffffffu, lv, ev);
+        key[u] = ~0u;
+        if (s < W) {
+          const int64_t src = erb + (s - excl);
+          key[u] = ((uint32_t)ri[src] << 8) | (uint32_t)s;
+          val[s] = __fmul_rn(elv, VT<T>::load(rd[src]));
+        }
+      }
+      __syncwarp();
+      reg_sort_row<T, RR>(row, W, key, keys[warp], val, sink, prune);
+    };
+    if (W <= 32) expand(std::integral_constant<int, 1>{});
+    else if (W <= 64) expand(std::integral_constant<int, 2>{});
+    else if (W <= 128) expand(std::integral_constant<int, 4>{});
+    else expand(std::integral_constant<int, 8>{});
   }
 }
 
@@ -454,16 +638,16 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
   const int64_t n_sums = scan_scratch_elems(m);
   size_t off = 0;
   const size_t o_work = off; off += al(sizeof(int64_t) * m);
-  const size_t o_lists = off; off += al(sizeof(int) * 3 * m);
+  const size_t o_lists = off; off += al(sizeof(int) * 4 * m);
   const size_t o_counts = off; off += al(sizeof(int) * 8);
   const size_t o_sums = off; off += al(sizeof(int64_t) * n_sums);
   Scratch scratch(off, s);
   char *base = scratch.as<char>();
   int64_t *work = reinterpret_cast<int64_t *>(base + o_work);
   int *lists = reinterpret_cast<int *>(base + o_lists);
-  int *counts = reinterpret_cast<int *>(base + o_counts);  // [0..2] bins, [3] flags
+  int *counts = reinterpret_cast<int *>(base + o_counts);  // [0..3] bins, [4] flags
   int64_t *sums = reinterpret_cast<int64_t *>(base + o_sums);
-  int *flags = counts + 3;
+  int *flags = counts + 4;
 
   // the product's own memory: offsets (m + 1), exact counts (m), then the
   // rows' columns and values at the offsets (sized after the first sync)
@@ -476,18 +660,20 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
   row_work_kernel<LI, RI><<<(unsigned)ceil_div(m, t), t, 0, s>>>(li, lp, rp, m, rhs_rows, work, flags);
   if (rhs_rows > 0)
     rhs_check_kernel<RI><<<(unsigned)ceil_div(rhs_rows, t), t, 0, s>>>(ri, rp, rhs_rows, n_cols, flags);
-  bin_kernel<<<(unsigned)ceil_div(m, t), t, 0, s>>>(work, m, lists, counts, row_nnz);
+  // column << 8 | position fits 32 bits below the all-ones padding key
+  const bool reg_ok = n_cols < ((int64_t)1 << 24);
+  bin_kernel<LI><<<(unsigned)ceil_div(m, t), t, 0, s>>>(work, lp, m, reg_ok, lists, counts, row_nnz);
   MSX_CHECK_LAUNCH();
   scan_counts_to_indptr<int64_t>(work, m, row_off, sums, s);
   struct {
-    int counts[4];
+    int counts[5];
     int64_t total;
   } h{};
   MSX_CUDA(cudaMemcpyAsync(h.counts, counts, sizeof(h.counts), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaMemcpyAsync(&h.total, sums + n_sums - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
-  if (h.counts[3] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
-  if (h.counts[3] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
+  if (h.counts[4] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
+  if (h.counts[4] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
   const int64_t total = h.total;
 
   const size_t o_col = 0;
@@ -511,6 +697,13 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
     const int grid = (int)std::min<int64_t>(ceil_div(h.counts[0], wpb), (int64_t)sms * 8);
     spgemm_warp_kernel<T, LI, RI><<<grid, kBlockThreads, 0, s>>>(lists, counts + 0, flags, ld, li, lp, rd, ri, rp,
                                                                   sink, prune);
+    MSX_CHECK_LAUNCH();
+  }
+  if (h.counts[3] > 0) {
+    const int wpb = kBlockThreads / 32;
+    const int grid = (int)std::min<int64_t>(ceil_div(h.counts[3], wpb), (int64_t)sms * 8);
+    spgemm_warp_reg_kernel<T, LI, RI><<<grid, kBlockThreads, 0, s>>>(lists + 3 * m, counts + 3, flags, work, ld, li,
+                                                                      lp, rd, ri, rp, sink, prune);
     MSX_CHECK_LAUNCH();
   }
   if (h.counts[1] > 0) {

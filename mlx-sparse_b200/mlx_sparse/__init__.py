@@ -20,6 +20,7 @@ from mlx_sparse._ops import (
     csr_matmat,
     csr_matmul,
     csr_matmul_data_vjp,
+    csr_matmul_streamed,
     csr_matmul_transpose,
     csr_matvec,
     csr_matvec_data_vjp,
@@ -42,6 +43,7 @@ __all__ = [
     "csr_batched_matvec",
     "csr_matmul",
     "csr_matmul_data_vjp",
+    "csr_matmul_streamed",
     "csr_matmul_transpose",
     "csr_matvec",
     "csr_matvec_data_vjp",

@@ -235,3 +235,78 @@ def coo_matmat(a: COOArray, b: COOArray) -> COOArray:
     reference's ``COOArray.__matmul__``), through the CSR SpGEMM kernels."""
     c = csr_matmat(a.tocsr(canonical=True), b.tocsr(canonical=True))
     return c.tocoo()
+
+
+# ---------------------------------------------------------------------------
+# Host-resident operands streamed through the GPU
+# ---------------------------------------------------------------------------
+def csr_matmul_streamed(a: CSRArray, rhs, *, device=None, chunks: int = 8, out=None):
+    """``Y = A @ B`` for a CSR matrix and a dense ``B`` that live in host
+    memory (pinned for full speed), computed on a GPU and returned in pinned
+    host memory.
+
+    The reference's arrays are host arrays (MLX unified memory); this entry
+    keeps that calling convention while the product runs in the CUDA SpMM
+    kernels. ``out`` may be a caller-owned pinned host tensor of shape
+    ``(n_rows, k)`` (allocating pinned memory per call is slow). The
+    transfers are pipelined on three streams: B and the row
+    pointers go up first, then the matrix in ``chunks`` row blocks; each block
+    is multiplied as soon as it has landed, and its rows of Y go back down
+    while later blocks are still uploading (PCIe is full duplex). Nothing is
+    computed on the CPU. Results equal ``A @ B`` on the device.
+    """
+    if not isinstance(a, CSRArray):
+        raise TypeError(f"csr_matmul_streamed expects CSRArray, got {type(a).__name__}.")
+    if not isinstance(rhs, torch.Tensor) or rhs.ndim != 2:
+        raise ValueError("csr_matmul_streamed expects a rank-2 host tensor RHS.")
+    if a.data.is_cuda or rhs.is_cuda:
+        raise ValueError("csr_matmul_streamed takes host operands; use A @ B for device operands.")
+    validate_csr_matmul_inputs(a.data, a.indices, a.indptr, rhs, a.shape)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    n_rows, n_cols = a.shape
+    k = int(rhs.shape[1])
+    if out is None:
+        out = torch.empty((n_rows, k), dtype=a.data.dtype, pin_memory=True)
+    elif out.is_cuda or tuple(out.shape) != (n_rows, k) or out.dtype != a.data.dtype or not out.is_contiguous():
+        raise ValueError(f"csr_matmul_streamed out must be a contiguous host tensor of shape ({n_rows}, {k}).")
+    if n_rows == 0 or k == 0:
+        return out
+    indptr_h = a.indptr.contiguous()
+    ptr = indptr_h.to(torch.int64).numpy() if indptr_h.dtype != torch.int64 else indptr_h.numpy()
+    with torch.cuda.device(dev):
+        up, comp, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        cur = torch.cuda.current_stream(dev)
+        up.wait_stream(cur)
+        d_data = torch.empty(a.data.shape, dtype=a.data.dtype, device=dev)
+        d_idx = torch.empty(a.indices.shape, dtype=a.indices.dtype, device=dev)
+        d_out = torch.empty((n_rows, k), dtype=a.data.dtype, device=dev)
+        with torch.cuda.stream(up):
+            d_ptr = indptr_h.to(dev, non_blocking=True)
+            d_rhs = rhs.contiguous().to(dev, non_blocking=True)
+            ready_rhs = torch.cuda.Event()
+            ready_rhs.record(up)
+        bounds = [(n_rows * c) // chunks for c in range(chunks + 1)]
+        for c in range(chunks):
+            r0, r1 = bounds[c], bounds[c + 1]
+            if r1 <= r0:
+                continue
+            k0, k1 = int(ptr[r0]), int(ptr[r1])
+            with torch.cuda.stream(up):
+                if k1 > k0:
+                    d_data[k0:k1].copy_(a.data[k0:k1], non_blocking=True)
+                    d_idx[k0:k1].copy_(a.indices[k0:k1], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(up)
+            comp.wait_event(ready_rhs)
+            comp.wait_event(landed)
+            with torch.cuda.stream(comp):
+                _native.csr_matmul(d_data, d_idx, d_ptr[r0:r1 + 1], d_rhs, (r1 - r0, n_cols), out=d_out[r0:r1])
+                computed = torch.cuda.Event()
+                computed.record(comp)
+            down.wait_event(computed)
+            with torch.cuda.stream(down):
+                out[r0:r1].copy_(d_out[r0:r1], non_blocking=True)
+        # the host waits for the last copy down (it waited on every block), so
+        # the device buffers are free again when they are released
+        down.synchronize()
+    return out

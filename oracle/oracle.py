@@ -246,6 +246,32 @@ def gershgorin(data, indices, indptr):
     return tuple(float(v) for v in out)
 
 
+REF_LIB = os.path.join(HERE, "_ref", "libref_parallel.so")
+
+
+def build_ref() -> str | None:
+    """Compiles oracle/_ref/libref_parallel.so from the reference's own
+    src/common/cpu_parallel.cpp when the reference checkout is present
+    (MSX_REFERENCE_ROOT, default: a `reference` folder beside the repository);
+    returns its path or None."""
+    root = os.environ.get("MSX_REFERENCE_ROOT", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
+    if not os.path.exists(os.path.join(root, "src", "common", "cpu_parallel.cpp")):
+        return REF_LIB if os.path.exists(REF_LIB) else None
+    subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={root}"], check=True)
+    return REF_LIB
+
+
+def ref_weighted_ranges(work, parts):
+    """The reference's weighted_cpu_ranges (cpu_parallel.cpp:202-253), run from
+    its own source compiled by build_ref(); list of (begin, end)."""
+    L = ctypes.CDLL(REF_LIB)
+    L.ref_weighted_ranges.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+    w = np.ascontiguousarray(work, dtype=np.int64)
+    out = np.empty(2 * max(parts, 1), dtype=np.int64)
+    k = L.ref_weighted_ranges(_ptr(w), w.shape[0], parts, _ptr(out))
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(k)]
+
+
 def weighted_ranges(work, parts):
     work = np.ascontiguousarray(work, dtype=np.int64)
     out = np.empty(2 * max(parts, 1), dtype=np.int64)

@@ -308,3 +308,18 @@ def test_chebyshev_oracle_approaches_the_solve(orc):
     np.testing.assert_allclose(x, np.linalg.solve(S, r), rtol=1e-4, atol=1e-4)
     lo, hi, dmin, dmax = orc.gershgorin(d, i, p)
     assert (lo, hi, dmin, dmax) == (0.0, 8.0, 4.0, 4.0)
+
+
+def test_weighted_ranges_match_the_reference_compiled_from_source(orc):
+    """The oracle restates the reference's nnz-weighted partition; where the
+    reference checkout is present, its own src/common/cpu_parallel.cpp is
+    compiled (oracle/_ref, `make -C oracle ref`) and the two must agree."""
+    if orc.build_ref() is None:
+        pytest.skip("reference checkout not present")
+    rng = np.random.default_rng(11)
+    cases = [np.ones(100, np.int64), np.arange(1, 1000, dtype=np.int64), rng.integers(0, 50, 5000),
+             np.zeros(10, np.int64), np.asarray([10 ** 6] + [1] * 999, np.int64),
+             np.diff(wl.power_law(20000, 3)[0][2]).astype(np.int64)]
+    for work in cases:
+        for parts in (1, 2, 3, 7, 16, 64):
+            assert orc.weighted_ranges(work, parts) == orc.ref_weighted_ranges(work, parts), (work[:5], parts)

@@ -117,3 +117,21 @@ def test_full_size_baseline_config(ms, orc, bf16):
     scale = orc.csr_matmul(np.abs(orc.bf16_bits_to_f32(db)), i, p, np.abs(orc.bf16_bits_to_f32(Bb)), n, workers=8)
     err = np.abs(Y.astype(np.float64) - Y_ref)
     assert np.all(err <= 1e-2 * np.maximum(np.abs(Y_ref), scale)), float(np.max(err / np.maximum(scale, 1e-30)))
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_streamed_host_operands_equal_the_device_product(ms, chunks):
+    """csr_matmul_streamed (host operands, pipelined uploads / row-block
+    products / downloads) gives the device product bit for bit, also with
+    empty rows and blocks without nonzeros."""
+    (d, i, p), shape = wl.ragged_csr(5000, 3000, 6, 40)
+    B = wl.uniform_matrix(shape[1], 48, 7)
+    A_host = ms.CSRArray(torch.from_numpy(d).pin_memory(), torch.from_numpy(i).pin_memory(),
+                         torch.from_numpy(p).pin_memory(), shape, has_canonical_format=True)
+    Y = ms.csr_matmul_streamed(A_host, torch.from_numpy(B).pin_memory(), chunks=chunks)
+    assert not Y.is_cuda
+    Y_dev = (_csr(ms, d, i, p, shape) @ _dev(B)).cpu()
+    assert torch.equal(Y, Y_dev)
+    out = torch.empty_like(Y).pin_memory()
+    ms.csr_matmul_streamed(A_host, torch.from_numpy(B), chunks=chunks, out=out)
+    assert torch.equal(out, Y_dev)
