@@ -421,10 +421,11 @@ int msx_csr_matmat_numeric(int value_dtype, int lhs_index_dtype, const void *lhs
     check_ptr(out_indptr, lhs_n_rows + 1, "csr_matmat out_indptr");
     check_ptr(out_data, out_nnz, "csr_matmat out_data");
     check_ptr(out_indices, out_nnz, "csr_matmat out_indices");
-    int64_t unused = 0;
+    int64_t capacity = out_nnz;
     spgemm_run(true, value_dtype, lhs_index_dtype, lhs_data, lhs_indices, lhs_indptr, rhs_index_dtype, rhs_data,
                rhs_indices, rhs_indptr, lhs_n_rows, rhs_n_rows, rhs_n_cols, out_index_dtype,
-               const_cast<void *>(out_indptr), out_indices, out_data, &unused, prune_zeros != 0, as_stream(stream));
+               const_cast<void *>(out_indptr), out_indices, out_data, &capacity, prune_zeros != 0,
+               as_stream(stream));
   });
 }
 

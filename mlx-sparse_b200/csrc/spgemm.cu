@@ -49,6 +49,7 @@ constexpr int kWarpCap = 256;    // products per warp-level row
 constexpr int kBlockCap = 4096;  // products per CTA-level row
 constexpr int kBlockThreads = 256;
 constexpr int kDenseThreads = 512;
+constexpr int kBins = 7;  // smem warp, CTA, dense, register warp R = 1, 2, 4, 8
 
 __device__ __forceinline__ uint32_t key_col(uint64_t k) { return (uint32_t)(k >> 32); }
 __device__ __forceinline__ uint32_t key_seq(uint64_t k) { return (uint32_t)(k & 0xffffffffu); }
@@ -103,14 +104,18 @@ __global__ void bin_kernel(const int64_t *__restrict__ work, const LI *__restric
     if (w == 0) {
       row_nnz[row] = 0;
     } else if (w <= kWarpCap) {
-      // bin 3: one warp with the keys in registers (<= 32 lhs entries)
-      bin = (reg_ok && (int64_t)lp[row + 1] - (int64_t)lp[row] <= 32) ? 3 : 0;
+      // bins 3..6: one warp with the keys in 1, 2, 4 or 8 registers per lane
+      // (<= 32 lhs entries); else the shared-memory warp path
+      if (reg_ok && (int64_t)lp[row + 1] - (int64_t)lp[row] <= 32)
+        bin = w <= 32 ? 3 : (w <= 64 ? 4 : (w <= 128 ? 5 : 6));
+      else
+        bin = 0;
     } else {
       bin = w <= kBlockCap ? 1 : 2;
     }
   }
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
+  for (int b = 0; b < kBins; ++b) {
     const unsigned mask = __ballot_sync(0xffffffffu, bin == b);
     if (mask == 0) continue;
     const int leader = __ffs(mask) - 1;
@@ -390,7 +395,7 @@ __device__ __forceinline__ void reg_sort_row(int64_t row, int W, uint32_t (&key)
   __syncwarp();
 }
 
-template <typename T, typename LI, typename RI>
+template <typename T, typename LI, typename RI, int R>
 __global__ void __launch_bounds__(kBlockThreads)
 spgemm_warp_reg_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
                        const int64_t *__restrict__ work, const T *__restrict__ ld, const LI *__restrict__ li,
@@ -423,36 +428,29 @@ spgemm_warp_reg_kernel(const int *__restrict__ list, const int *__restrict__ cou
       if (lane >= o) incl += v;
     }
     // product s = 32 u + lane goes to register u
-    auto expand = [&](auto rtag) {
-      constexpr int RR = decltype(rtag)::value;
-      uint32_t key[RR];
+    uint32_t key[R];
 #pragma unroll
-      for (int u = 0; u < RR; ++u) {
-        const int s = 32 * u + lane;
-        int e = 0;
+    for (int u = 0; u < R; ++u) {
+      const int s = 32 * u + lane;
+      int e = 0;
 #pragma unroll
-        for (int b = 16; b > 0; b >>= 1) {
-          const int v = __shfl_sync(0xffffffffu, incl, (e + b - 1) & 31);
-          if (e + b <= nq && v <= s) e += b;
-        }
-        const int ev = e & 31;
-        const int excl = __shfl_sync(0xffffffffu, incl, ev) - __shfl_sync(0xffffffffu, len, ev);
-        const int64_t erb = __shfl_sync(0xffffffffu, rb, ev);
-        const float elv = __shfl_sync(0xffffffffu, lv, ev);
-        key[u] = ~0u;
-        if (s < W) {
-          const int64_t src = erb + (s - excl);
-          key[u] = ((uint32_t)ri[src] << 8) | (uint32_t)s;
-          val[s] = __fmul_rn(elv, VT<T>::load(rd[src]));
-        }
+      for (int b = 16; b > 0; b >>= 1) {
+        const int v = __shfl_sync(0xffffffffu, incl, (e + b - 1) & 31);
+        if (e + b <= nq && v <= s) e += b;
       }
-      __syncwarp();
-      reg_sort_row<T, RR>(row, W, key, keys[warp], val, sink, prune);
-    };
-    if (W <= 32) expand(std::integral_constant<int, 1>{});
-    else if (W <= 64) expand(std::integral_constant<int, 2>{});
-    else if (W <= 128) expand(std::integral_constant<int, 4>{});
-    else expand(std::integral_constant<int, 8>{});
+      const int ev = e & 31;
+      const int excl = __shfl_sync(0xffffffffu, incl, ev) - __shfl_sync(0xffffffffu, len, ev);
+      const int64_t erb = __shfl_sync(0xffffffffu, rb, ev);
+      const float elv = __shfl_sync(0xffffffffu, lv, ev);
+      key[u] = ~0u;
+      if (s < W) {
+        const int64_t src = erb + (s - excl);
+        key[u] = ((uint32_t)ri[src] << 8) | (uint32_t)s;
+        val[s] = __fmul_rn(elv, VT<T>::load(rd[src]));
+      }
+    }
+    __syncwarp();
+    reg_sort_row<T, R>(row, W, key, keys[warp], val, sink, prune);
   }
 }
 
@@ -569,7 +567,9 @@ spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_
 }
 
 // Copies every finished row from its upper-bound slot to its final place.
-// One warp per row; lanes copy consecutive entries.
+// A warp takes 32 consecutive rows: the lanes read the 32 rows' offsets and
+// counts with one load each, then the warp copies the rows one after another
+// with coalesced lanes, with no dependent global load between rows.
 template <typename T, typename OutI>
 __global__ void copy_rows_kernel(const int64_t *__restrict__ off, const int64_t *__restrict__ row_nnz,
                                  const int *__restrict__ col, const T *__restrict__ val, int64_t m,
@@ -577,14 +577,33 @@ __global__ void copy_rows_kernel(const int64_t *__restrict__ off, const int64_t 
                                  T *__restrict__ out_data) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < m; row += warps) {
-    const int64_t n = row_nnz[row];
-    const int64_t src = off[row], dst = (int64_t)out_indptr[row];
-    for (int64_t j = lane; j < n; j += 32) {
-      out_idx[dst + j] = (OutI)col[src + j];
-      out_data[dst + j] = val[src + j];
+  for (int64_t r0 = (blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; r0 < m;
+       r0 += warps * 32) {
+    const int64_t r = r0 + lane;
+    int64_t my_n = 0, my_src = 0, my_dst = 0;
+    if (r < m) {
+      my_n = row_nnz[r];
+      my_src = off[r];
+      my_dst = (int64_t)out_indptr[r];
+    }
+    const int rows = (int)min((int64_t)32, m - r0);
+#pragma unroll 4
+    for (int q = 0; q < rows; ++q) {
+      const int64_t n = __shfl_sync(0xffffffffu, my_n, q);
+      const int64_t src = __shfl_sync(0xffffffffu, my_src, q);
+      const int64_t dst = __shfl_sync(0xffffffffu, my_dst, q);
+      for (int64_t j = lane; j < n; j += 32) {
+        out_idx[dst + j] = (OutI)col[src + j];
+        out_data[dst + j] = val[src + j];
+      }
     }
   }
+}
+
+template <typename OutI>
+__global__ void widen_kernel(const int *__restrict__ col, int64_t n, OutI *__restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (OutI)col[i];
 }
 
 int dense_slots(int64_t n_cols) {
@@ -609,6 +628,7 @@ struct Product {
   int *col = nullptr;
   void *val = nullptr;
   int64_t nnz = 0;
+  int64_t total_w = -1;  // products (the upper-bound layout's length)
   ~Product() {
     if (mem) cudaFreeAsync(mem, stream);
   }
@@ -638,20 +658,20 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
   const int64_t n_sums = scan_scratch_elems(m);
   size_t off = 0;
   const size_t o_work = off; off += al(sizeof(int64_t) * m);
-  const size_t o_lists = off; off += al(sizeof(int) * 4 * m);
-  const size_t o_counts = off; off += al(sizeof(int) * 8);
+  const size_t o_lists = off; off += al(sizeof(int) * kBins * m);
+  const size_t o_counts = off; off += al(sizeof(int) * (kBins + 1));
   const size_t o_sums = off; off += al(sizeof(int64_t) * n_sums);
   Scratch scratch(off, s);
   char *base = scratch.as<char>();
   int64_t *work = reinterpret_cast<int64_t *>(base + o_work);
   int *lists = reinterpret_cast<int *>(base + o_lists);
-  int *counts = reinterpret_cast<int *>(base + o_counts);  // [0..3] bins, [4] flags
+  int *counts = reinterpret_cast<int *>(base + o_counts);  // [0..kBins) bins, [kBins] flags
   int64_t *sums = reinterpret_cast<int64_t *>(base + o_sums);
-  int *flags = counts + 4;
+  int *flags = counts + kBins;
 
   // the product's own memory: offsets (m + 1), exact counts (m), then the
   // rows' columns and values at the offsets (sized after the first sync)
-  MSX_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * 8, s));
+  MSX_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * (kBins + 1), s));
   const int t = 256;
   size_t head = al(sizeof(int64_t) * (m + 1)) + al(sizeof(int64_t) * m);
   Scratch head_mem(head, s);
@@ -666,15 +686,16 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
   MSX_CHECK_LAUNCH();
   scan_counts_to_indptr<int64_t>(work, m, row_off, sums, s);
   struct {
-    int counts[5];
+    int counts[kBins + 1];
     int64_t total;
   } h{};
   MSX_CUDA(cudaMemcpyAsync(h.counts, counts, sizeof(h.counts), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaMemcpyAsync(&h.total, sums + n_sums - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
   MSX_CUDA(cudaStreamSynchronize(s));
-  if (h.counts[4] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
-  if (h.counts[4] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
+  if (h.counts[kBins] & 1) fail(MSX_ERR_INVALID, "csr_matmat lhs indices contain an out-of-bounds column.");
+  if (h.counts[kBins] & 2) fail(MSX_ERR_INVALID, "csr_matmat rhs indices contain an out-of-bounds column.");
   const int64_t total = h.total;
+  P->total_w = total;
 
   const size_t o_col = 0;
   size_t bytes = al(sizeof(int) * std::max<int64_t>(total, 1));
@@ -699,13 +720,20 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
                                                                   sink, prune);
     MSX_CHECK_LAUNCH();
   }
-  if (h.counts[3] > 0) {
+  auto reg_rows = [&](auto rtag) {
+    constexpr int R = decltype(rtag)::value;
+    constexpr int b = R == 1 ? 3 : (R == 2 ? 4 : (R == 4 ? 5 : 6));
+    if (h.counts[b] == 0) return;
     const int wpb = kBlockThreads / 32;
-    const int grid = (int)std::min<int64_t>(ceil_div(h.counts[3], wpb), (int64_t)sms * 8);
-    spgemm_warp_reg_kernel<T, LI, RI><<<grid, kBlockThreads, 0, s>>>(lists + 3 * m, counts + 3, flags, work, ld, li,
-                                                                      lp, rd, ri, rp, sink, prune);
+    const int grid = (int)std::min<int64_t>(ceil_div(h.counts[b], wpb), (int64_t)sms * 8);
+    spgemm_warp_reg_kernel<T, LI, RI, R><<<grid, kBlockThreads, 0, s>>>(lists + b * m, counts + b, flags, work, ld,
+                                                                         li, lp, rd, ri, rp, sink, prune);
     MSX_CHECK_LAUNCH();
-  }
+  };
+  reg_rows(std::integral_constant<int, 1>{});
+  reg_rows(std::integral_constant<int, 2>{});
+  reg_rows(std::integral_constant<int, 4>{});
+  reg_rows(std::integral_constant<int, 8>{});
   if (h.counts[1] > 0) {
     const size_t smem = (size_t)kBlockCap * (sizeof(uint64_t) + sizeof(float));
     const int grid = (int)std::min<int64_t>(h.counts[1], (int64_t)sms * 4);
@@ -736,6 +764,8 @@ template <typename T, typename LI, typename RI, typename OutI>
 void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *rd, const RI *ri, const RI *rp,
                  int64_t m, int64_t rhs_rows, int64_t n_cols, const int types[4], OutI *out_indptr, OutI *out_idx,
                  T *out_data, int64_t *out_nnz, bool prune, cudaStream_t s) {
+  // numeric call: *out_nnz is the capacity of the caller's arrays
+  const int64_t out_nnz_cap = write ? *out_nnz : 0;
   if (m == 0) {
     if (!write) {
       MSX_CUDA(cudaMemsetAsync(out_indptr, 0, sizeof(OutI), s));
@@ -773,7 +803,23 @@ void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *r
     // (the caller's indptr already holds the output layout)
     P = compute_product<T, LI, RI, OutI>(std::move(key), ld, li, lp, rd, ri, rp, nullptr, s);
   }
-  const int grid = (int)std::min<int64_t>(ceil_div(m, 8), (int64_t)num_sms() * 16);
+  if (P->nnz == P->total_w && P->nnz >= 0 && P->nnz <= out_nnz_cap) {
+    // no row lost an entry (no repeated columns, nothing pruned): the upper-
+    // bound layout is already the packed output
+    const int64_t n = P->nnz;
+    if (n > 0) {
+      MSX_CUDA(cudaMemcpyAsync(out_data, P->val, sizeof(T) * (size_t)n, cudaMemcpyDeviceToDevice, s));
+      if constexpr (sizeof(OutI) == sizeof(int)) {
+        MSX_CUDA(cudaMemcpyAsync(out_idx, P->col, sizeof(int) * (size_t)n, cudaMemcpyDeviceToDevice, s));
+      } else {
+        widen_kernel<OutI><<<(unsigned)std::min<int64_t>(ceil_div(n, 256), (int64_t)num_sms() * 16), 256, 0, s>>>(
+            P->col, n, out_idx);
+        MSX_CHECK_LAUNCH();
+      }
+    }
+    return;
+  }
+  const int grid = (int)std::min<int64_t>(ceil_div(m, 8 * 32), (int64_t)num_sms() * 16);
   copy_rows_kernel<T, OutI><<<grid, 256, 0, s>>>(P->off, P->row_nnz, P->col, static_cast<const T *>(P->val), m,
                                                  out_indptr, out_idx, out_data);
   MSX_CHECK_LAUNCH();
