@@ -296,21 +296,15 @@ spmv_short_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
       const int q0 = (int)((int64_t)ptr_s[tid] - k0);
       const int q1 = (int)((int64_t)ptr_s[tid + 1] - k0);
       float xv[8];
-      I cv[8];
-      // all gathers of owned columns first, so they are in flight together;
-      // halo columns (multi-GPU: read from peer-written words, possibly
-      // waiting) only afterwards, off the common path
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (q0 + u < q1) {
-          cv[u] = idx_s[si + q0 + u];
-          if (!Epi::kHalo || (int64_t)cv[u] < halo_from) xv[u] = VT<T>::load(__ldg(x + cv[u]));
+          const I c = idx_s[si + q0 + u];
+          if constexpr (Epi::kHalo)
+            xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
+          else
+            xv[u] = VT<T>::load(__ldg(x + c));
         }
-      if constexpr (Epi::kHalo) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (q0 + u < q1 && (int64_t)cv[u] >= halo_from) xv[u] = epi.halo_x(cv[u]);
-      }
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
@@ -397,21 +391,15 @@ spmv_short_pipe_kernel(const T *__restrict__ data, const I *__restrict__ indices
       const int q0 = (int)((int64_t)ptr_s[pc][tid] - k0);
       const int q1 = (int)((int64_t)ptr_s[pc][tid + 1] - k0);
       float xv[8];
-      I cv[8];
-      // all gathers of owned columns first, so they are in flight together;
-      // halo columns (multi-GPU: read from peer-written words, possibly
-      // waiting) only afterwards, off the common path
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (q0 + u < q1) {
-          cv[u] = idx_base[dc * kIdxElems + si + q0 + u];
-          if (!Epi::kHalo || (int64_t)cv[u] < halo_from) xv[u] = VT<T>::load(__ldg(x + cv[u]));
+          const I c = idx_base[dc * kIdxElems + si + q0 + u];
+          if constexpr (Epi::kHalo)
+            xv[u] = (int64_t)c >= halo_from ? epi.halo_x(c) : VT<T>::load(__ldg(x + c));
+          else
+            xv[u] = VT<T>::load(__ldg(x + c));
         }
-      if constexpr (Epi::kHalo) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (q0 + u < q1 && (int64_t)cv[u] >= halo_from) xv[u] = epi.halo_x(cv[u]);
-      }
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u)
