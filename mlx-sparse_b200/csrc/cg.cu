@@ -34,6 +34,7 @@
 // each reduction. The solver state (plan, buffers, captured graph) lives in a
 // CgEngine that is reused across solves.
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -173,16 +174,39 @@ __device__ bool ll_allreduce(CgState *st, const P2pLink *L) {
   return ok;
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Trace hook at a reduction kernel's start (slot 0: SpMV + dots, 1: update).
+__device__ __forceinline__ void trace_start(CgState *st, int slot) {
+  if (st->tracing && threadIdx.x == 0) atomicMin(&st->k_start[slot], global_ns());
+}
+
 // The last CTA of a reduction: combine over the ranks (peer memory) and run
 // the decision `f` in one thread. Single GPU: decide directly when `decide`.
 template <typename F>
 __device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partials, CgState *st, const P2pLink *L,
-                                                  bool decide, F f) {
+                                                  bool decide, F f, int trace_slot = -1) {
   if (!reduce_last(v, partials, st)) return;
+  unsigned long long t_ready = 0;
+  if (threadIdx.x == 0 && trace_slot >= 0 && st->tracing) t_ready = global_ns();
+  auto trace_done = [&]() {
+    if (trace_slot >= 0 && st->tracing) {
+      const unsigned long long t_done = global_ns();
+      st->trace[3 * trace_slot] += t_ready - st->k_start[trace_slot];
+      st->trace[3 * trace_slot + 1] += t_done - t_ready;
+      st->trace[3 * trace_slot + 2] += 1;
+      st->k_start[trace_slot] = ~0ull;
+    }
+  };
   if (L) {
     if (threadIdx.x < 32) {
       const bool ok = ll_allreduce(st, L);
       if (threadIdx.x == 0) {
+        trace_done();
         if (ok) {
           f();
         } else {
@@ -192,6 +216,7 @@ __device__ __forceinline__ void reduce_and_decide(double (&v)[4], double *partia
       }
     }
   } else if (threadIdx.x == 0 && decide) {
+    trace_done();
     f();
   }
 }
@@ -477,7 +502,10 @@ template <bool kHaloWords> struct DotsEpilogueT {
   double pap, pp, apap, bad;
   static constexpr bool kHalo = kHaloWords;
   static constexpr bool kShortPipe = true;  // measured faster inside the CG iteration (256^3: 61.3 vs 64.0 ms)
-  __device__ __forceinline__ bool skip() const { return st->status != kStatusRunning; }
+  __device__ __forceinline__ bool skip() const {
+    trace_start(st, 0);
+    return st->status != kStatusRunning;
+  }
   __device__ __forceinline__ int64_t halo_from() const { return halo ? n_owned : INT64_MAX; }
   __device__ __forceinline__ float halo_x(int64_t col) {
     return halo_read(st, L, col - n_owned, st->round_base + (unsigned)st->it);
@@ -491,7 +519,7 @@ template <bool kHaloWords> struct DotsEpilogueT {
   }
   __device__ __forceinline__ void finish() {
     double v[4] = {pap, pp, apap, bad};
-    reduce_and_decide(v, partials, st, L, decide, [&] { decide_spmv(st, kind); });
+    reduce_and_decide(v, partials, st, L, decide, [&] { decide_spmv(st, kind); }, 0);
   }
 };
 
@@ -518,6 +546,7 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
               int64_t n, double *partials, CgState *st, bool decide, const P2pLink *L) {
   pdl_wait();
   pdl_trigger();
+  trace_start(st, 1);
   if (st->status != kStatusRunning) return;
   double v[4] = {0.0, 0.0, 0.0, 0.0};
   if (kind == kCG) {
@@ -585,7 +614,7 @@ update_kernel(int kind, float *__restrict__ x, float *__restrict__ r, float *__r
       z[i] = zo;
     }
   }
-  reduce_and_decide(v, partials, st, L, decide, [&] { decide_update(st, kind); });
+  reduce_and_decide(v, partials, st, L, decide, [&] { decide_update(st, kind); }, 1);
 }
 
 // p_next = r + beta p (CG, double) or z + beta p (PCG, float), from p_cur
@@ -797,7 +826,8 @@ struct CgEngine {
   cudaGraphExec_t exec = nullptr;
   int batch = 4;
   bool pdl = false;          // programmatic dependent launch inside the iteration graph (MSX_CG_PDL=1)
-  int *status_host = nullptr;
+  int *status_host = nullptr;  // two slots (batches in flight)
+  cudaEvent_t batch_done[2] = {};
   // Chebyshev preconditioner: plan of M, its chunk carry, the three
   // semi-iteration buffers and the host-computed step coefficients
   BinnedPlan plan_m;
@@ -920,7 +950,15 @@ void engine_iteration(CgEngine *e, int par, cudaStream_t q) {
   float *pc = e->p[par], *pn = e->p[par ^ 1];
   engine_exchange_nccl(e, pc, q);
   // the short-row SpMV reads the halo words itself; other kernels get them unpacked
-  const bool words_in_spmv = p2p(e) && e->fused && short_rows_plan(e->plan);
+  // The halo words are unpacked into p's halo slots by a small kernel before
+  // the SpMV (default): reading them inside the SpMV (MSX_CG_HALO_IN_SPMV=1)
+  // slowed its gathers (2 GPUs, 8.4 M rows each: 149 us against 131 us plus
+  // a 2.4 us unpack).
+  static const int halo_in_spmv = [] {
+    const char *v = std::getenv("MSX_CG_HALO_IN_SPMV");
+    return v && *v ? std::atoi(v) : 0;
+  }();
+  const bool words_in_spmv = p2p(e) && e->fused && short_rows_plan(e->plan) && halo_in_spmv != 0;
   if (p2p(e) && !words_in_spmv) engine_unpack(e, pc, -1, q);
   if (e->fused) {
     dispatch_index(c.index_dtype, [&](auto ityp) {
@@ -1085,7 +1123,8 @@ CgEngine *cg_engine_create(const CgEngineConfig &cfg, cudaStream_t user_stream) 
   } else if (!cfg.preconditioned) {
     E->z = nullptr, E->inv = nullptr;
   }
-  MSX_CUDA(cudaMallocHost(&E->status_host, sizeof(int)));
+  MSX_CUDA(cudaMallocHost(&E->status_host, 2 * sizeof(int)));
+  for (auto &ev : E->batch_done) MSX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
   E->link.world = 1;
   E->link.rank = 0;
   E->link.cs = E->cs;
@@ -1117,6 +1156,8 @@ void cg_engine_destroy(CgEngine *e) {
   for (void *p : e->opened)
     if (p) cudaIpcCloseMemHandle(p);
   if (e->status_host) cudaFreeHost(e->status_host);
+  for (auto ev : e->batch_done)
+    if (ev) cudaEventDestroy(ev);
   if (e->pbuf) cudaFree(e->pbuf);
   if (e->halo_words) cudaFree(e->halo_words);
   if (e->mbox) cudaFree(e->mbox);
@@ -1205,6 +1246,12 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
   init.it = 1;
   init.maxiter = maxiter;
   init.round_base = e->round_base;
+  static const bool tracing = [] {
+    const char *v = std::getenv("MSX_CG_TRACE");
+    return v && *v == '1';
+  }();
+  init.tracing = tracing ? 1 : 0;
+  init.k_start[0] = init.k_start[1] = ~0ull;
   MSX_CUDA(cudaMemcpyAsync(e->st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
 
   // r0 = b - A x0 (x0 staged in p[0], whose halo the exchange fills); p[0]
@@ -1243,16 +1290,35 @@ CgResult cg_engine_solve(CgEngine *e, const float *b_in, const float *x0_in, con
       MSX_CUDA(cudaStreamEndCapture(s, &e->graph));
       MSX_CUDA(cudaGraphInstantiate(&e->exec, e->graph, 0));
     }
+    // Two batches in flight: while the host reads the status after batch k,
+    // batch k + 1 already runs, so the GPU never waits for the host. A batch
+    // launched after the solve stopped costs only its kernels' early exits
+    // (identically on every rank, whose statuses agree).
     int64_t launched = 0;
-    while (true) {
+    int slot = 0;
+    auto launch_batch = [&](int sl) {
       MSX_CUDA(cudaGraphLaunch(e->exec, s));
       launched += e->batch;
-      MSX_CUDA(cudaMemcpyAsync(e->status_host, &e->st->status, sizeof(int), cudaMemcpyDeviceToHost, s));
-      MSX_CUDA(cudaStreamSynchronize(s));
-      if (*e->status_host != kStatusRunning || launched >= maxiter) break;
+      MSX_CUDA(cudaMemcpyAsync(e->status_host + sl, &e->st->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+      MSX_CUDA(cudaEventRecord(e->batch_done[sl], s));
+    };
+    launch_batch(0);
+    while (true) {
+      const bool more = launched < maxiter;
+      if (more) launch_batch(slot ^ 1);
+      MSX_CUDA(cudaEventSynchronize(e->batch_done[slot]));
+      if (e->status_host[slot] != kStatusRunning || !more) break;
+      slot ^= 1;
     }
     MSX_CUDA(cudaMemcpyAsync(&host, e->st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
     MSX_CUDA(cudaStreamSynchronize(s));
+  }
+  if (host.tracing) {
+    auto avg = [&](int k) { return host.trace[k] / 1000.0 / std::max<unsigned long long>(host.trace[k % 3 == 2 ? k : k + (2 - k % 3)], 1); };
+    std::fprintf(stderr,
+                 "[msx cg trace] rank %d: spmv+dots start->last CTA %.1f us, all-reduce %.1f us; update start->last "
+                 "CTA %.1f us, all-reduce %.1f us (%llu iterations)\n",
+                 c.rank, avg(0), avg(1), avg(3), avg(4), host.trace[2]);
   }
   // rounds 0 .. completed + 1 were used; the next solve starts past them
   e->round_base += (unsigned)host.completed + 3u;

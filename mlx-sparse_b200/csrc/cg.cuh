@@ -29,6 +29,14 @@ struct CgState {
   int pad[2];
   double bb_init;     // Chebyshev PCG: b.b and the non-finite count of the
   double bad_init;    // initial residual, kept until r.z is known
+  // Timing trace (MSX_CG_TRACE=1, diagnostics only): per reduction kernel
+  // (0: SpMV + dots, 1: update) the earliest CTA start of the current
+  // launch, and summed over iterations {first CTA start -> last CTA ready,
+  // cross-rank all-reduce, count} in globaltimer nanoseconds.
+  unsigned long long k_start[2];
+  unsigned long long trace[6];
+  int tracing;
+  int pad2;
 };
 
 constexpr int kMaxRanks = 8;  // one node
