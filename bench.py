@@ -466,10 +466,10 @@ class PcgWorkload(Workload):
         self.units_per_step = float(self.iterations)
         self.local_bytes = self.bytes_per_iter * self.iterations / world
         # per iteration: SpMV(+dots), update, direction update; peer memory
-        # fuses the halo exchange and the scalar all-reduces into those three;
-        # NCCL adds the halo pack and two decision kernels (NCCL's own
-        # kernels are not counted)
-        per_it = 3 if world == 1 or self.mode == "p2p" else 6
+        # fuses the scalar all-reduces and the halo push into those and adds
+        # the halo unpack; NCCL adds the halo pack and two decision kernels
+        # (NCCL's own kernels are not counted)
+        per_it = 3 if world == 1 else (4 if self.mode == "p2p" else 6)
         self.launches_per_step = per_it * self.iterations + 6
 
     def step(self):
