@@ -49,7 +49,7 @@ constexpr int kWarpCap = 256;    // products per warp-level row
 constexpr int kBlockCap = 4096;  // products per CTA-level row
 constexpr int kBlockThreads = 256;
 constexpr int kDenseThreads = 512;
-constexpr int kBins = 7;  // smem warp, CTA, dense, register warp R = 1, 2, 4, 8
+constexpr int kBins = 8;  // smem warp, CTA, dense, register warp R = 1, 2, 4, 8, four rows per warp
 
 __device__ __forceinline__ uint32_t key_col(uint64_t k) { return (uint32_t)(k >> 32); }
 __device__ __forceinline__ uint32_t key_seq(uint64_t k) { return (uint32_t)(k & 0xffffffffu); }
@@ -95,7 +95,8 @@ __global__ void rhs_check_kernel(const RI *__restrict__ ri, const RI *__restrict
 // counter hit by every row serialises).
 template <typename LI>
 __global__ void bin_kernel(const int64_t *__restrict__ work, const LI *__restrict__ lp, int64_t m, bool reg_ok,
-                           int *__restrict__ lists, int *__restrict__ counts, int64_t *__restrict__ row_nnz) {
+                           bool quad_ok, int *__restrict__ lists, int *__restrict__ counts,
+                           int64_t *__restrict__ row_nnz) {
   const int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int lane = threadIdx.x & 31;
   int bin = -1;
@@ -104,9 +105,13 @@ __global__ void bin_kernel(const int64_t *__restrict__ work, const LI *__restric
     if (w == 0) {
       row_nnz[row] = 0;
     } else if (w <= kWarpCap) {
+      // bin 7: four rows per warp (<= 64 products, <= 8 lhs entries each);
       // bins 3..6: one warp with the keys in 1, 2, 4 or 8 registers per lane
       // (<= 32 lhs entries); else the shared-memory warp path
-      if (reg_ok && (int64_t)lp[row + 1] - (int64_t)lp[row] <= 32)
+      const int64_t nq = (int64_t)lp[row + 1] - (int64_t)lp[row];
+      if (quad_ok && w <= 64 && nq <= 8)
+        bin = 7;
+      else if (reg_ok && nq <= 32)
         bin = w <= 32 ? 3 : (w <= 64 ? 4 : (w <= 128 ? 5 : 6));
       else
         bin = 0;
@@ -454,6 +459,186 @@ spgemm_warp_reg_kernel(const int *__restrict__ list, const int *__restrict__ cou
   }
 }
 
+// Four rows per warp, each with <= 64 products and <= 8 lhs entries: row g
+// of the four owns lanes 8g..8g+7. Those lanes hold its lhs entries and rhs
+// row bounds (one round trip of index loads serves four rows), then its 64
+// key slots, 8 registers per lane, with the keys column << 8 | position
+// (padding all ones). Lane e of the group expands products e, e + 8, ...,
+// so a group's loads of one rhs row are consecutive. A bitonic sort whose
+// stages stop at 64 keys orders each group's segment on its own (21 stages,
+// 3 of them across lanes). Rows without repeated columns are compacted from
+// the registers through a shared-memory staging slot (so the stores of a row
+// are consecutive); if any row of the four repeats a column, the four rows
+// take the shared-memory run summation one after another.
+template <typename T, typename LI, typename RI>
+__global__ void __launch_bounds__(kBlockThreads)
+spgemm_quad_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
+                   const int64_t *__restrict__ work, const T *__restrict__ ld, const LI *__restrict__ li,
+                   const LI *__restrict__ lp, const T *__restrict__ rd, const RI *__restrict__ ri,
+                   const RI *__restrict__ rp, RowSink<T> sink, bool prune) {
+  __shared__ uint64_t keys[kBlockThreads / 32][64];
+  __shared__ float vals[kBlockThreads / 32][256];
+  __shared__ int cols[kBlockThreads / 32][256];
+  if (*flags & 3) return;
+  constexpr int R = 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g_mine = lane >> 3, e_mine = lane & 7, base = g_mine * 8;
+  const int count = *count_ptr;
+  const int n_quads = (count + 3) / 4;
+  float *val = vals[warp];
+  float *my_val = val + g_mine * 64;
+  for (int w = blockIdx.x * (kBlockThreads / 32) + warp; w < n_quads; w += gridDim.x * (kBlockThreads / 32)) {
+    const int li_idx = 4 * w + g_mine;  // slots past the list's end stay empty
+    const int64_t my_row = li_idx < count ? (int64_t)list[li_idx] : -1;
+    int rw = 0, nq = 0;
+    int64_t q0 = 0;
+    if (my_row >= 0) {
+      rw = (int)work[my_row];
+      q0 = (int64_t)lp[my_row];
+      nq = (int)((int64_t)lp[my_row + 1] - q0);
+    }
+    int64_t rb = 0;
+    int len = 0;
+    float lv = 0.f;
+    if (e_mine < nq) {
+      const int64_t k = (int64_t)li[q0 + e_mine];
+      lv = VT<T>::load(ld[q0 + e_mine]);
+      rb = (int64_t)rp[k];
+      len = (int)((int64_t)rp[k + 1] - rb);
+    }
+    int incl = len;  // inclusive prefix over the group's 8 lanes
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o, 8);
+      if (e_mine >= o) incl += v;
+    }
+    uint32_t key[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int t = r * 8 + e_mine;  // product position within the row
+      int e = 0;
+#pragma unroll
+      for (int b = 4; b > 0; b >>= 1) {
+        const int v = __shfl_sync(0xffffffffu, incl, base + ((e + b - 1) & 7));
+        if (e + b <= nq && v <= t) e += b;
+      }
+      const int src_lane = base + (e & 7);
+      const int excl = __shfl_sync(0xffffffffu, incl, src_lane) - __shfl_sync(0xffffffffu, len, src_lane);
+      const int64_t erb = __shfl_sync(0xffffffffu, rb, src_lane);
+      const float elv = __shfl_sync(0xffffffffu, lv, src_lane);
+      key[r] = 0xffffffffu;
+      if (t < rw) {
+        const int64_t src = erb + (t - excl);
+        key[r] = ((uint32_t)ri[src] << 8) | (uint32_t)t;
+        my_val[t] = __fmul_rn(elv, VT<T>::load(rd[src]));
+      }
+    }
+    __syncwarp();
+    // element i = lane * R + r; every stage sorts within aligned 64-key
+    // segments, all ascending
+#pragma unroll
+    for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        if (j >= R) {
+          const int lm = j / R;
+          const bool lower = (lane & lm) == 0;
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, key[r], lm);
+            const bool up = k == 64 || (((lane * R + r) & k) == 0);
+            key[r] = (lower == up) ? min(key[r], other) : max(key[r], other);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            if ((r & j) == 0) {
+              const bool up = k == 64 || (((lane * R + r) & k) == 0);
+              const uint32_t a = key[r], b = key[r | j];
+              if ((a > b) == up) {
+                key[r] = b;
+                key[r | j] = a;
+              }
+            }
+          }
+        }
+      }
+    }
+    // this lane holds positions e_mine * R .. e_mine * R + 7 of its row
+    const uint32_t next_first = __shfl_down_sync(0xffffffffu, key[0], 1);
+    bool dup = false;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = e_mine * R + r;
+      const uint32_t nk = r + 1 < R ? key[r + 1] : next_first;
+      if (i + 1 < rw && (key[r] >> 8) == (nk >> 8)) dup = true;
+    }
+    if (__any_sync(0xffffffffu, dup)) {
+      // every row of the quad through the shared-memory run summation
+      for (int g = 0; g < 4; ++g) {
+        const int64_t row = __shfl_sync(0xffffffffu, my_row, g * 8);
+        const int W = __shfl_sync(0xffffffffu, rw, g * 8);
+        if (row < 0) continue;
+        __syncwarp();  // the previous row's summation has finished reading keys
+        if (g_mine == g) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int i = e_mine * R + r;
+            if (i < W) keys[warp][i] = ((uint64_t)(key[r] >> 8) << 32) | (key[r] & 0xffu);
+          }
+        }
+        __syncwarp();
+        compact_sorted_row<T, true>(row, W, lane, 32, keys[warp], val + g * 64, nullptr, sink, prune);
+      }
+      __syncwarp();
+      continue;
+    }
+    bool keep[R];
+    T outv[R];
+    int mine = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = e_mine * R + r;
+      keep[r] = false;
+      if (i < rw) {
+        outv[r] = VT<T>::store(my_val[key[r] & 0xffu]);
+        keep[r] = !prune || VT<T>::load(outv[r]) != 0.0f;
+      }
+      mine += keep[r] ? 1 : 0;
+    }
+    int incl_k = mine;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl_k, o, 8);
+      if (e_mine >= o) incl_k += v;
+    }
+    // stage the compacted row in shared memory (the values were read into
+    // registers above), then the group's 8 lanes write it out consecutively
+    __syncwarp();
+    T *st_val = reinterpret_cast<T *>(my_val);
+    int *st_col = cols[warp] + g_mine * 64;
+    int pos = incl_k - mine;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (keep[r]) {
+        st_col[pos] = (int)(key[r] >> 8);
+        st_val[pos] = outv[r];
+        ++pos;
+      }
+    __syncwarp();
+    const int cnt = __shfl_sync(0xffffffffu, incl_k, base + 7);
+    if (my_row >= 0) {
+      const int64_t out0 = sink.off[my_row];
+      for (int j = e_mine; j < cnt; j += 8) {
+        sink.col[out0 + j] = st_col[j];
+        sink.val[out0 + j] = st_val[j];
+      }
+      if (e_mine == 7) sink.row_nnz[my_row] = cnt;
+    }
+    __syncwarp();
+  }
+}
+
 template <typename T, typename LI, typename RI>
 __global__ void __launch_bounds__(kBlockThreads)
 spgemm_block_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
@@ -567,9 +752,7 @@ spgemm_dense_kernel(const int *__restrict__ list, const int *__restrict__ count_
 }
 
 // Copies every finished row from its upper-bound slot to its final place.
-// A warp takes 32 consecutive rows: the lanes read the 32 rows' offsets and
-// counts with one load each, then the warp copies the rows one after another
-// with coalesced lanes, with no dependent global load between rows.
+// One warp per row; lanes copy consecutive entries.
 template <typename T, typename OutI>
 __global__ void copy_rows_kernel(const int64_t *__restrict__ off, const int64_t *__restrict__ row_nnz,
                                  const int *__restrict__ col, const T *__restrict__ val, int64_t m,
@@ -577,25 +760,12 @@ __global__ void copy_rows_kernel(const int64_t *__restrict__ off, const int64_t 
                                  T *__restrict__ out_data) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r0 = (blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; r0 < m;
-       r0 += warps * 32) {
-    const int64_t r = r0 + lane;
-    int64_t my_n = 0, my_src = 0, my_dst = 0;
-    if (r < m) {
-      my_n = row_nnz[r];
-      my_src = off[r];
-      my_dst = (int64_t)out_indptr[r];
-    }
-    const int rows = (int)min((int64_t)32, m - r0);
-#pragma unroll 4
-    for (int q = 0; q < rows; ++q) {
-      const int64_t n = __shfl_sync(0xffffffffu, my_n, q);
-      const int64_t src = __shfl_sync(0xffffffffu, my_src, q);
-      const int64_t dst = __shfl_sync(0xffffffffu, my_dst, q);
-      for (int64_t j = lane; j < n; j += 32) {
-        out_idx[dst + j] = (OutI)col[src + j];
-        out_data[dst + j] = val[src + j];
-      }
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < m; row += warps) {
+    const int64_t n = row_nnz[row];
+    const int64_t src = off[row], dst = (int64_t)out_indptr[row];
+    for (int64_t j = lane; j < n; j += 32) {
+      out_idx[dst + j] = (OutI)col[src + j];
+      out_data[dst + j] = val[src + j];
     }
   }
 }
@@ -682,7 +852,8 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
     rhs_check_kernel<RI><<<(unsigned)ceil_div(rhs_rows, t), t, 0, s>>>(ri, rp, rhs_rows, n_cols, flags);
   // column << 8 | position fits 32 bits below the all-ones padding key
   const bool reg_ok = n_cols < ((int64_t)1 << 24);
-  bin_kernel<LI><<<(unsigned)ceil_div(m, t), t, 0, s>>>(work, lp, m, reg_ok, lists, counts, row_nnz);
+  const bool quad_ok = reg_ok;
+  bin_kernel<LI><<<(unsigned)ceil_div(m, t), t, 0, s>>>(work, lp, m, reg_ok, quad_ok, lists, counts, row_nnz);
   MSX_CHECK_LAUNCH();
   scan_counts_to_indptr<int64_t>(work, m, row_off, sums, s);
   struct {
@@ -730,6 +901,13 @@ std::unique_ptr<Product> compute_product(std::unique_ptr<Product> P, const T *ld
                                                                          li, lp, rd, ri, rp, sink, prune);
     MSX_CHECK_LAUNCH();
   };
+  if (h.counts[7] > 0) {
+    const int wpb = kBlockThreads / 32;
+    const int grid = (int)std::min<int64_t>(ceil_div(ceil_div(h.counts[7], 4), wpb), (int64_t)sms * 8);
+    spgemm_quad_kernel<T, LI, RI><<<grid, kBlockThreads, 0, s>>>(lists + 7 * m, counts + 7, flags, work, ld, li, lp,
+                                                                  rd, ri, rp, sink, prune);
+    MSX_CHECK_LAUNCH();
+  }
   reg_rows(std::integral_constant<int, 1>{});
   reg_rows(std::integral_constant<int, 2>{});
   reg_rows(std::integral_constant<int, 4>{});
@@ -819,7 +997,7 @@ void spgemm_pass(bool write, const T *ld, const LI *li, const LI *lp, const T *r
     }
     return;
   }
-  const int grid = (int)std::min<int64_t>(ceil_div(m, 8 * 32), (int64_t)num_sms() * 16);
+  const int grid = (int)std::min<int64_t>(ceil_div(m, 8), (int64_t)num_sms() * 16);
   copy_rows_kernel<T, OutI><<<grid, 256, 0, s>>>(P->off, P->row_nnz, P->col, static_cast<const T *>(P->val), m,
                                                  out_indptr, out_idx, out_data);
   MSX_CHECK_LAUNCH();

@@ -141,3 +141,23 @@ def test_full_size_config(ms, orc):
     A = _csr(ms, ad, ai, ap, sa)
     C = A @ A
     _compare(C, orc.csr_matmat((ad, ai, ap), (ad, ai, ap), sa, sa))
+
+
+@pytest.mark.parametrize("n_cols", [40, 5000, 1 << 21])
+def test_four_rows_per_warp_bin(ms, orc, n_cols):
+    # rows of <= 8 lhs entries and <= 64 products, packed four to a warp:
+    # ragged lengths, empty lhs and rhs rows, a row count that is not a
+    # multiple of four, and few (n_cols 40: many repeated columns) to no
+    # repeats
+    rng = np.random.default_rng(n_cols)
+    m, k = 1001, 700
+    alen = rng.integers(0, 9, m)
+    blen = rng.integers(0, 9, k)
+    ap = np.concatenate([[0], np.cumsum(alen)]).astype(np.int32)
+    bp = np.concatenate([[0], np.cumsum(blen)]).astype(np.int32)
+    ai = np.concatenate([np.sort(rng.choice(k, n, replace=False)) for n in alen]).astype(np.int32)
+    bi = rng.integers(0, n_cols, bp[-1]).astype(np.int32)
+    ad = rng.standard_normal(ap[-1]).astype(np.float32)
+    bd = rng.standard_normal(bp[-1]).astype(np.float32)
+    C = _csr(ms, ad, ai, ap, (m, k)) @ _csr(ms, bd, bi, bp, (k, n_cols), canonical=False)
+    _compare(C, orc.csr_matmat((ad, ai, ap), (bd, bi, bp), (m, k), (k, n_cols)), exact_frac=1.0)
