@@ -160,12 +160,12 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <typename T, typename I, int V, int L, int kDepth>
-__global__ void __launch_bounds__(256)
-spmm_async_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
-                  const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+__device__ __forceinline__ void spmm_async_block(const T *__restrict__ data, const I *__restrict__ indices,
+                                                 const I *__restrict__ indptr, const T *__restrict__ rhs,
+                                                 T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols,
+                                                 int64_t block_x, int64_t slab_y, unsigned char *spmm_sm) {
   static_assert(V * sizeof(T) == 16, "16-byte vectors only");
   constexpr int kRows = 256 / L;
-  extern __shared__ __align__(16) unsigned char spmm_sm[];
   float4 *stage = reinterpret_cast<float4 *>(spmm_sm);  // [kDepth][256]
   I *col_s = reinterpret_cast<I *>(spmm_sm + (size_t)kDepth * 256 * 16);  // [kRows][kAsyncChunk]
   float *val_s = reinterpret_cast<float *>(col_s + kRows * kAsyncChunk);     // [kRows][kAsyncChunk]
@@ -174,9 +174,9 @@ spmm_async_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
   const int lane_in_row = tid % L;
   const int rloc = tid / L;
   const unsigned gmask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
-  const int64_t row = blockIdx.x * (int64_t)kRows + rloc;
+  const int64_t row = block_x * kRows + rloc;
   const bool row_ok = row < n_rows;
-  const int64_t slab0 = blockIdx.y * slab_cols;
+  const int64_t slab0 = slab_y * slab_cols;
   const int64_t slab1 = min(slab0 + slab_cols, k);
   const int64_t p0 = row_ok ? (int64_t)indptr[row] : 0;
   const int64_t p1 = row_ok ? (int64_t)indptr[row + 1] : 0;
@@ -225,6 +225,15 @@ spmm_async_kernel(const T *__restrict__ data, const I *__restrict__ indices, con
 }
 
 template <typename T, typename I, int V, int L, int kDepth>
+__global__ void __launch_bounds__(256)
+spmm_async_kernel(const T *__restrict__ data, const I *__restrict__ indices, const I *__restrict__ indptr,
+                  const T *__restrict__ rhs, T *__restrict__ out, int64_t n_rows, int64_t k, int64_t slab_cols) {
+  extern __shared__ __align__(16) unsigned char spmm_sm[];
+  spmm_async_block<T, I, V, L, kDepth>(data, indices, indptr, rhs, out, n_rows, k, slab_cols, blockIdx.x, blockIdx.y,
+                                       spmm_sm);
+}
+
+template <typename T, typename I, int V, int L, int kDepth>
 void launch_spmm_async(dim3 grid, cudaStream_t stream, const T *data, const I *indices, const I *indptr,
                        const T *rhs, T *out, int64_t n_rows, int64_t k, int64_t slab_cols) {
   constexpr size_t smem = spmm_async_smem<I, L, kDepth>();
@@ -260,15 +269,17 @@ void launch_spmm(const T *data, const I *indices, const I *indptr, const T *rhs,
   MSX_CHECK_LAUNCH();
 }
 
-// Bytes per RHS row of one column slab: one 128-byte line. Narrower slabs
-// (MSX_SPMM_SLAB_BYTES = 64 or 32) fit L2 better but measured slower on B200:
-// the kernel is bound by gather issue and latency, not by DRAM misses.
+// Bytes per RHS row of one column slab: 256 (two 128-byte lines). On the
+// 2^20 x 2^20, 16/row, k = 64 fp32 config a single 256-byte pass (matrix read
+// once) measured 0.541 ms against 0.553 for two 128-byte slabs, 0.79 for 64;
+// narrower slabs fit L2 better but the kernel is bound by gather issue
+// (L1/TEX), not by DRAM misses. MSX_SPMM_SLAB_BYTES = 32/64/128/256 overrides.
 int64_t spmm_slab_bytes(int64_t, int64_t) {
   if (const char *env = getenv("MSX_SPMM_SLAB_BYTES")) {
     const int64_t v = atoll(env);
-    if (v == 32 || v == 64 || v == 128) return v;
+    if (v == 32 || v == 64 || v == 128 || v == 256) return v;
   }
-  return 128;
+  return 256;
 }
 
 // Bytes of the RHS slab that should stay L2 resident while rows stream by.

@@ -240,7 +240,7 @@ def coo_matmat(a: COOArray, b: COOArray) -> COOArray:
 # ---------------------------------------------------------------------------
 # Host-resident operands streamed through the GPU
 # ---------------------------------------------------------------------------
-def csr_matmul_streamed(a: CSRArray, rhs, *, device=None, chunks: int = 8, out=None):
+def csr_matmul_streamed(a: CSRArray, rhs, *, device=None, chunks: int = 16, out=None):
     """``Y = A @ B`` for a CSR matrix and a dense ``B`` that live in host
     memory (pinned for full speed), computed on a GPU and returned in pinned
     host memory.
@@ -272,7 +272,7 @@ def csr_matmul_streamed(a: CSRArray, rhs, *, device=None, chunks: int = 8, out=N
     if n_rows == 0 or k == 0:
         return out
     indptr_h = a.indptr.contiguous()
-    ptr = indptr_h.to(torch.int64).numpy() if indptr_h.dtype != torch.int64 else indptr_h.numpy()
+    ptr = indptr_h.numpy()  # only the block boundaries are read on the host
     with torch.cuda.device(dev):
         up, comp, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         cur = torch.cuda.current_stream(dev)
