@@ -664,6 +664,25 @@ def _measure(wk, steps, warmup, device):
     return times
 
 
+class _CopyStep:
+    def __init__(self, nbytes, device):
+        import torch
+
+        half = max(16, nbytes // 2) // 16 * 16
+        self.src = torch.ones(half, dtype=torch.uint8, device=device)
+        self.dst = torch.empty_like(self.src)
+        self.nbytes = 2 * half
+
+    def step(self):
+        self.dst.copy_(self.src)
+
+
+def _copy_gbs(nbytes, steps, device):
+    cs = _CopyStep(nbytes, device)
+    t = _measure(cs, max(3, steps), 3, device)
+    return cs.nbytes / (sum(t) / len(t) * 1e-3) / 1e9
+
+
 def _measure_e2e(wk, steps, warmup, device):
     import torch
 
@@ -826,6 +845,14 @@ def _extra(name, args, device, peak, rank=0, world=1):
            "config": wk.config(), "dtype": wk.dtype}
     if isinstance(wk, PcgWorkload):
         out.update({"iterations": wk.iterations, "info": wk.info, "bytes_per_iteration": int(wk.bytes_per_iter)})
+    if world == 1 and b < (1 << 30) and not isinstance(wk, (PcgWorkload, SpgemmWorkload)):
+        # small problems are bound by launch and round-trip latency as much
+        # as by bandwidth: the same byte count as one device-to-device copy
+        # (half read, half written), timed the same way, is the reachable
+        # figure at this size
+        cg = _copy_gbs(int(b), steps, device)
+        out["copy_same_bytes"] = {"gbs": round(cg, 1), "frac_of_peak": round(cg / peak, 4),
+                                  "kernel_frac_of_copy": round(b / (ms_step * 1e-3) / 1e9 / cg, 4)}
     if isinstance(wk, SpgemmWorkload):
         out["products_per_s"] = round(wk.products / (ms_max * 1e-3), 1)
     if world > 1 and hasattr(wk, "parity"):
