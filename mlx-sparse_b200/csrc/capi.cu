@@ -42,14 +42,20 @@ struct msx_spmv_plan {
 };
 
 namespace {
-// Kernel used by planned products: row-length bins (default) or merge-path
-// tiles (MSX_SPMV_KERNEL=tiles).
-bool planned_use_tiles() {
-  static const bool tiles = [] {
+// Kernel used by planned products: row-length bins when every row falls in
+// one bin (stencils: the short-row kernels stage each block's contiguous
+// nonzeros), else merge-path tiles, which read the matrix in row order (on a
+// 2^22-row power-law matrix 0.551 ms against 0.588 for the bins, whose
+// permuted rows re-fetch shared sectors). MSX_SPMV_KERNEL=tiles / bins forces
+// either.
+int planned_kernel_override() {
+  static const int v = [] {
     const char *e = getenv("MSX_SPMV_KERNEL");
-    return e && std::string(e) == "tiles";
+    if (e && std::string(e) == "tiles") return 1;
+    if (e && std::string(e) == "bins") return 2;
+    return 0;
   }();
-  return tiles;
+  return v;
 }
 }  // namespace
 
@@ -110,7 +116,8 @@ int msx_spmv_plan_create(int index_dtype, const void *indptr, int64_t n_rows, in
         return plan->dev;
       };
       build_binned_plan(index_dtype, indptr, n_rows, nnz, as_stream(stream), alloc, plan->bins);
-      plan->use_tiles = planned_use_tiles();
+      const int force = planned_kernel_override();
+      plan->use_tiles = force == 1 || (force == 0 && !plan->bins.info.identity);
       plan->n_tiles = spmv_num_tiles(n_rows, nnz);
       cudaError_t e = cudaMalloc(&plan->tiles, spmv_plan_device_bytes(plan->n_tiles));
       if (e != cudaSuccess)

@@ -5,6 +5,8 @@ the north-star's 1e-5 relative per-row bound made safe for rows that cancel;
 fp16/bf16 (fp32 accumulation): 1e-2 of the same scale.
 """
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -169,7 +171,39 @@ def test_full_size_power_law_int64(ms, orc):
     _check(y2, y_ref, scale, 1e-5)
 
 
-def test_bulk_copy_wait_timeout_is_reported(ms):
+@pytest.fixture
+def tma_pipeline():
+    """Selects the opt-in TMA bulk-copy pipeline of the stateless tile SpMV
+    (read at every call) for one test."""
+    old = os.environ.get("MSX_SPMV_TMA")
+    os.environ["MSX_SPMV_TMA"] = "1"
+    yield
+    if old is None:
+        del os.environ["MSX_SPMV_TMA"]
+    else:
+        os.environ["MSX_SPMV_TMA"] = old
+
+
+def test_tma_pipeline_matches_plain_loads(ms, orc):
+    from mlx_sparse import _native
+
+    (d, i, p), shape = wl.ragged_csr(30000, 20000, 9, 300)
+    A = _csr(ms, d, i, p, shape)
+    x = _dev(wl.uniform_vector(shape[1], 3))
+    y_plain = _native.csr_matvec(A.data, A.indices, A.indptr, x, A.shape)
+    os.environ["MSX_SPMV_TMA"] = "1"
+    try:
+        y_tma = _native.csr_matvec(A.data, A.indices, A.indptr, x, A.shape)
+        _native.check_device_errors()
+    finally:
+        del os.environ["MSX_SPMV_TMA"]
+    assert torch.equal(y_plain, y_tma)
+    xh = wl.uniform_vector(shape[1], 3)
+    y_ref = orc.csr_matvec(d, i, p, xh, shape[0])
+    _check(y_plain.cpu().numpy(), y_ref, _row_scale(orc, d, i, p, xh, shape[0]), 1e-5)
+
+
+def test_bulk_copy_wait_timeout_is_reported(ms, tma_pipeline):
     """A bulk-copy wait that gives up is reported by msx_check_device_errors
     (the poll limit is set to 0 so every wait gives up at once; the copies
     still land and are waited for before the kernel exits)."""
