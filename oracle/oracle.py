@@ -31,10 +31,17 @@ BF16 = "bf16"
 
 
 def build() -> str:
-    """Compiles liboracle.so if it is missing or older than oracle.cpp."""
+    """Compiles liboracle.so if it is missing or older than oracle.cpp. Holds a
+    file lock while it checks and builds, so processes that start together
+    (multi-rank tests) build it once; the library is written under a
+    temporary name and renamed into place."""
+    import fcntl
+
     src = os.path.join(HERE, "oracle.cpp")
-    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
-        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    with open(os.path.join(HERE, ".build.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+            subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
 
 
@@ -44,8 +51,7 @@ _lib = None
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            build()
+        build()
         L = ctypes.CDLL(LIB_PATH)
         c_i64, c_int, c_float, p = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
         L.orc_last_error.restype = ctypes.c_char_p
