@@ -85,7 +85,9 @@ MSX_API int msx_version(void);
 MSX_API int msx_compiled_sm(void);
 
 /* Device-side error check. The SpMV kernels that stage tiles with bulk copies
- * wait on shared-memory barriers with a bounded number of polls; if a wait
+ * (the tile SpMV when the environment sets MSX_SPMV_TMA=1, read at every
+ * call; off by default, plain loads measured faster on B200) wait on
+ * shared-memory barriers with a bounded number of polls; if a wait
  * gives up, the kernel stops, records the event in a per-device flag and the
  * rows it had not reached stay unwritten. The flag is sticky: this call
  * synchronises `stream`, reads and clears the flag of the current device and
