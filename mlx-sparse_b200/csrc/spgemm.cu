@@ -471,7 +471,7 @@ spgemm_warp_reg_kernel(const int *__restrict__ list, const int *__restrict__ cou
 // are consecutive); if any row of the four repeats a column, the four rows
 // take the shared-memory run summation one after another.
 template <typename T, typename LI, typename RI>
-__global__ void __launch_bounds__(kBlockThreads)
+__global__ void __launch_bounds__(kBlockThreads, 4)  // 64 registers: 4 CTAs/SM (80 unbounded: 3; 161 -> 145 us)
 spgemm_quad_kernel(const int *__restrict__ list, const int *__restrict__ count_ptr, const int *__restrict__ flags,
                    const int64_t *__restrict__ work, const T *__restrict__ ld, const LI *__restrict__ li,
                    const LI *__restrict__ lp, const T *__restrict__ rd, const RI *__restrict__ ri,
