@@ -159,6 +159,21 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// acc0 += s * b0 and acc1 += s * b1, each as a round-to-nearest multiply
+// followed by a round-to-nearest add (the reference's `acc += a * b` without
+// contraction): both products with one packed f32x2 multiply (sm_100), the
+// adds as scalar round-to-nearest adds.
+__device__ __forceinline__ void mul_add_rn_x2(float &acc0, float &acc1, float s, float b0, float b1) {
+  unsigned long long bb, ss, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(ss), "l"(bb));
+  float p0, p1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(p0), "=f"(p1) : "l"(p));
+  acc0 = __fadd_rn(acc0, p0);
+  acc1 = __fadd_rn(acc1, p1);
+}
+
 template <typename T, typename I, int V, int L, int kDepth>
 __device__ __forceinline__ void spmm_async_block(const T *__restrict__ data, const I *__restrict__ indices,
                                                  const I *__restrict__ indptr, const T *__restrict__ rhs,
@@ -212,7 +227,7 @@ __device__ __forceinline__ void spmm_async_block(const T *__restrict__ data, con
           for (int i = 0; i < V; ++i) b[i] = VT<T>::load(e[i]);
           const float a = my_vals[q];
 #pragma unroll
-          for (int i = 0; i < V; ++i) acc[i] = add_rn(acc[i], mul_rn(a, b[i]));
+          for (int i = 0; i < V; i += 2) mul_add_rn_x2(acc[i], acc[i + 1], a, b[i], b[i + 1]);
         }
         if (q + kDepth < cnt && col_ok)
           cp_async16_hint(&stage[slot], rhs + (int64_t)my_cols[q + kDepth] * k + c, pol_rhs);
